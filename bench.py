@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""Benchmark of the multi-parameter DBSCAN grid fit (fit_multi) on B200.
+
+A "step" is one k x l grid fit over the workload's points: neighbourhood pass, degrees,
+core masks, CSR, batched connected components and relabel, labels left on the device.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4] [--impl reference]
+
+Default workload (c4): N=1,000,000, D=33 (32 informative + 1 zero column), 100 Gaussian
+blobs (centres U[-20,20]^32, std U[0.8,1.5]) + 5% uniform noise, 4 x 4 grid
+eps {3.0,3.5,4.0,4.5} x minPts {5,10,20,40}, a 128 GB budget with neigh_per_row=64
+(8 batches of 127,8xx rows).  Seeded synthetic data with the shapes of the published
+configuration.
+
+Metric: pair-distances per second = N^2 ordered pairs per grid / grid wall time (the
+reference's unit; each distance evaluated here covers two ordered pairs).  `value` times
+device-resident input with CUDA events; `e2e` times the host-buffer C-ABI entry point with
+the point copy in and the label copy out inside the timed region.
+
+Multi-GPU (torchrun, one process per GPU): each rank runs its own full replica of the
+workload ("replicas only" until the sharded path lands); value = all ranks' pairs / max time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "cuml-dbscanmulti_b200", ROOT / "oracle"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+CONFIGS = {
+    "c1": dict(n=10_000, d=2, centers=8, box=10.0, std=(0.5, 0.5), noise=0.05, zero_cols=0,
+               eps=[0.2, 0.3, 0.5], min_samples=[5, 10, 20], budget=None, npr=0,
+               desc="Gaussian blobs N=10,000 D=2, 8 centres U[-10,10]^2, std 0.5, 5% noise; 3x3 grid"),
+    "c2": dict(n=100_000, d=8, centers=20, box=10.0, std=(0.5, 1.0), noise=0.05, zero_cols=0,
+               eps=[0.4, 0.6, 0.8, 1.0, 1.2], min_samples=[10], budget=None, npr=0,
+               desc="Multi-EPS N=100,000 D=8, 20 centres U[-10,10]^8, std U[0.5,1.0], 5% noise; k=5, l=1"),
+    "c3": dict(n=500_000, d=32, centers=50, box=20.0, std=(1.0, 1.0), noise=0.10, zero_cols=0,
+               eps=[4.0], min_samples=[5, 10, 20, 40, 80], budget=None, npr=0,
+               desc="Multi-minPts N=500,000 D=32, 50 centres U[-20,20]^32, std 1.0, 10% noise; k=1, l=5"),
+    "c4": dict(n=1_000_000, d=33, centers=100, box=20.0, std=(0.8, 1.5), noise=0.05, zero_cols=1,
+               eps=[3.0, 3.5, 4.0, 4.5], min_samples=[5, 10, 20, 40], budget=128 * 10**9, npr=64,
+               desc="Multi-Both N=1,000,000 D=33 (32 informative + 1 zero column), 100 centres "
+                    "U[-20,20]^32, std U[0.8,1.5], 5% noise; 4x4 grid; 128 GB budget, "
+                    "neigh_per_row 64 -> 8 batches"),
+    "c5": dict(n=200_000, d=64, centers=10, box=5.0, std=(2.0, 2.0), noise=0.0, zero_cols=0,
+               eps=[6.0, 9.0, 12.0], min_samples=[10, 50, 200], budget=None, npr=0,
+               desc="Dense-route stress as written: N=200,000 D=64, 10 centres U[-5,5]^64, std 2.0, "
+                    "no noise; 3x3 grid"),
+}
+
+
+def make_points(cfg: dict, seed: int = 0) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    n, d, zc = cfg["n"], cfg["d"], cfg["zero_cols"]
+    di = d - zc
+    centres = rng.uniform(-cfg["box"], cfg["box"], size=(cfg["centers"], di))
+    lo, hi = cfg["std"]
+    std = rng.uniform(lo, hi, size=cfg["centers"]) if hi > lo else np.full(cfg["centers"], lo)
+    m = n - int(round(cfg["noise"] * n))
+    assign = rng.integers(0, cfg["centers"], size=m)
+    pts = np.zeros((n, d), dtype=np.float32)
+    pts[:m, :di] = (centres[assign] + rng.standard_normal((m, di)) * std[assign, None]).astype(np.float32)
+    pts[m:, :di] = rng.uniform(-cfg["box"], cfg["box"], size=(n - m, di)).astype(np.float32)
+    return pts
+
+
+# ---- clocks during the timed region (NVML reads only) -------------------------------------------
+class ClockSampler:
+    def __init__(self, device: int):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.hdl = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.hdl, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        nv = self.nv
+        names = {
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.hdl, nv.NVML_CLOCK_SM)
+                util = nv.nvmlDeviceGetUtilizationRates(self.hdl).gpu
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.hdl)
+                if util > 50:
+                    self.samples.append(mhz)
+                    for k, bit in names.items():
+                        if mask & bit:
+                            self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(0.1)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self) -> dict:
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml-unavailable"]}
+        self._stop.set()
+        if self._t:
+            self._t.join()
+        med = float(np.median(self.samples)) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples_under_load": len(self.samples)}
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {}
+
+
+def sgemm_fp32_peak(torch, dev) -> float:
+    """Measured CUDA-core FP32 throughput: cuBLAS SGEMM 8192^3 with TF32 off, best of 5
+    (TFLOP/s, FMA = 2 flops).  The distance kernel is bound by the same FP32 pipes."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        a = torch.randn(8192, 8192, device=dev)
+        b = torch.randn(8192, 8192, device=dev)
+        torch.matmul(a, b)
+        torch.cuda.synchronize()
+        best = 0.0
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b)
+            e1.record()
+            e1.synchronize()
+            best = max(best, 2 * 8192**3 / (e0.elapsed_time(e1) * 1e-3) / 1e12)
+        del a, b
+        return best
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def cpu_baseline(pts: np.ndarray, eps, target_s: float = 12.0) -> dict:
+    """The oracle's fp32 distance/degree loop (the CPU restatement of the path) on a bounded
+    sample of query rows against all N points, every host core."""
+    import oracle
+
+    threads = oracle.default_threads()
+    n = len(pts)
+    rows = 32
+    t0 = time.perf_counter()
+    oracle.codes_degrees(pts, eps, row0=0, rows=rows, want_codes=False, threads=threads)
+    dt = time.perf_counter() - t0
+    rows2 = int(min(n, max(rows, rows * target_s / max(dt, 1e-6))))
+    t0 = time.perf_counter()
+    oracle.codes_degrees(pts, eps, row0=0, rows=rows2, want_codes=False, threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": rows2 * n / dt, "unit": "pair-distances/s", "cores": threads, "kind": "port",
+            "sample": f"{rows2} query rows x all {n} points (codes + per-eps degrees), "
+                      f"{dt:.1f} s; grid wall time extrapolates as N^2 / value",
+            "seconds": dt}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def e2e_leg(h, pts, eps, ms, kw, labels, flush, steps, ws, dev, torch, dist, pairs):
+    """Host buffers through dbm_fit_multi_host: pinned points copied in and labels copied out
+    inside every timed step (wall clock around the call)."""
+    k, l, n = len(eps), len(ms), len(pts)
+    xp = torch.from_numpy(pts).pin_memory()
+    lab_host = torch.empty((k * l, n), dtype=torch.int32).pin_memory()
+    h.fit_multi(xp.numpy(), eps, ms, labels_out=lab_host.numpy(), **kw)
+    e2e_t = []
+    for _ in range(steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        h.fit_multi(xp.numpy(), eps, ms, labels_out=lab_host.numpy(), **kw)
+        e2e_t.append(time.perf_counter() - t0)
+    assert np.array_equal(lab_host.numpy(), labels.cpu().numpy()), "host and device paths disagree"
+    e2e_s = float(np.sum(e2e_t))
+    if ws > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    return pairs * ws * steps / e2e_s, e2e_s
+
+
+def run_reference(args, cfg) -> None:
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    pts = make_points(cfg)
+    cb = None
+    values = []
+    for _ in range(args.warmup):
+        cpu_baseline(pts, cfg["eps"], target_s=2.0)
+    for _ in range(args.steps):
+        cb = cpu_baseline(pts, cfg["eps"], target_s=args.cpu_seconds / max(1, args.steps))
+        values.append(cb["value"])
+    value = float(np.median(values))
+    n = cfg["n"]
+    out = {
+        "impl": "reference", "metric": "pair_distances_per_s", "value": value, "unit": "pairs/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": n * n / value * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config, "desc": cfg["desc"], "n": n, "d": cfg["d"],
+                   "eps": cfg["eps"], "min_samples": cfg["min_samples"]},
+        "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": cb["cores"], "kind": "port",
+                         "sample": cb["sample"]},
+        "e2e": {"value": value, "unit": "pairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's own path needs RAFT/cuVS/RMM and cannot be built offline; its CPU "
+                "restatement (oracle/dbm_oracle.c, pthreads, sequential fp32 FMA) is timed instead",
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
+    ap.add_argument("--n", type=int, default=0, help="override N (small cases for ncu captures)")
+    args = ap.parse_args()
+    cfg = dict(CONFIGS[args.config])
+    if args.n:
+        cfg["n"] = args.n
+        cfg["desc"] += f" [N overridden to {args.n}]"
+
+    if args.impl == "reference":
+        run_reference(args, cfg)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import dbscan_multi as dm
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=__import__("datetime").timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+
+    n, d = cfg["n"], cfg["d"]
+    eps, ms = cfg["eps"], cfg["min_samples"]
+    k, l = len(eps), len(ms)
+    pts = make_points(cfg)
+    x = torch.from_numpy(pts).to(dev)
+    h = dm.DbscanMulti(local)
+    kw = dict(neigh_per_row=cfg["npr"])
+    if cfg["budget"]:
+        kw["max_bytes_per_batch"] = cfg["budget"]
+    labels = torch.empty((k * l, n), dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
+
+    h.set_phase_timing(True)
+    for _ in range(args.warmup):
+        h.fit_multi(x, eps, ms, labels_out=labels, **kw)
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    times, dist_ms, stats = [], [], None
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    for _ in range(args.steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        r = h.fit_multi(x, eps, ms, labels_out=labels, **kw)
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+        dist_ms.append(r.stats["ms_distance"])
+        stats = r.stats
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    total_ms = float(np.sum(times))
+    if ws > 1:
+        t = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    pairs = float(n) * float(n)
+    value = pairs * ws * args.steps / (total_ms * 1e-3)
+
+    # e2e through the host-buffer entry point: pinned points in, labels out, every step
+    h.set_phase_timing(False)
+    if args.no_e2e:
+        e2e_value, e2e_s = None, None
+    else:
+        e2e_value, e2e_s = e2e_leg(h, pts, eps, ms, kw, labels, flush, args.steps, ws, dev, torch, dist,
+                                   pairs)
+    # roofline of the dominant kernel (the distance pass): FP32 pipes
+    unique_pairs = n * (n - 1) / 2
+    flops = unique_pairs * 3.0 * d  # D FSUB + D FFMA (FMA = 2 flops)
+    dms = float(np.mean(dist_ms)) if dist_ms else float("nan")
+    achieved = flops / (dms * 1e-3) / 1e12
+    peak = sgemm_fp32_peak(torch, dev)
+    sm_mhz = clk.get("sm_mhz") or 1965.0
+    nominal = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+    lane_frac = (unique_pairs * 2.0 * d) / (dms * 1e-3) / (148 * 128 * sm_mhz * 1e6)
+    traffic_path = ROOT / "profiles" / "dist_tri_kernel_traffic.json"
+    traffic = None
+    if traffic_path.exists():
+        try:
+            traffic = json.loads(traffic_path.read_text()).get(args.config)
+        except Exception:
+            traffic = None
+
+    if rank == 0:
+        cb = None
+        if not args.no_cpu_baseline and ws == 1:
+            cb = cpu_baseline(pts, eps, target_s=args.cpu_seconds)
+            cb.pop("seconds", None)
+        out = {
+            "metric": "pair_distances_per_s",
+            "value": value,
+            "unit": "pairs/s",
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "grid_wall_s": ms_per_step / 1e3,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded numpy generator with the published configuration's shapes)",
+            "config": {"workload": args.config, "desc": cfg["desc"], "n": n, "d": d, "eps": eps,
+                       "min_samples": ms, "max_bytes_per_batch": cfg["budget"] or 0,
+                       "neigh_per_row": cfg["npr"], "batches": stats["batches"],
+                       "batch_size": stats["batch_size"], "parallelism": f"replicas{ws}" if ws > 1 else "1gpu",
+                       "l2": "flushed (256 MB write) between timed steps"},
+            "gpu_launches": int(stats["launches"]) * args.steps,
+            "clocks": clk,
+            "roofline": {"bound": "fp32", "kernel": "dist_tri_kernel", "achieved": achieved,
+                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
+                         "peak_source": "measured here: cuBLAS SGEMM 8192^3, TF32 off (no FP32 figure "
+                                        "in MEASURED_PEAKS.json)",
+                         "peak_nominal": nominal, "fp32_lane_utilisation": lane_frac,
+                         "flops_per_launch": flops, "ms_per_launch": dms,
+                         "traffic": traffic,
+                         "accounting": "unique pairs N(N-1)/2 x 3D flops (D FSUB + D FFMA)"},
+            "e2e": None if e2e_value is None else {
+                "value": e2e_value, "unit": "pairs/s",
+                "h2d_bytes_per_step": int(n * d * 4), "d2h_bytes_per_step": int(k * l * n * 4),
+                "ms_per_step": e2e_s / args.steps * 1e3},
+            "graph": {"edges": stats["edges"], "total_nnz_max_eps": stats["total_nnz_max_eps"],
+                      "distance_passes": stats["distance_passes"]},
+            "phase_ms": {"distance": dms},
+            "cpu_baseline": cb,
+            "hbm_peak_gbs": measured_peaks().get("hbm_gbs"),
+        }
+        print(json.dumps(out), flush=True)
+    h.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

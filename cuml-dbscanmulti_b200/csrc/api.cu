@@ -1,0 +1,788 @@
+// api.cu -- fit_multi orchestrator and the C ABI of libdbm.so.
+//
+// Pass structure (B200 design; the reference's is runner_multi.cuh:549-749 / 771-1251):
+//   1. X -> XT (dim-major, padded) for TMA.
+//   2. One distance pass over the upper triangle of tile pairs: exact per-eps degree
+//      histograms for every row and the list of neighbour pairs (i < j) within the largest
+//      eps, each with its smallest-eps code.  If the pair buffer was too small the pass is
+//      repeated once with the exact size (the counts are always complete).
+//   3. Degrees, core counts (and the optional byte core masks), scan, symmetric max-eps CSR
+//      with codes.
+//   4. Batch plan: the reference's batch size for the budget, then its batch-correction
+//      rule replayed on the measured per-batch nnz (runner_multi.cuh:1340-1456), and the
+//      per-batch route (anotar_compensa or forced).
+//   5. Labelling, batches ascending: per eps a CSR slab for the batch rows (the max-eps rows
+//      as they are; smaller eps by order-preserving compaction), then the batched CC kernels
+//      for the l minPts configs of that eps.
+//   6. Roots -> ranks -> labels for all k*l configs at once.
+#include "dbm_internal.cuh"
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <vector>
+
+#ifndef DBM_GIT_SHA
+#define DBM_GIT_SHA "unknown"
+#endif
+#ifndef DBM_BUILD_ID
+#define DBM_BUILD_ID "unknown"
+#endif
+
+namespace dbm {
+
+static std::atomic<int64_t> g_launches{0};
+int64_t count_launch(int64_t n) { return g_launches.fetch_add(n) + n; }
+int64_t launches_so_far() { return g_launches.load(); }
+
+// launchers defined in dist.cu / graph.cu / cc.cu
+Status launch_distance(const DistLaunch& a, cudaStream_t s);
+Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s);
+int32_t padded_dims(int32_t d);
+int64_t padded_points(int64_t n);
+Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
+                      int32_t* deg, int32_t* corecnt, int32_t* rowcnt, uint8_t* core_out,
+                      cudaStream_t s);
+Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, int32_t* fill,
+                          uint32_t* col, cudaStream_t s);
+Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, int64_t* out,
+                        cudaStream_t s);
+Status launch_slab_counts(const int32_t* deg_e, int64_t s0, int64_t rows, int32_t* counts,
+                          cudaStream_t s);
+Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int e,
+                     const int64_t* off_e, int32_t* col_e, cudaStream_t s);
+Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigned long long* best,
+                      cudaStream_t s);
+Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, const int32_t* cc_e, bool single_batch,
+                       int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur, uint32_t tag,
+                       int32_t* err, cudaStream_t s);
+Status launch_cc_roots(int64_t n, int k, int l, const int32_t* cc, int32_t* G, int32_t* flags,
+                       cudaStream_t s);
+Status launch_cc_labels(int64_t n, int k, int l, const int32_t* cc, int32_t* G, const int32_t* cur,
+                        const int64_t* rank, int32_t* labels, cudaStream_t s);
+
+// ---- batch-size rules (runner_multi.cuh:79-119, 214-268, 437-499) --------------------------
+struct Plan {
+  uint64_t budget = 0;
+  uint64_t batch_size = 0;
+  int index_bits = 32;
+  bool use_cuvs = true;
+};
+
+static uint64_t isz_of(int bits) { return bits == 64 ? 8 : 4; }
+
+static uint64_t mem_per_row(int64_t n, int k, bool use_cuvs, int64_t hint, uint64_t isz)
+{
+  const uint64_t npr = hint > 0 ? static_cast<uint64_t>(hint) : static_cast<uint64_t>(n);
+  if (use_cuvs) {
+    const uint64_t per_entry = (k > 1 ? 2 : 1) * isz + (k > 1 ? 1 : 0);
+    return static_cast<uint64_t>(n) + npr * per_entry + 2 * isz + static_cast<uint64_t>(k) * isz;
+  }
+  return 2ull * static_cast<uint64_t>(n) + (npr + 2) * isz + static_cast<uint64_t>(k) * isz;
+}
+
+static uint64_t mem_fixed(int64_t n, int k, int l, uint64_t isz)
+{
+  return static_cast<uint64_t>(n) * static_cast<uint64_t>(k) * static_cast<uint64_t>(l) +
+         static_cast<uint64_t>(n) * isz * 2;
+}
+
+static Status batch_size_rule(int64_t n, int k, int l, uint64_t max_bytes, bool use_cuvs, int64_t hint,
+                              int index_bits, uint64_t* out)
+{
+  const uint64_t isz = isz_of(index_bits);
+  const uint64_t per_row = mem_per_row(n, k, use_cuvs, hint, isz);
+  const uint64_t fixed = mem_fixed(n, k, l, isz);
+  if (!(max_bytes > fixed))
+    return Status::Err(DBM_ERR_FIXED_BUFFERS,
+                       "insufficient memory for the fixed buffers: more than " +
+                         std::to_string(fixed) + " bytes are needed for N=" + std::to_string(n) +
+                         " and " + std::to_string(static_cast<long long>(k) * l) + " configurations");
+  uint64_t bs = (max_bytes - fixed) / per_row;
+  bs = std::min<uint64_t>(static_cast<uint64_t>(n), bs);
+  if (bs < 1) bs = 1;
+  const uint64_t imax = index_bits == 64 ? static_cast<uint64_t>(INT64_MAX)
+                                         : static_cast<uint64_t>(INT32_MAX);
+  const uint64_t cap = (imax - 1) / static_cast<uint64_t>(n);
+  if (cap < 1)
+    return Status::Err(DBM_ERR_INDEX_OVERFLOW,
+                       "N=" + std::to_string(n) + " does not allow a single-row batch with the chosen index type");
+  *out = std::min(bs, cap);
+  return Status::Ok();
+}
+
+static uint64_t csr_bytes_per_entry(int k, bool use_cuvs, uint64_t isz)
+{
+  return (use_cuvs && k > 1) ? 2 * isz + 1 : isz;
+}
+
+static bool csr_fits(int64_t nnz, uint64_t per_entry, uint64_t available)
+{
+  return 1.1 * static_cast<double>(nnz) * static_cast<double>(per_entry) <= static_cast<double>(available);
+}
+
+static int64_t measured_degree(int64_t nnz, int64_t rows)
+{
+  const int64_t g = (nnz + rows - 1) / rows;
+  return g > 1 ? g : 1;
+}
+
+static uint64_t csr_rows_that_fit(int64_t degree, uint64_t per_entry, uint64_t available)
+{
+  const uint64_t per_row = static_cast<uint64_t>(degree) * per_entry;
+  const uint64_t fit = static_cast<uint64_t>(0.8 * static_cast<double>(available)) /
+                       std::max<uint64_t>(1, per_row);
+  return std::max<uint64_t>(1, fit);
+}
+
+static int annotate_pays(int64_t nnz, int64_t pairs, int k, int64_t d)
+{
+  const long double a = static_cast<long double>(nnz) * static_cast<long double>(d) * 40.0L;
+  const long double b = static_cast<long double>(k - 1) *
+                        (static_cast<long double>(pairs) * static_cast<long double>(d) + 60000000000.0L);
+  return a < b;
+}
+
+// ---- workspace --------------------------------------------------------------------------------
+struct Buffer {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+static Status ensure(Buffer& b, size_t bytes)
+{
+  if (bytes == 0) bytes = 256;
+  if (b.bytes >= bytes) return Status::Ok();
+  if (b.p) cudaFree(b.p);
+  b.p = nullptr;
+  b.bytes = 0;
+  bytes = align_up(bytes, 256);
+  cudaError_t e = cudaMalloc(&b.p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    b.p = nullptr;
+    return Status::Err(DBM_ERR_OOM, "device allocation of " + std::to_string(bytes) +
+                                      " bytes failed: " + cudaGetErrorString(e));
+  }
+  b.bytes = bytes;
+  return Status::Ok();
+}
+
+template <typename T>
+static T* as(Buffer& b) { return static_cast<T*>(b.p); }
+
+}  // namespace dbm
+
+struct dbm_handle {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int sm_count = 148;
+  bool timing = false;
+  uint64_t edge_cap_hint = 0;
+  dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, minpts, counters, err;
+  dbm::Buffer slab_counts, slab_off, slab_col, G, L, best, cur, flags, rank, scan_scratch, bnnz;
+  dbm::Buffer xdev, labels_dev, core_dev;  // host-buffer entry point only
+  int64_t* pinned = nullptr;               // small D2H staging
+  size_t pinned_count = 0;
+
+  uint64_t workspace_bytes() const
+  {
+    const dbm::Buffer* all[] = {&xt, &hist, &deg, &cc, &rowcnt, &off, &fill, &edges, &col,
+                                &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
+                                &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz};
+    uint64_t s = 0;
+    for (auto* b : all) s += b->bytes;
+    return s;
+  }
+};
+
+namespace dbm {
+
+static void set_err(char* err, size_t len, const std::string& msg)
+{
+  if (!err || len == 0) return;
+  const size_t c = std::min(len - 1, msg.size());
+  std::memcpy(err, msg.data(), c);
+  err[c] = '\0';
+}
+
+static Status ensure_pinned(dbm_handle* h, size_t count)
+{
+  if (h->pinned_count >= count) return Status::Ok();
+  if (h->pinned) cudaFreeHost(h->pinned);
+  h->pinned = nullptr;
+  h->pinned_count = 0;
+  count = std::max<size_t>(count, 64);
+  DBM_CUDA(cudaMallocHost(reinterpret_cast<void**>(&h->pinned), count * sizeof(int64_t)));
+  h->pinned_count = count;
+  return Status::Ok();
+}
+
+struct PhaseTimer {
+  dbm_handle* h;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr, b = nullptr;
+  double* out;
+  PhaseTimer(dbm_handle* h_, cudaStream_t s_, double* out_) : h(h_), s(s_), out(out_)
+  {
+    if (!h->timing || !out) return;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, s);
+  }
+  ~PhaseTimer()
+  {
+    if (!a) return;
+    cudaEventRecord(b, s);
+    cudaEventSynchronize(b);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    *out += ms;
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+  }
+};
+
+static Status validate(int64_t n, int64_t d, const float* eps, int k, const int32_t* minpts, int l)
+{
+  if (n < 1) return Status::Err(DBM_ERR_INVALID, "No rows in the input array. DBSCAN cannot be fitted!");
+  if (d < 1) return Status::Err(DBM_ERR_INVALID, "d must be >= 1");
+  if (k < 1 || k > kMaxEps)
+    return Status::Err(DBM_ERR_INVALID, "the number of eps values must be between 1 and 16");
+  if (l < 1) return Status::Err(DBM_ERR_INVALID, "At least one minPts value is required");
+  if (!eps || !minpts) return Status::Err(DBM_ERR_INVALID, "eps and minPts lists are required");
+  const float safe = std::sqrt(std::numeric_limits<float>::max());
+  for (int e = 0; e < k; ++e) {
+    if (!std::isfinite(eps[e]) || eps[e] <= 0.0f || eps[e] > safe)
+      return Status::Err(DBM_ERR_INVALID, "eps values must be finite, positive and not overflow eps^2");
+    if (e > 0 && !(eps[e] > eps[e - 1]))
+      return Status::Err(DBM_ERR_INVALID, "eps values must be strictly ascending (sort and deduplicate)");
+  }
+  for (int m = 0; m < l; ++m) {
+    if (minpts[m] <= 0) return Status::Err(DBM_ERR_INVALID, "min-samples values must be positive");
+    if (m > 0 && !(minpts[m] > minpts[m - 1]))
+      return Status::Err(DBM_ERR_INVALID, "min-samples values must be strictly ascending (sort and deduplicate)");
+  }
+  if (n >= (int64_t(1) << kCodeShift))
+    return Status::Err(DBM_ERR_TOO_LARGE, "N must be below 2^28");
+  if (d > (int64_t(1) << 20)) return Status::Err(DBM_ERR_TOO_LARGE, "D must be below 2^20");
+  return Status::Ok();
+}
+
+static Status read_err_flag(dbm_handle* h, cudaStream_t s)
+{
+  DBM_TRY(ensure_pinned(h, 4));
+  h->pinned[0] = 0;
+  DBM_CUDA(cudaMemcpyAsync(h->pinned, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  DBM_CUDA(cudaStreamSynchronize(s));
+  const int32_t f = static_cast<int32_t>(h->pinned[0] & 0xffffffff);
+  if (f & kErrTmaTimeout)
+    return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded TMA wait in the distance kernel ran out");
+  if (f & kErrUnionLimit)
+    return Status::Err(DBM_ERR_NOT_CONVERGED, "union-find retry bound ran out");
+  return Status::Ok();
+}
+
+// Degree-only pass: the distance kernel with no room for pairs still counts every pair.
+static Status neighbor_counts(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps,
+                              int k, int32_t* deg_out, cudaStream_t s)
+{
+  const int32_t one = 1;
+  DBM_TRY(validate(n, d, eps, k, &one, 1));
+  if (!x || !deg_out) return Status::Err(DBM_ERR_INVALID, "x and deg must be device pointers");
+  DBM_CUDA(cudaSetDevice(h->device));
+  float eps2[kMaxEps];
+  for (int e = 0; e < k; ++e) {
+    volatile float v = eps[e] * eps[e];
+    eps2[e] = v;
+  }
+  const int32_t di = static_cast<int32_t>(d);
+  const int64_t kn = static_cast<int64_t>(k) * n;
+  DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(padded_dims(di)) * padded_points(n)));
+  DBM_TRY(ensure(h->hist, sizeof(int32_t) * kn));
+  DBM_TRY(ensure(h->cc, sizeof(int32_t) * kn));
+  DBM_TRY(ensure(h->rowcnt, sizeof(int32_t) * n));
+  DBM_TRY(ensure(h->minpts, sizeof(int32_t)));
+  DBM_TRY(ensure(h->counters, 4 * sizeof(unsigned long long)));
+  DBM_TRY(ensure(h->err, 16));
+  DBM_TRY(ensure(h->edges, sizeof(uint64_t)));
+  DBM_CUDA(cudaMemcpyAsync(h->minpts.p, &one, sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  DBM_CUDA(cudaMemsetAsync(h->err.p, 0, 16, s));
+  DBM_CUDA(cudaMemsetAsync(h->hist.p, 0, sizeof(int32_t) * kn, s));
+  DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 4 * sizeof(unsigned long long), s));
+  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s));
+  DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
+               as<uint64_t>(h->edges), 0, as<int32_t>(h->hist), as<int32_t>(h->err), h->sm_count};
+  DBM_TRY(launch_distance(a, s));
+  DBM_TRY(launch_degrees(as<int32_t>(h->hist), n, k, as<int32_t>(h->minpts), 1, deg_out,
+                         as<int32_t>(h->cc), as<int32_t>(h->rowcnt), nullptr, s));
+  DBM_TRY(ensure_pinned(h, 4));
+  h->pinned[0] = 0;
+  DBM_CUDA(cudaMemcpyAsync(h->pinned, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  DBM_CUDA(cudaStreamSynchronize(s));
+  if (h->pinned[0] & kErrNonFinite) return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
+  if (h->pinned[0] & kErrTmaTimeout)
+    return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded TMA wait in the distance kernel ran out");
+  return Status::Ok();
+}
+
+static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps, int k,
+                  const int32_t* minpts, int l, int32_t* labels, uint8_t* core_out,
+                  const dbm_options& opt, dbm_stats& st, std::vector<uint8_t>& routes, cudaStream_t s)
+{
+  DBM_TRY(validate(n, d, eps, k, minpts, l));
+  if (!x || !labels) return Status::Err(DBM_ERR_INVALID, "x and labels must be device pointers");
+  DBM_CUDA(cudaSetDevice(h->device));
+
+  // ---- plan: budget and first batch size ----
+  Plan plan;
+  plan.use_cuvs = opt.backend != DBM_BACKEND_CODES;
+  plan.index_bits = opt.index_bits == 64 ? 64
+                    : opt.index_bits == 32 ? 32
+                    : (static_cast<long double>(n) * n >= static_cast<long double>(INT32_MAX) ? 64 : 32);
+  if (opt.max_bytes_per_batch == 0) {
+    size_t free_b = 0, total_b = 0;
+    DBM_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    const uint64_t reusable = h->workspace_bytes();
+    const uint64_t used = total_b - std::min<uint64_t>(total_b, free_b);
+    const uint64_t available = reusable > used ? total_b : std::min<uint64_t>(total_b, free_b + reusable);
+    plan.budget = 80 * available / 100;
+  } else {
+    plan.budget = opt.max_bytes_per_batch;
+  }
+  st.max_bytes_per_batch = plan.budget;
+  st.index_bits = plan.index_bits;
+  {
+    uint64_t bs0 = 0;
+    DBM_TRY(batch_size_rule(n, k, l, plan.budget, plan.use_cuvs, opt.neigh_per_row, plan.index_bits, &bs0));
+  }
+
+  float eps2[kMaxEps];
+  for (int e = 0; e < k; ++e) {
+    volatile float v = eps[e] * eps[e];  // float product, as the reference's host does
+    eps2[e] = v;
+  }
+
+  const int32_t di = static_cast<int32_t>(d);
+  const int32_t dp = padded_dims(di);
+  const int64_t npad = padded_points(n);
+  const int64_t kn = static_cast<int64_t>(k) * n;
+  const int64_t kln = kn * l;
+
+  // ---- buffers that do not depend on the graph ----
+  DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(dp) * npad));
+  DBM_TRY(ensure(h->hist, sizeof(int32_t) * kn));
+  DBM_TRY(ensure(h->deg, sizeof(int32_t) * kn));
+  DBM_TRY(ensure(h->cc, sizeof(int32_t) * kn));
+  DBM_TRY(ensure(h->rowcnt, sizeof(int32_t) * n));
+  DBM_TRY(ensure(h->off, sizeof(int64_t) * (n + 1)));
+  DBM_TRY(ensure(h->fill, sizeof(int32_t) * n));
+  DBM_TRY(ensure(h->minpts, sizeof(int32_t) * l));
+  DBM_TRY(ensure(h->counters, 4 * sizeof(unsigned long long)));
+  DBM_TRY(ensure(h->err, 16));
+  DBM_TRY(ensure(h->scan_scratch, std::max(scan_scratch_bytes(n + 1), scan_scratch_bytes(kln + 1))));
+  DBM_TRY(ensure_pinned(h, 16));
+
+  DBM_CUDA(cudaMemcpyAsync(h->minpts.p, minpts, sizeof(int32_t) * l, cudaMemcpyHostToDevice, s));
+  DBM_CUDA(cudaMemsetAsync(h->err.p, 0, 16, s));
+
+  // ---- distance pass ----
+  uint64_t found = 0;
+  {
+    PhaseTimer t(h, s, &st.ms_distance);
+    DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s));
+    uint64_t cap = h->edge_cap_hint;
+    if (cap == 0) {
+      const int64_t guess = opt.neigh_per_row > 0 ? opt.neigh_per_row : 16;
+      cap = static_cast<uint64_t>(n) * static_cast<uint64_t>(guess) / 2 + 1024;
+    }
+    for (int pass = 0; pass < 2; ++pass) {
+      DBM_TRY(ensure(h->edges, sizeof(uint64_t) * cap));
+      cap = h->edges.bytes / sizeof(uint64_t);
+      DBM_CUDA(cudaMemsetAsync(h->hist.p, 0, sizeof(int32_t) * kn, s));
+      DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 4 * sizeof(unsigned long long), s));
+      DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
+                   as<uint64_t>(h->edges), cap, as<int32_t>(h->hist), as<int32_t>(h->err), h->sm_count};
+      DBM_TRY(launch_distance(a, s));
+      st.distance_passes = pass + 1;
+      h->pinned[0] = 0;
+      h->pinned[1] = 0;
+      DBM_CUDA(cudaMemcpyAsync(h->pinned, h->counters.p, sizeof(unsigned long long),
+                               cudaMemcpyDeviceToHost, s));
+      DBM_CUDA(cudaMemcpyAsync(h->pinned + 1, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+      DBM_CUDA(cudaStreamSynchronize(s));
+      found = static_cast<uint64_t>(h->pinned[0]);
+      if (h->pinned[1] & kErrNonFinite)
+        return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
+      if (h->pinned[1] & kErrTmaTimeout)
+        return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded TMA wait in the distance kernel ran out");
+      if (found <= cap) break;
+      if (pass == 1) return Status::Err(DBM_ERR_CUDA, "neighbour-pair buffer overflowed twice");
+      cap = found;
+    }
+    h->edge_cap_hint = std::max<uint64_t>(h->edge_cap_hint, found);
+  }
+  st.unique_pairs = n * (n - 1) / 2;
+  st.edges = static_cast<int64_t>(found);
+
+  // ---- degrees, core counts, CSR ----
+  {
+    PhaseTimer t(h, s, &st.ms_graph);
+    DBM_TRY(launch_degrees(as<int32_t>(h->hist), n, k, as<int32_t>(h->minpts), l, as<int32_t>(h->deg),
+                           as<int32_t>(h->cc), as<int32_t>(h->rowcnt), core_out, s));
+    DBM_TRY(exclusive_scan_i32(as<int32_t>(h->rowcnt), as<int64_t>(h->off), n, h->scan_scratch.p,
+                               h->scan_scratch.bytes, s));
+    DBM_TRY(ensure(h->col, sizeof(uint32_t) * 2 * std::max<uint64_t>(found, 1)));
+    DBM_CUDA(cudaMemsetAsync(h->fill.p, 0, sizeof(int32_t) * n, s));
+    DBM_TRY(launch_csr_scatter(as<uint64_t>(h->edges), static_cast<int64_t>(found), as<int64_t>(h->off),
+                               as<int32_t>(h->fill), as<uint32_t>(h->col), s));
+  }
+
+  // ---- batch plan with the reference's correction rule ----
+  const uint64_t isz = isz_of(plan.index_bits);
+  const uint64_t per_entry = csr_bytes_per_entry(k, plan.use_cuvs, isz);
+  uint64_t cap_rows = static_cast<uint64_t>(n);
+  std::vector<int64_t> bnnz;
+  uint64_t bs = 0;
+  int64_t nb = 0;
+  bool planned = false;
+  for (int attempt = 0; attempt < 3 && !planned; ++attempt) {
+    uint64_t rule_bs = 0;
+    DBM_TRY(batch_size_rule(n, k, l, plan.budget, plan.use_cuvs, opt.neigh_per_row, plan.index_bits, &rule_bs));
+    bs = std::min(rule_bs, cap_rows);
+    nb = ceil_div(n, static_cast<int64_t>(bs));
+    st.attempts = attempt + 1;
+    DBM_TRY(ensure(h->bnnz, sizeof(int64_t) * nb));
+    DBM_TRY(ensure_pinned(h, static_cast<size_t>(nb)));
+    DBM_TRY(launch_batch_nnz(as<int64_t>(h->off), n, static_cast<int64_t>(bs), nb, as<int64_t>(h->bnnz), s));
+    DBM_CUDA(cudaMemcpyAsync(h->pinned, h->bnnz.p, sizeof(int64_t) * nb, cudaMemcpyDeviceToHost, s));
+    DBM_CUDA(cudaStreamSynchronize(s));
+    bnnz.assign(h->pinned, h->pinned + nb);
+    uint64_t available = opt.csr_cap_bytes;
+    if (available == 0) {
+      size_t fr = 0, to = 0;
+      DBM_CUDA(cudaMemGetInfo(&fr, &to));
+      available = fr;
+    }
+    int64_t measured = 0;
+    if (plan.use_cuvs) {
+      for (int64_t b = nb - 1; b >= 0; --b) {
+        const int64_t rows = std::min<int64_t>(n - b * static_cast<int64_t>(bs), static_cast<int64_t>(bs));
+        if (!csr_fits(bnnz[b], per_entry, available)) {
+          measured = measured_degree(bnnz[b], rows);
+          break;
+        }
+      }
+    } else {
+      const int64_t mx = *std::max_element(bnnz.begin(), bnnz.end());
+      if (!csr_fits(mx, per_entry, available)) measured = measured_degree(mx, static_cast<int64_t>(bs));
+    }
+    if (measured == 0) {
+      planned = true;
+      break;
+    }
+    st.batch_corrections += 1;
+    const int64_t degree = attempt == 0 ? measured : n;
+    const uint64_t new_cap = csr_rows_that_fit(degree, per_entry, available);
+    if (!(new_cap < bs))
+      return Status::Err(DBM_ERR_CSR_NOT_FIT,
+                         "the CSR does not fit in memory even with a batch of " + std::to_string(bs) +
+                           " rows (N=" + std::to_string(n) + ", measured degree " + std::to_string(measured) +
+                           "); reduce --max-mbytes-per-batch or revisit eps");
+    cap_rows = new_cap;
+  }
+  if (!planned) return Status::Err(DBM_ERR_CSR_NOT_FIT, "could not size the batch in 3 attempts");
+  st.batch_size = bs;
+  st.batches = static_cast<int32_t>(nb);
+  routes.assign(static_cast<size_t>(nb), DBM_BATCH_NOT_APPLICABLE);
+  st.max_nnz = 0;
+  st.total_nnz_max_eps = 0;
+  for (int64_t b = 0; b < nb; ++b) {
+    st.max_nnz = std::max<int64_t>(st.max_nnz, bnnz[b]);
+    st.total_nnz_max_eps += bnnz[b];
+    if (plan.use_cuvs && k > 1) {
+      const int64_t rows = std::min<int64_t>(n - b * static_cast<int64_t>(bs), static_cast<int64_t>(bs));
+      const bool annotate = opt.route == DBM_ROUTE_ANNOTATED ? true
+                            : opt.route == DBM_ROUTE_DENSE   ? false
+                                                             : annotate_pays(bnnz[b], n * rows, k, d);
+      routes[b] = annotate ? DBM_BATCH_ANNOTATED : DBM_BATCH_DENSE;
+      if (annotate) st.annotated_batches += 1; else st.dense_batches += 1;
+    }
+  }
+
+  // ---- labelling ----
+  {
+    PhaseTimer t(h, s, &st.ms_label);
+    int64_t max_slab = 0;
+    for (int64_t b = 0; b < nb; ++b) {
+      const int64_t rows = std::min<int64_t>(n - b * static_cast<int64_t>(bs), static_cast<int64_t>(bs));
+      max_slab = std::max<int64_t>(max_slab, bnnz[b] - rows);
+    }
+    DBM_TRY(ensure(h->G, sizeof(int32_t) * kln));
+    DBM_TRY(ensure(h->cur, sizeof(int32_t) * kln));
+    DBM_TRY(ensure(h->best, sizeof(unsigned long long) * kln));
+    if (nb > 1) DBM_TRY(ensure(h->L, sizeof(int32_t) * kln));
+    if (k > 1) {
+      DBM_TRY(ensure(h->slab_counts, sizeof(int32_t) * bs));
+      DBM_TRY(ensure(h->slab_off, sizeof(int64_t) * (bs + 1)));
+      DBM_TRY(ensure(h->slab_col, sizeof(int32_t) * std::max<int64_t>(max_slab, 1)));
+    }
+    DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur),
+                           as<unsigned long long>(h->best), s));
+    for (int64_t b = 0; b < nb; ++b) {
+      const int64_t s0 = b * static_cast<int64_t>(bs);
+      const int64_t rows = std::min<int64_t>(n - s0, static_cast<int64_t>(bs));
+      const uint32_t tag = static_cast<uint32_t>(nb - 1 - b);
+      for (int e = 0; e < k; ++e) {
+        Slab sl;
+        sl.s0 = s0;
+        sl.rows = rows;
+        if (e == k - 1) {
+          sl.off = as<int64_t>(h->off) + s0;
+          sl.col = reinterpret_cast<const int32_t*>(h->col.p);
+        } else {
+          DBM_TRY(launch_slab_counts(as<int32_t>(h->deg) + static_cast<int64_t>(e) * n, s0, rows,
+                                     as<int32_t>(h->slab_counts), s));
+          DBM_TRY(exclusive_scan_i32(as<int32_t>(h->slab_counts), as<int64_t>(h->slab_off), rows,
+                                     h->scan_scratch.p, h->scan_scratch.bytes, s));
+          DBM_TRY(launch_filter(as<int64_t>(h->off), as<uint32_t>(h->col), s0, rows, e,
+                                as<int64_t>(h->slab_off), as<int32_t>(h->slab_col), s));
+          sl.off = as<int64_t>(h->slab_off);
+          sl.col = as<int32_t>(h->slab_col);
+        }
+        DBM_TRY(launch_cc_batch(sl, n, l, e, as<int32_t>(h->cc) + static_cast<int64_t>(e) * n, nb == 1,
+                                as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
+                                as<int32_t>(h->cur), tag, as<int32_t>(h->err), s));
+      }
+    }
+  }
+
+  // ---- final relabel ----
+  {
+    PhaseTimer t(h, s, &st.ms_relabel);
+    DBM_TRY(ensure(h->flags, sizeof(int32_t) * kln));
+    DBM_TRY(ensure(h->rank, sizeof(int64_t) * (kln + 1)));
+    DBM_TRY(launch_cc_roots(n, k, l, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->flags), s));
+    DBM_TRY(exclusive_scan_i32(as<int32_t>(h->flags), as<int64_t>(h->rank), kln, h->scan_scratch.p,
+                               h->scan_scratch.bytes, s));
+    DBM_TRY(launch_cc_labels(n, k, l, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->cur),
+                             as<int64_t>(h->rank), labels, s));
+  }
+  DBM_TRY(read_err_flag(h, s));
+  return Status::Ok();
+}
+
+static dbm_options default_options()
+{
+  dbm_options o;
+  std::memset(&o, 0, sizeof(o));
+  o.backend = DBM_BACKEND_CUVS;
+  return o;
+}
+
+}  // namespace dbm
+
+// =============================================================================================
+// C ABI
+// =============================================================================================
+extern "C" {
+
+dbm_handle* dbm_create(int device, void* stream, char* err, size_t err_len)
+{
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0 || device < 0 || device >= count) {
+    cudaGetLastError();
+    dbm::set_err(err, err_len, "no CUDA device " + std::to_string(device));
+    return nullptr;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major < 10) {
+    dbm::set_err(err, err_len, "device " + std::to_string(device) + " is not sm_100 class");
+    return nullptr;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    dbm::set_err(err, err_len, "cudaSetDevice failed");
+    return nullptr;
+  }
+  dbm_handle* h = new dbm_handle();
+  h->device = device;
+  h->sm_count = prop.multiProcessorCount;
+  if (stream) {
+    h->stream = static_cast<cudaStream_t>(stream);
+  } else {
+    if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) {
+      delete h;
+      dbm::set_err(err, err_len, "cudaStreamCreate failed");
+      return nullptr;
+    }
+    h->own_stream = true;
+  }
+  return h;
+}
+
+void dbm_destroy(dbm_handle* h)
+{
+  if (!h) return;
+  cudaSetDevice(h->device);
+  cudaStreamSynchronize(h->stream);
+  dbm::Buffer* all[] = {&h->xt, &h->hist, &h->deg, &h->cc, &h->rowcnt, &h->off, &h->fill, &h->edges,
+                        &h->col, &h->minpts, &h->counters, &h->err, &h->slab_counts, &h->slab_off,
+                        &h->slab_col, &h->G, &h->L, &h->best, &h->cur, &h->flags, &h->rank,
+                        &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev, &h->core_dev};
+  for (auto* b : all)
+    if (b->p) cudaFree(b->p);
+  if (h->pinned) cudaFreeHost(h->pinned);
+  if (h->own_stream) cudaStreamDestroy(h->stream);
+  delete h;
+}
+
+uint64_t dbm_workspace_bytes(const dbm_handle* h) { return h ? h->workspace_bytes() : 0; }
+
+void dbm_set_phase_timing(dbm_handle* h, int enabled)
+{
+  if (h) h->timing = enabled != 0;
+}
+
+int dbm_fit_multi(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host,
+                  int k, const int32_t* min_pts_host, int l, int32_t* labels_dev, uint8_t* core_dev,
+                  const dbm_options* opt, dbm_stats* stats, uint8_t* batch_routes, int routes_len,
+                  void* stream, char* err, size_t err_len)
+{
+  if (!h) {
+    dbm::set_err(err, err_len, "null handle");
+    return DBM_ERR_INVALID;
+  }
+  const dbm_options o = opt ? *opt : dbm::default_options();
+  dbm_stats st;
+  std::memset(&st, 0, sizeof(st));
+  std::vector<uint8_t> routes;
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  const int64_t launches0 = dbm::launches_so_far();
+  dbm::Status r = dbm::fit(h, x_dev, n, d, eps_host, k, min_pts_host, l, labels_dev, core_dev, o, st,
+                           routes, s);
+  st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
+  if (r.ok()) {
+    cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) r = dbm::Status::Err(DBM_ERR_CUDA, cudaGetErrorString(e));
+  }
+  if (stats) *stats = st;
+  if (batch_routes && routes_len > 0) {
+    for (int i = 0; i < routes_len; ++i)
+      batch_routes[i] = i < static_cast<int>(routes.size()) ? routes[i] : DBM_BATCH_NOT_APPLICABLE;
+  }
+  if (!r.ok()) {
+    dbm::set_err(err, err_len, r.msg);
+    return r.code;
+  }
+  dbm::set_err(err, err_len, "");
+  return DBM_OK;
+}
+
+int dbm_fit_multi_host(dbm_handle* h, const float* x_host, int64_t n, int64_t d,
+                       const float* eps_host, int k, const int32_t* min_pts_host, int l,
+                       int32_t* labels_host, uint8_t* core_host, const dbm_options* opt,
+                       dbm_stats* stats, uint8_t* batch_routes, int routes_len, char* err,
+                       size_t err_len)
+{
+  if (!h || !x_host || !labels_host || n < 1 || d < 1 || k < 1 || l < 1) {
+    dbm::set_err(err, err_len, "invalid arguments");
+    return DBM_ERR_INVALID;
+  }
+  cudaSetDevice(h->device);
+  const size_t xb = sizeof(float) * static_cast<size_t>(n) * static_cast<size_t>(d);
+  const size_t lb = sizeof(int32_t) * static_cast<size_t>(n) * k * l;
+  dbm::Status r = dbm::ensure(h->xdev, xb);
+  if (r.ok()) r = dbm::ensure(h->labels_dev, lb);
+  if (r.ok() && core_host) r = dbm::ensure(h->core_dev, static_cast<size_t>(n) * k * l);
+  if (!r.ok()) {
+    dbm::set_err(err, err_len, r.msg);
+    return r.code;
+  }
+  if (cudaMemcpyAsync(h->xdev.p, x_host, xb, cudaMemcpyHostToDevice, h->stream) != cudaSuccess) {
+    dbm::set_err(err, err_len, "host-to-device copy of the points failed");
+    return DBM_ERR_CUDA;
+  }
+  int rc = dbm_fit_multi(h, static_cast<const float*>(h->xdev.p), n, d, eps_host, k, min_pts_host, l,
+                         static_cast<int32_t*>(h->labels_dev.p),
+                         core_host ? static_cast<uint8_t*>(h->core_dev.p) : nullptr, opt, stats,
+                         batch_routes, routes_len, h->stream, err, err_len);
+  if (rc != DBM_OK) return rc;
+  if (cudaMemcpyAsync(labels_host, h->labels_dev.p, lb, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess ||
+      (core_host && cudaMemcpyAsync(core_host, h->core_dev.p, static_cast<size_t>(n) * k * l,
+                                    cudaMemcpyDeviceToHost, h->stream) != cudaSuccess) ||
+      cudaStreamSynchronize(h->stream) != cudaSuccess) {
+    dbm::set_err(err, err_len, "device-to-host copy of the labels failed");
+    return DBM_ERR_CUDA;
+  }
+  const size_t total = static_cast<size_t>(n) * k * l;
+  for (size_t i = 0; i < total; ++i) {
+    if (labels_host[i] < -1 || labels_host[i] >= n) {
+      dbm::set_err(err, err_len, "invalid CUDA label at position " + std::to_string(i) + ": " +
+                                   std::to_string(labels_host[i]) + " (expected -1 <= label < " +
+                                   std::to_string(n) + ")");
+      return DBM_ERR_CUDA;
+    }
+  }
+  return DBM_OK;
+}
+
+int dbm_neighbor_counts(dbm_handle* h, const float* x_dev, int64_t n, int64_t d,
+                        const float* eps_host, int k, int32_t* deg_dev, void* stream, char* err,
+                        size_t err_len)
+{
+  if (!h) {
+    dbm::set_err(err, err_len, "null handle");
+    return DBM_ERR_INVALID;
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  dbm::Status r = dbm::neighbor_counts(h, x_dev, n, d, eps_host, k, deg_dev, s);
+  dbm::set_err(err, err_len, r.msg);
+  return r.code;
+}
+
+int dbm_batch_size(int64_t n, int k, int l, uint64_t max_bytes, int backend, int64_t neigh_per_row,
+                   int index_bits, uint64_t* batch_size_out, char* err, size_t err_len)
+{
+  if (n < 1 || k < 1 || l < 1 || !batch_size_out) {
+    dbm::set_err(err, err_len, "invalid arguments");
+    return DBM_ERR_INVALID;
+  }
+  const int bits = index_bits == 64 ? 64 : index_bits == 32 ? 32 : dbm_auto_index_bits(n);
+  dbm::Status r = dbm::batch_size_rule(n, k, l, max_bytes, backend != DBM_BACKEND_CODES,
+                                       neigh_per_row, bits, batch_size_out);
+  dbm::set_err(err, err_len, r.msg);
+  return r.code;
+}
+
+uint64_t dbm_max_bytes_for_batch_size(int64_t n, int k, int l, uint64_t batch_size, int backend,
+                                      int64_t neigh_per_row, int index_bits)
+{
+  const int bits = index_bits == 64 ? 64 : index_bits == 32 ? 32 : dbm_auto_index_bits(n);
+  const uint64_t isz = dbm::isz_of(bits);
+  return dbm::mem_fixed(n, k, l, isz) +
+         batch_size * dbm::mem_per_row(n, k, backend != DBM_BACKEND_CODES, neigh_per_row, isz) + 1;
+}
+
+int dbm_annotate_pays(int64_t nnz, int64_t pairs, int k, int64_t d)
+{
+  return dbm::annotate_pays(nnz, pairs, k, d);
+}
+
+int dbm_auto_index_bits(int64_t n)
+{
+  return static_cast<long double>(n) * n >= static_cast<long double>(INT32_MAX) ? 64 : 32;
+}
+
+const char* dbm_build_info_json(void)
+{
+  return "{\"git_sha\":\"" DBM_GIT_SHA "\",\"revision_kind\":\"provided\",\"git_dirty\":null,"
+         "\"build_id\":\"" DBM_BUILD_ID "\",\"cuda_arch\":\"sm_100a\","
+         "\"configured_backend\":\"cuvs\",\"compiled_backends\":[\"cuvs\",\"codes\"],"
+         "\"flags\":\"arch=sm_100a,O3,fmad=default\","
+         "\"neighborhood_kernel\":\"dbm-sm100a-fp32-triangle-tma\"}";
+}
+
+}  // extern "C"

@@ -1,0 +1,236 @@
+// cc.cu -- batched connected components, cross-batch label merge and final relabel.
+//
+// What the reference computes (Math-BUG/cuML-DBSCANMulti, runner_multi.cuh:1045-1092 and
+// 1228-1234, with RAFT's weak_cc_batched / merge_labels / make_monotonic): for each config,
+// batches in ascending order, a weak-CC over the batch's rows with the core mask as filter
+// (labels min-index + 1 per core component, non-core points take the smallest adjacent core
+// label the batch can see), merged into the accumulated labels by a root map R, then ids by
+// rank of the surviving labels.  The resulting labels have a closed form that these kernels
+// evaluate directly, with one global union-find instead of a merge per batch:
+//
+//   core point c:   label = minimum index of c's core component (over every batch's edges);
+//   border point p: cur(p) is folded batch by batch, b = 0..nb-1, as
+//                     cur = min(G_b(cur), G_b(L_b*(p)))
+//                   where G_b is the global union-find after batch b's edges, and L_b*(p) is the
+//                   smallest batch-local component root among the core neighbours of p that
+//                   batch b can see (edges whose row lies in batch b).  That is exactly the
+//                   value RAFT's merge leaves in labels_a, including its dependence on the
+//                   batch partition and order for points adjacent to several clusters.
+//
+// Everything is min-index union-find: roots are hooked larger-under-smaller with atomicCAS,
+// so a root is always its tree's minimum and the fixpoint does not depend on thread order.
+// Per-(batch, eps) kernels process the l minPts configs of that eps together: with minPts
+// ascending, a point is core for config (e, m) iff m < corecnt[e][i].
+#include "dbm_internal.cuh"
+
+namespace dbm {
+
+
+__global__ void cc_init_kernel(int64_t n, int64_t total, int32_t* __restrict__ G,
+                               int32_t* __restrict__ cur, unsigned long long* __restrict__ best)
+{
+  const int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (x >= total) return;
+  G[x] = static_cast<int32_t>(x % n);
+  cur[x] = kNone;
+  best[x] = ~0ull;
+}
+
+// L[cfg][v] = v for both endpoints of every slab edge (configs where v is core).
+__global__ void cc_touch_kernel(Slab sl, int64_t n, int l, int cfg0, const int32_t* __restrict__ cc,
+                                int32_t* __restrict__ L)
+{
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= sl.rows) return;
+  const int64_t r = sl.s0 + t;
+  const int cr = cc[r];
+  for (int m = 0; m < cr; ++m) L[static_cast<int64_t>(cfg0 + m) * n + r] = static_cast<int32_t>(r);
+  for (int64_t q = sl.off[t]; q < sl.off[t + 1]; ++q) {
+    const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
+    const int cj = cc[j];
+    for (int m = 0; m < cj; ++m) L[static_cast<int64_t>(cfg0 + m) * n + j] = j;
+  }
+}
+
+// unite(P[cfg], r, j) for every core-core slab edge
+__global__ void cc_union_kernel(Slab sl, int64_t n, int l, int cfg0, const int32_t* __restrict__ cc,
+                                int32_t* __restrict__ P, int32_t* __restrict__ err)
+{
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= sl.rows) return;
+  const int64_t r = sl.s0 + t;
+  const int cr = cc[r];
+  if (cr == 0) return;
+  bool ok = true;
+  for (int64_t q = sl.off[t]; q < sl.off[t + 1]; ++q) {
+    const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
+    const int mm = min(cr, cc[j]);
+    for (int m = 0; m < mm; ++m)
+      ok &= uf_unite(P + static_cast<int64_t>(cfg0 + m) * n, static_cast<int32_t>(r), j);
+  }
+  if (!ok) atomicOr(err, kErrUnionLimit);
+}
+
+// For every slab edge with exactly one core endpoint c: best[p] = min(tag << 32 | find(P, c)).
+__global__ void cc_best_kernel(Slab sl, int64_t n, int l, int cfg0, const int32_t* __restrict__ cc,
+                               int32_t* __restrict__ P, unsigned long long* __restrict__ best,
+                               uint32_t tag)
+{
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= sl.rows) return;
+  const int64_t r = sl.s0 + t;
+  const int cr = cc[r];
+  for (int64_t q = sl.off[t]; q < sl.off[t + 1]; ++q) {
+    const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
+    const int cj = cc[j];
+    const int lo = min(cr, cj), hi = max(cr, cj);
+    for (int m = lo; m < hi; ++m) {
+      const bool r_core = m < cr;
+      const int32_t c = r_core ? static_cast<int32_t>(r) : j;
+      const int64_t p = r_core ? static_cast<int64_t>(j) : r;
+      const int64_t base = static_cast<int64_t>(cfg0 + m) * n;
+      const int32_t root = uf_find(P + base, c);
+      atomicMin(best + base + p,
+                (static_cast<unsigned long long>(tag) << 32) | static_cast<uint32_t>(root));
+    }
+  }
+}
+
+// cur[p] = min(find(G, cur[p]), find(G, best[p])) for every border endpoint of the slab.
+__global__ void cc_border_kernel(Slab sl, int64_t n, int l, int cfg0, const int32_t* __restrict__ cc,
+                                 int32_t* __restrict__ G, const unsigned long long* __restrict__ best,
+                                 int32_t* __restrict__ cur, uint32_t tag)
+{
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= sl.rows) return;
+  const int64_t r = sl.s0 + t;
+  const int cr = cc[r];
+  for (int64_t q = sl.off[t]; q < sl.off[t + 1]; ++q) {
+    const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
+    const int cj = cc[j];
+    const int lo = min(cr, cj), hi = max(cr, cj);
+    for (int m = lo; m < hi; ++m) {
+      const bool r_core = m < cr;
+      const int64_t p = r_core ? static_cast<int64_t>(j) : r;
+      const int64_t base = static_cast<int64_t>(cfg0 + m) * n;
+      const unsigned long long v = best[base + p];
+      if (static_cast<uint32_t>(v >> 32) != tag) continue;
+      const int32_t cand = uf_find(G + base, static_cast<int32_t>(v & 0xffffffffu));
+      volatile int32_t* cp = cur + base + p;
+      const int32_t old = *cp;
+      const int32_t prev = (old == kNone) ? kNone : uf_find(G + base, old);
+      *cp = prev < cand ? prev : cand;
+    }
+  }
+}
+
+// flags[cfg][i] = 1 for the root of every core component (compressing G on the way)
+__global__ void cc_roots_kernel(int64_t n, int k, int l, const int32_t* __restrict__ cc,
+                                int32_t* __restrict__ G, int32_t* __restrict__ flags)
+{
+  const int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = n * k * l;
+  if (x >= total) return;
+  const int64_t cfg = x / n, i = x - cfg * n;
+  const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
+  int32_t f = 0;
+  if (m < cc[static_cast<int64_t>(e) * n + i]) {
+    const int32_t root = uf_find(G + cfg * n, static_cast<int32_t>(i));
+    f = (root == static_cast<int32_t>(i));
+  }
+  flags[x] = f;
+}
+
+// cluster id = rank of the component root among the config's roots; -1 noise
+__global__ void cc_labels_kernel(int64_t n, int k, int l, const int32_t* __restrict__ cc,
+                                 int32_t* __restrict__ G, const int32_t* __restrict__ cur,
+                                 const int64_t* __restrict__ rank, int32_t* __restrict__ labels)
+{
+  const int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = n * k * l;
+  if (x >= total) return;
+  const int64_t cfg = x / n, i = x - cfg * n;
+  const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
+  int32_t* g = G + cfg * n;
+  const int64_t r0 = rank[cfg * n];
+  int32_t out;
+  if (m < cc[static_cast<int64_t>(e) * n + i]) {
+    const int32_t root = uf_find(g, static_cast<int32_t>(i));
+    out = static_cast<int32_t>(rank[cfg * n + root] - r0);
+  } else {
+    const int32_t v = cur[x];
+    if (v == kNone) {
+      out = -1;
+    } else {
+      const int32_t root = uf_find(g, v);
+      out = static_cast<int32_t>(rank[cfg * n + root] - r0);
+    }
+  }
+  labels[x] = out;
+}
+
+// ---- launchers ----------------------------------------------------------------------------
+static inline unsigned blocks_for(int64_t work, int threads)
+{
+  return static_cast<unsigned>(ceil_div(work > 0 ? work : 1, threads));
+}
+
+Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigned long long* best,
+                      cudaStream_t s)
+{
+  const int64_t total = n * k * l;
+  count_launch();
+  cc_init_kernel<<<blocks_for(total, 256), 256, 0, s>>>(n, total, G, cur, best);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// One batch of one eps: local components (when there is more than one batch), border
+// candidates, global union, border fold.
+Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, const int32_t* cc_e, bool single_batch,
+                       int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur, uint32_t tag,
+                       int32_t* err, cudaStream_t s)
+{
+  if (sl.rows <= 0) return Status::Ok();
+  const int cfg0 = e * l;
+  const unsigned nb = blocks_for(sl.rows, 128);
+  if (single_batch) {
+    count_launch();
+    cc_union_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, G, err);
+    count_launch();
+    cc_best_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, G, best, tag);
+  } else {
+    count_launch();
+    cc_touch_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, L);
+    count_launch();
+    cc_union_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, L, err);
+    count_launch();
+    cc_best_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, L, best, tag);
+    count_launch();
+    cc_union_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, G, err);
+  }
+  count_launch();
+  cc_border_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, G, best, cur, tag);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+Status launch_cc_roots(int64_t n, int k, int l, const int32_t* cc, int32_t* G, int32_t* flags,
+                       cudaStream_t s)
+{
+  count_launch();
+  cc_roots_kernel<<<blocks_for(n * k * l, 256), 256, 0, s>>>(n, k, l, cc, G, flags);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+Status launch_cc_labels(int64_t n, int k, int l, const int32_t* cc, int32_t* G, const int32_t* cur,
+                        const int64_t* rank, int32_t* labels, cudaStream_t s)
+{
+  count_launch();
+  cc_labels_kernel<<<blocks_for(n * k * l, 256), 256, 0, s>>>(n, k, l, cc, G, cur, rank, labels);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+}  // namespace dbm

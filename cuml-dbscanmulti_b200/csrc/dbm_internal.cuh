@@ -1,0 +1,180 @@
+// dbm_internal.cuh -- shared device helpers and host plumbing of libdbm.so (sm_100a).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/dbm.h"
+
+namespace dbm {
+
+// ---- status plumbing (host) ------------------------------------------------------------
+struct Status {
+  int code = DBM_OK;
+  std::string msg;
+  bool ok() const { return code == DBM_OK; }
+  static Status Ok() { return Status{}; }
+  static Status Err(int c, std::string m) { return Status{c, std::move(m)}; }
+};
+
+#define DBM_CUDA(call)                                                                       \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      return ::dbm::Status::Err(e_ == cudaErrorMemoryAllocation ? DBM_ERR_OOM : DBM_ERR_CUDA, \
+                                std::string(#call) + ": " + cudaGetErrorString(e_));         \
+  } while (0)
+
+#define DBM_TRY(expr)                 \
+  do {                                \
+    ::dbm::Status s_ = (expr);        \
+    if (!s_.ok()) return s_;          \
+  } while (0)
+
+// ---- constants -------------------------------------------------------------------------
+constexpr uint8_t kNoNeighbor = 255;      // per-pair code when no eps contains the pair
+constexpr int kMaxEps = DBM_MAX_EPS;
+constexpr uint32_t kColMask = 0x0FFFFFFFu; // packed neighbour word: code << 28 | column
+constexpr int kCodeShift = 28;
+constexpr int32_t kNone = INT32_MAX;       // "no label yet" / noise before relabel
+
+// device error flags (bitmask written by kernels, read by the host after a stage)
+constexpr int kErrTmaTimeout = 1;
+constexpr int kErrUnionLimit = 2;
+constexpr int kErrNonFinite = 4;
+
+// ---- small device helpers ----------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// mbarrier / TMA (PTX ISA 8.x, sm_90+; used here on sm_100a)
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init()
+{
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+  uint32_t done;
+  asm volatile(
+    "{\n\t.reg .pred p;\n\t"
+    "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+    "selp.u32 %0, 1, 0, p;\n\t}"
+    : "=r"(done)
+    : "r"(smem_u32(bar)), "r"(parity)
+    : "memory");
+  return done != 0;
+}
+// Bounded wait: gives up after `limit` polls (each poll may suspend briefly in hardware).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit)
+{
+  for (uint32_t it = 0; it < limit; ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 2-D tiled TMA load (no multicast) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                            uint64_t* bar)
+{
+  asm volatile(
+    "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+    " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+    "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+    : "memory");
+}
+
+// ---- union-find with minimum-index roots --------------------------------------------------
+// Roots are always the smallest index of their tree: a root is only ever re-pointed at a
+// smaller root, so a fully compressed parent array maps every member to its component's
+// minimum index.  Path halving writes only ancestors, so concurrent finds are safe.
+__device__ __forceinline__ int32_t uf_find(int32_t* parent, int32_t x)
+{
+  volatile int32_t* p = parent;
+  int32_t px = p[x];
+  while (px != x) {
+    const int32_t gp = p[px];
+    if (gp != px) p[x] = gp;
+    x = px;
+    px = p[x];
+  }
+  return x;
+}
+
+// Returns false if the retry bound ran out (never expected; reported as an error flag).
+__device__ __forceinline__ bool uf_unite(int32_t* parent, int32_t a, int32_t b)
+{
+  for (int it = 0; it < (1 << 20); ++it) {
+    a = uf_find(parent, a);
+    b = uf_find(parent, b);
+    if (a == b) return true;
+    if (a > b) {
+      const int32_t t = a;
+      a = b;
+      b = t;
+    }
+    // hook the larger root under the smaller one
+    const int32_t old = atomicCAS(parent + b, b, a);
+    if (old == b) return true;
+    b = old;
+  }
+  return false;
+}
+
+// ---- launch descriptors shared by the orchestrator and the kernels ------------------------
+// One CSR slab: the rows [s0, s0 + rows) of a batch, entries col[off[t] .. off[t+1]) for row
+// s0 + t; only the low 28 bits of a column word are the neighbour id.
+struct Slab {
+  const int64_t* off;
+  const int32_t* col;
+  int64_t s0, rows;
+};
+
+struct DistLaunch {
+  int64_t n;
+  int32_t d, k;
+  const float* xt;                 // dp x npad, dim-major
+  const float* eps2;               // host, k values
+  unsigned long long* counters;    // [0] pair cursor, [1] tile cursor
+  uint64_t* edges;
+  uint64_t edge_cap;
+  int32_t* hist;                   // k x n
+  int32_t* err;
+  int sm_count;
+};
+
+// ---- kernel launch accounting (host) --------------------------------------------------------
+// Every kernel launch site calls count_launch(); dbm_stats.launches reports the difference
+// over one fit (the bench's evidence that the native kernels ran).
+int64_t count_launch(int64_t n = 1);
+int64_t launches_so_far();
+
+// ---- scans (host launchers, implemented in graph.cu) ------------------------------------
+// exclusive scan of n int32 counts into n+1 int64 offsets (out[n] = total)
+Status exclusive_scan_i32(const int32_t* in, int64_t* out, int64_t n, void* scratch,
+                          size_t scratch_bytes, cudaStream_t s);
+size_t scan_scratch_bytes(int64_t n);
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace dbm

@@ -1,0 +1,278 @@
+// graph.cu -- degrees, core counts, scans and CSR construction (HBM-bound integer kernels).
+//
+// Reference counterparts (Math-BUG/cuML-DBSCANMulti):
+//   degrees_kernel       per-eps degree vectors vd[e] (eps_neighborhood.cuh:171-174, 370-378)
+//                        and the k*l core masks (corepoints_multi.cuh:86-123): a point is core
+//                        for (e, m) iff degree_e >= minPts[m]; with minPts ascending that is
+//                        m < corecnt[e][i].
+//   exclusive_scan_i32   thrust::exclusive_scan of the degrees (csr_multi_eps.cuh:320-323,
+//                        third_party/cuml/cpp/src/dbscan/adjgraph/algo.cuh:54)
+//   csr_scatter_kernel   the max-eps CSR with a code per entry that the reference builds with
+//                        adj_to_csr + annotateKernel (adjgraph/algo.cuh:56-57,
+//                        csr_multi_eps.cuh:93-185); here it is filled straight from the
+//                        neighbour pairs the distance kernel emitted, both directions.
+//   filter_kernel        order-preserving per-row compaction of the max-eps CSR to eps_e
+//                        (filterKernel, csr_multi_eps.cuh:194-234): the annotated route.
+//   batch_nnz_kernel     per-batch nnz at the largest eps (runner_multi.cuh:898-904).
+#include "dbm_internal.cuh"
+
+namespace dbm {
+
+// ---- scan ---------------------------------------------------------------------------------
+constexpr int kScanThreads = 1024;
+constexpr int kScanItems = 4;
+constexpr int64_t kScanBlock = kScanThreads * kScanItems;
+
+template <typename T>
+__device__ __forceinline__ T block_exclusive_sum(T v, T* warp_sums, T& total)
+{
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  T incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const T u = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += u;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    T w = (lane < (blockDim.x >> 5)) ? warp_sums[lane] : T(0);
+    T wi = w;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const T u = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += u;
+    }
+    warp_sums[lane] = wi - w;
+    if (lane == 31) warp_sums[32] = wi;
+  }
+  __syncthreads();
+  const T res = warp_sums[warp] + incl - v;
+  total = warp_sums[32];
+  __syncthreads();
+  return res;
+}
+
+__global__ void scan_partials_kernel(const int32_t* __restrict__ in, int64_t n,
+                                     int64_t* __restrict__ partials)
+{
+  __shared__ int64_t ws[33];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock + threadIdx.x * kScanItems;
+  int64_t s = 0;
+#pragma unroll
+  for (int q = 0; q < kScanItems; ++q)
+    if (base + q < n) s += in[base + q];
+  int64_t total;
+  block_exclusive_sum<int64_t>(s, ws, total);
+  if (threadIdx.x == 0) partials[blockIdx.x] = total;
+}
+
+__global__ void scan_top_kernel(int64_t* __restrict__ partials, int64_t nparts)
+{
+  __shared__ int64_t ws[33];
+  __shared__ int64_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int64_t b0 = 0; b0 < nparts; b0 += kScanThreads) {
+    const int64_t i = b0 + threadIdx.x;
+    const int64_t v = i < nparts ? partials[i] : 0;
+    int64_t total;
+    const int64_t ex = block_exclusive_sum<int64_t>(v, ws, total);
+    if (i < nparts) partials[i] = carry + ex;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) partials[nparts] = carry;
+}
+
+__global__ void scan_final_kernel(const int32_t* __restrict__ in, int64_t n,
+                                  const int64_t* __restrict__ partials, int64_t* __restrict__ out,
+                                  int64_t nparts)
+{
+  __shared__ int64_t ws[33];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanBlock + threadIdx.x * kScanItems;
+  int64_t v[kScanItems];
+  int64_t s = 0;
+#pragma unroll
+  for (int q = 0; q < kScanItems; ++q) {
+    v[q] = (base + q < n) ? in[base + q] : 0;
+    s += v[q];
+  }
+  int64_t total;
+  int64_t ex = block_exclusive_sum<int64_t>(s, ws, total) + partials[blockIdx.x];
+#pragma unroll
+  for (int q = 0; q < kScanItems; ++q) {
+    if (base + q < n) out[base + q] = ex;
+    ex += v[q];
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) out[n] = partials[nparts];
+}
+
+size_t scan_scratch_bytes(int64_t n) { return sizeof(int64_t) * (ceil_div(n, kScanBlock) + 2); }
+
+Status exclusive_scan_i32(const int32_t* in, int64_t* out, int64_t n, void* scratch,
+                          size_t scratch_bytes, cudaStream_t s)
+{
+  if (n <= 0) {
+    DBM_CUDA(cudaMemsetAsync(out, 0, sizeof(int64_t), s));
+    return Status::Ok();
+  }
+  const int64_t nparts = ceil_div(n, kScanBlock);
+  if (scratch_bytes < scan_scratch_bytes(n))
+    return Status::Err(DBM_ERR_INVALID, "scan scratch too small");
+  int64_t* partials = static_cast<int64_t*>(scratch);
+  count_launch();
+  scan_partials_kernel<<<static_cast<unsigned>(nparts), kScanThreads, 0, s>>>(in, n, partials);
+  count_launch();
+  scan_top_kernel<<<1, kScanThreads, 0, s>>>(partials, nparts);
+  count_launch();
+  scan_final_kernel<<<static_cast<unsigned>(nparts), kScanThreads, 0, s>>>(in, n, partials, out,
+                                                                          nparts);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// ---- degrees and core counts ----------------------------------------------------------------
+// deg[e][i] = 1 + sum_{c <= e} hist[c][i]; corecnt[e][i] = #{m : deg >= minpts[m]};
+// rowcnt[i] = deg[k-1][i] - 1 (max-eps neighbours without the point itself).
+__global__ void degrees_kernel(const int32_t* __restrict__ hist, int64_t n, int k,
+                               const int32_t* __restrict__ minpts, int l, int32_t* __restrict__ deg,
+                               int32_t* __restrict__ corecnt, int32_t* __restrict__ rowcnt,
+                               uint8_t* __restrict__ core_out)
+{
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int32_t run = 1;
+  for (int e = 0; e < k; ++e) {
+    run += hist[static_cast<int64_t>(e) * n + i];
+    deg[static_cast<int64_t>(e) * n + i] = run;
+    // minpts ascending: count of thresholds <= run by binary search
+    int lo = 0, hi = l;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (__ldg(minpts + mid) <= run) lo = mid + 1; else hi = mid;
+    }
+    corecnt[static_cast<int64_t>(e) * n + i] = lo;
+    if (core_out) {
+      for (int m = 0; m < l; ++m)
+        core_out[(static_cast<int64_t>(e) * l + m) * n + i] = static_cast<uint8_t>(m < lo);
+    }
+  }
+  rowcnt[i] = run - 1;
+}
+
+Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
+                      int32_t* deg, int32_t* corecnt, int32_t* rowcnt, uint8_t* core_out,
+                      cudaStream_t s)
+{
+  count_launch();
+  degrees_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(hist, n, k, minpts, l, deg,
+                                                                         corecnt, rowcnt, core_out);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// ---- max-eps CSR from the neighbour pairs ---------------------------------------------------
+__global__ void csr_scatter_kernel(const uint64_t* __restrict__ edges, int64_t m,
+                                   const int64_t* __restrict__ off, int32_t* __restrict__ fill,
+                                   uint32_t* __restrict__ col)
+{
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= m) return;
+  const uint64_t w = edges[q];
+  const uint32_t i = static_cast<uint32_t>(w >> 32);
+  const uint32_t lo = static_cast<uint32_t>(w);
+  const uint32_t j = lo & kColMask;
+  const uint32_t code = lo & ~kColMask;
+  const int32_t pi = atomicAdd(fill + i, 1);
+  col[off[i] + pi] = code | j;
+  const int32_t pj = atomicAdd(fill + j, 1);
+  col[off[j] + pj] = code | i;
+}
+
+Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, int32_t* fill,
+                          uint32_t* col, cudaStream_t s)
+{
+  if (m <= 0) return Status::Ok();
+  count_launch();
+  csr_scatter_kernel<<<static_cast<unsigned>(ceil_div(m, 256)), 256, 0, s>>>(edges, m, off, fill, col);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// per-batch nnz at the largest eps, self pairs included (the reference's vd[n_points])
+__global__ void batch_nnz_kernel(const int64_t* __restrict__ off, int64_t n, int64_t bs, int64_t nb,
+                                 int64_t* __restrict__ out)
+{
+  const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (b >= nb) return;
+  const int64_t s0 = b * bs;
+  const int64_t t0 = (s0 + bs < n) ? (s0 + bs) : n;
+  out[b] = off[t0] - off[s0] + (t0 - s0);
+}
+
+Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, int64_t* out,
+                        cudaStream_t s)
+{
+  count_launch();
+  batch_nnz_kernel<<<static_cast<unsigned>(ceil_div(nb, 256)), 256, 0, s>>>(off, n, bs, nb, out);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// ---- per-eps compaction of a batch slab (annotated route) ----------------------------------
+// counts[r] = deg[e][s+r] - 1 for the batch rows
+__global__ void slab_counts_kernel(const int32_t* __restrict__ deg_e, int64_t s0, int64_t rows,
+                                   int32_t* __restrict__ counts)
+{
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r < rows) counts[r] = deg_e[s0 + r] - 1;
+}
+
+// One warp per row: ballot over the row's entries keeps those with code <= e, in order.
+__global__ void filter_kernel(const int64_t* __restrict__ off, const uint32_t* __restrict__ col,
+                              int64_t s0, int64_t rows, uint32_t e,
+                              const int64_t* __restrict__ off_e, int32_t* __restrict__ col_e)
+{
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int64_t r = s0 + warp;
+  const int64_t beg = off[r], end = off[r + 1];
+  int64_t out = off_e[warp];
+  for (int64_t q0 = beg; q0 < end; q0 += 32) {
+    const int64_t q = q0 + lane;
+    uint32_t w = 0;
+    bool keep = false;
+    if (q < end) {
+      w = col[q];
+      keep = (w >> kCodeShift) <= e;
+    }
+    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+    if (keep) col_e[out + __popc(bal & ((1u << lane) - 1u))] = static_cast<int32_t>(w & kColMask);
+    out += __popc(bal);
+  }
+}
+
+Status launch_slab_counts(const int32_t* deg_e, int64_t s0, int64_t rows, int32_t* counts,
+                          cudaStream_t s)
+{
+  count_launch();
+  slab_counts_kernel<<<static_cast<unsigned>(ceil_div(rows, 256)), 256, 0, s>>>(deg_e, s0, rows, counts);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int e,
+                     const int64_t* off_e, int32_t* col_e, cudaStream_t s)
+{
+  const int64_t threads = rows * 32;
+  count_launch();
+  filter_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(
+    off, col, s0, rows, static_cast<uint32_t>(e), off_e, col_e);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+}  // namespace dbm

@@ -1,0 +1,173 @@
+/*
+ * dbm.h -- C ABI of the B200-native multi-parameter DBSCAN (`fit_multi`) library, libdbm.so.
+ *
+ * One call clusters N points under every (eps, minPts) pair of a k x l grid and returns k*l
+ * label vectors (config = e*l + m, eps-major, -1 = noise) plus the k*l core masks.  Labels
+ * are identical, bit for bit, to the reference implementation's for the same float32 input
+ * and the same batch partition.
+ *
+ * Reference interfaces replaced (Math-BUG/cuML-DBSCANMulti):
+ *   dbm_fit_multi          ML::Dbscan::Multi::fit_multi<float, Index_>
+ *                          (src/multi/runner_multi.cuh:1290-1307), as driven by
+ *                          fit_com_handle (src/main.cu:498-598)
+ *   dbm_fit_multi_host     the CLI's fit() path with host buffers: H2D of points, fit,
+ *                          D2H of labels with the range check (src/main.cu:527-598)
+ *   dbm_neighbor_counts    VertexDeg::run_multi's per-eps degrees
+ *                          (src/multi/eps_neighborhood.cuh:440-479)
+ *   dbm_batch_size         compute_batch_size_multi (src/multi/runner_multi.cuh:458-499)
+ *   dbm_max_bytes_for_batch_size  max_bytes_for_batch_size (runner_multi.cuh:437-447)
+ *   dbm_annotate_pays      anotar_compensa (runner_multi.cuh:405-415)
+ *   dbm_options.route      rota_forcada (runner_multi.cuh:426-430)
+ *   dbm_options.csr_cap_bytes  csr_teto_de_teste (runner_multi.cuh:145-149)
+ *   dbm_stats              ExecutionStats / last_execution_stats (runner_multi.cuh:175-208),
+ *                          returned per call instead of thread-local
+ *   dbm_handle             the caller-owned workspace + BuffersCsr pair reused across calls
+ *                          (runner_multi.cuh:516-526, src/main.cu:621-645)
+ *   dbm_build_info_json    write_build_json (src/main.cu:130-156)
+ *
+ * Conventions: every entry point returns DBM_OK (0) or a negative DBM_ERR_* code and never
+ * aborts the process; a human-readable message goes to `err` (NUL-terminated, truncated
+ * to err_len) when err != NULL.  Device pointers are plain CUDA device addresses on the
+ * handle's device; `stream` is a cudaStream_t (NULL = the handle's own stream).  One fit
+ * per handle at a time.
+ */
+#ifndef DBM_H
+#define DBM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------- */
+#define DBM_OK 0
+#define DBM_ERR_INVALID (-1)          /* bad argument: k outside 1..16 (eps_neighborhood.cuh:455),
+                                         unsorted/duplicate lists, non-positive minPts, N<1 ... */
+#define DBM_ERR_FIXED_BUFFERS (-2)    /* fixed buffers exceed the budget (runner_multi.cuh:474-479) */
+#define DBM_ERR_INDEX_OVERFLOW (-3)   /* N too large for the index type (runner_multi.cuh:485-495) */
+#define DBM_ERR_CSR_NOT_FIT (-4)      /* CSR does not fit after the batch corrections
+                                         (runner_multi.cuh:1438-1445, 1456) */
+#define DBM_ERR_CUDA (-5)             /* a CUDA runtime call failed */
+#define DBM_ERR_OOM (-6)              /* device allocation failed */
+#define DBM_ERR_NOT_CONVERGED (-7)    /* a bounded device wait or iteration limit ran out */
+#define DBM_ERR_NO_DEVICE (-8)        /* no usable sm_100 device */
+#define DBM_ERR_TOO_LARGE (-9)        /* N >= 2^28 (column index + code share one 32-bit word) */
+#define DBM_ERR_NONFINITE (-10)       /* NaN/Inf in the points (src/main.cu:1419-1423) */
+
+#define DBM_MAX_EPS 16
+
+/* ---- options / statistics ------------------------------------------------------------ */
+#define DBM_BACKEND_CUVS 0   /* batch sizing + per-batch route policy of the reference's
+                                default (cuVS) backend */
+#define DBM_BACKEND_CODES 1  /* batch sizing of the reference's codes backend; no routes */
+
+#define DBM_ROUTE_AUTO 0
+#define DBM_ROUTE_ANNOTATED 1
+#define DBM_ROUTE_DENSE 2
+
+/* values written to batch_routes[] */
+#define DBM_BATCH_NOT_APPLICABLE 0
+#define DBM_BATCH_ANNOTATED 1
+#define DBM_BATCH_DENSE 2
+
+typedef struct dbm_options {
+  int backend;                /* DBM_BACKEND_* (reference CLI --backend; default cuvs) */
+  int index_bits;             /* 0 = auto (64 iff N*N >= INT32_MAX), 32 or 64 (--index) */
+  int route;                  /* DBM_ROUTE_* (--route) */
+  int64_t neigh_per_row;      /* expected neighbours per row for batch sizing; 0 = N (--neigh-per-row) */
+  uint64_t max_bytes_per_batch; /* memory budget; 0 = 80% of free + reusable (--max-mbytes-per-batch) */
+  uint64_t csr_cap_bytes;     /* test knob: pretend only this much memory is free for the CSR
+                                 check; 0 = real free memory */
+} dbm_options;
+
+typedef struct dbm_stats {
+  uint64_t max_bytes_per_batch; /* effective budget */
+  uint64_t batch_size;
+  int32_t batches;
+  int32_t attempts;
+  int32_t batch_corrections;
+  int32_t dense_batches;
+  int32_t annotated_batches;
+  int32_t index_bits;           /* index type the batch arithmetic used */
+  int64_t max_nnz;              /* largest per-batch CSR (max eps, reference accounting) */
+  int64_t total_nnz_max_eps;    /* sum over batches of the max-eps nnz (self pairs included) */
+  int64_t unique_pairs;         /* distinct pairs i<j evaluated by the distance kernel */
+  int64_t edges;                /* distinct neighbour pairs i<j within the largest eps */
+  int32_t distance_passes;      /* 1, or 2 when the edge buffer had to grow */
+  int32_t launches;             /* kernels this library launched during the call */
+  double ms_distance;           /* device time of the distance kernel(s), if timing enabled */
+  double ms_graph;              /* degrees, masks, CSR build */
+  double ms_label;              /* per-batch compaction, connected components, merge */
+  double ms_relabel;            /* final relabel */
+} dbm_stats;
+
+typedef struct dbm_handle dbm_handle;
+
+/* ---- lifecycle ---------------------------------------------------------------------- */
+/* Creates a handle on `device` (a CUDA ordinal).  `stream` may be NULL (the handle creates
+ * its own non-blocking stream).  Returns NULL on failure (message in err). */
+dbm_handle* dbm_create(int device, void* stream, char* err, size_t err_len);
+/* Frees the handle's workspace and stream (if it owns it). */
+void dbm_destroy(dbm_handle* h);
+/* Bytes currently held by the handle's persistent workspace. */
+uint64_t dbm_workspace_bytes(const dbm_handle* h);
+/* Record per-phase device times into dbm_stats.ms_* (adds stream syncs; off by default). */
+void dbm_set_phase_timing(dbm_handle* h, int enabled);
+
+/* ---- the fit ------------------------------------------------------------------------ */
+/*
+ * x_dev:        n x d float32, row-major, device
+ * eps_host:     k values, strictly ascending, finite, > 0, <= sqrt(FLT_MAX); 1 <= k <= 16
+ * min_pts_host: l values, strictly ascending, > 0
+ * labels_dev:   k*l*n int32 out (device), config = e*l + m
+ * core_dev:     optional k*l*n uint8 out (device), 1 = core point; NULL to skip
+ * opt:          NULL = defaults (cuvs backend, auto index, auto route, worst-case
+ *               neighbours, automatic budget)
+ * stats:        optional out
+ * batch_routes: optional out, DBM_BATCH_* per batch (ascending), routes_len entries
+ * Synchronises `stream` before returning (like the reference, which reads per-batch
+ * sizes back to the host).
+ */
+int dbm_fit_multi(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host,
+                  int k, const int32_t* min_pts_host, int l, int32_t* labels_dev, uint8_t* core_dev,
+                  const dbm_options* opt, dbm_stats* stats, uint8_t* batch_routes, int routes_len,
+                  void* stream, char* err, size_t err_len);
+
+/* Same, with host buffers: copies x to the device, fits, copies labels (and optionally core
+ * masks) back and checks -1 <= label < n.  x_host may be pageable or pinned. */
+int dbm_fit_multi_host(dbm_handle* h, const float* x_host, int64_t n, int64_t d,
+                       const float* eps_host, int k, const int32_t* min_pts_host, int l,
+                       int32_t* labels_host, uint8_t* core_host, const dbm_options* opt,
+                       dbm_stats* stats, uint8_t* batch_routes, int routes_len, char* err,
+                       size_t err_len);
+
+/* Per-eps neighbourhood sizes only (the point itself included): deg_dev[e*n + i] = #{j :
+ * dist2(i, j) <= eps_e^2}, int32, device.  This is the degree vector the reference's
+ * VertexDeg::run_multi produces per batch (src/multi/eps_neighborhood.cuh:440-479, vd[e]). */
+int dbm_neighbor_counts(dbm_handle* h, const float* x_dev, int64_t n, int64_t d,
+                        const float* eps_host, int k, int32_t* deg_dev, void* stream, char* err,
+                        size_t err_len);
+
+/* ---- host-side rules (no device work) ---------------------------------------------- */
+/* Batch rows for a budget; returns DBM_OK or DBM_ERR_FIXED_BUFFERS / DBM_ERR_INDEX_OVERFLOW. */
+int dbm_batch_size(int64_t n, int k, int l, uint64_t max_bytes, int backend, int64_t neigh_per_row,
+                   int index_bits, uint64_t* batch_size_out, char* err, size_t err_len);
+/* Inverse of dbm_batch_size: a budget that yields `batch_size` rows. */
+uint64_t dbm_max_bytes_for_batch_size(int64_t n, int k, int l, uint64_t batch_size, int backend,
+                                      int64_t neigh_per_row, int index_bits);
+/* The reference's per-batch route rule: 1 = annotate (sparse), 0 = dense. */
+int dbm_annotate_pays(int64_t nnz, int64_t pairs, int k, int64_t d);
+/* Index width the reference's --index auto would pick for n (32 or 64). */
+int dbm_auto_index_bits(int64_t n);
+
+/* ---- build identity ------------------------------------------------------------------ */
+/* Static JSON object: git_sha, build_id, cuda_arch, configured_backend, compiled_backends. */
+const char* dbm_build_info_json(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DBM_H */
