@@ -46,18 +46,18 @@ Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minp
                       int32_t* deg, int32_t* corecnt, int32_t* rowcnt, uint8_t* core_out,
                       cudaStream_t s);
 Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, int32_t* fill,
-                          uint32_t* col, cudaStream_t s);
+                          uint32_t* col, int32_t* row, cudaStream_t s);
 Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, int64_t* out,
                         cudaStream_t s);
 Status launch_slab_counts(const int32_t* deg_e, int64_t s0, int64_t rows, int32_t* counts,
                           cudaStream_t s);
 Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int e,
-                     const int64_t* off_e, int32_t* col_e, cudaStream_t s);
+                     const int64_t* off_e, int32_t* col_e, int32_t* row_e, cudaStream_t s);
 Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigned long long* best,
                       cudaStream_t s);
 Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, const int32_t* cc_e, bool single_batch,
                        int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur, uint32_t tag,
-                       int32_t* err, cudaStream_t s);
+                       int32_t* err, int sm_count, cudaStream_t s);
 Status launch_cc_roots(int64_t n, int k, int l, const int32_t* cc, int32_t* G, int32_t* flags,
                        cudaStream_t s);
 Status launch_cc_labels(int64_t n, int k, int l, const int32_t* cc, int32_t* G, const int32_t* cur,
@@ -182,17 +182,17 @@ struct dbm_handle {
   int sm_count = 148;
   bool timing = false;
   uint64_t edge_cap_hint = 0;
-  dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, minpts, counters, err;
-  dbm::Buffer slab_counts, slab_off, slab_col, G, L, best, cur, flags, rank, scan_scratch, bnnz;
+  dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
+  dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
   dbm::Buffer xdev, labels_dev, core_dev;  // host-buffer entry point only
   int64_t* pinned = nullptr;               // small D2H staging
   size_t pinned_count = 0;
 
   uint64_t workspace_bytes() const
   {
-    const dbm::Buffer* all[] = {&xt, &hist, &deg, &cc, &rowcnt, &off, &fill, &edges, &col,
+    const dbm::Buffer* all[] = {&xt, &hist, &deg, &cc, &rowcnt, &off, &fill, &edges, &col, &crow,
                                 &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
-                                &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz};
+                                &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz};
     uint64_t s = 0;
     for (auto* b : all) s += b->bytes;
     return s;
@@ -436,9 +436,10 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
     DBM_TRY(exclusive_scan_i32(as<int32_t>(h->rowcnt), as<int64_t>(h->off), n, h->scan_scratch.p,
                                h->scan_scratch.bytes, s));
     DBM_TRY(ensure(h->col, sizeof(uint32_t) * 2 * std::max<uint64_t>(found, 1)));
+    DBM_TRY(ensure(h->crow, sizeof(int32_t) * 2 * std::max<uint64_t>(found, 1)));
     DBM_CUDA(cudaMemsetAsync(h->fill.p, 0, sizeof(int32_t) * n, s));
     DBM_TRY(launch_csr_scatter(as<uint64_t>(h->edges), static_cast<int64_t>(found), as<int64_t>(h->off),
-                               as<int32_t>(h->fill), as<uint32_t>(h->col), s));
+                               as<int32_t>(h->fill), as<uint32_t>(h->col), as<int32_t>(h->crow), s));
   }
 
   // ---- batch plan with the reference's correction rule ----
@@ -529,34 +530,41 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
       DBM_TRY(ensure(h->slab_counts, sizeof(int32_t) * bs));
       DBM_TRY(ensure(h->slab_off, sizeof(int64_t) * (bs + 1)));
       DBM_TRY(ensure(h->slab_col, sizeof(int32_t) * std::max<int64_t>(max_slab, 1)));
+      DBM_TRY(ensure(h->slab_row, sizeof(int32_t) * std::max<int64_t>(max_slab, 1)));
     }
     DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur),
                            as<unsigned long long>(h->best), s));
+    int64_t base = 0;  // first max-eps CSR entry of the batch
     for (int64_t b = 0; b < nb; ++b) {
       const int64_t s0 = b * static_cast<int64_t>(bs);
       const int64_t rows = std::min<int64_t>(n - s0, static_cast<int64_t>(bs));
+      const int64_t count = bnnz[b] - rows;  // entries without the self pairs
       const uint32_t tag = static_cast<uint32_t>(nb - 1 - b);
       for (int e = 0; e < k; ++e) {
         Slab sl;
-        sl.s0 = s0;
-        sl.rows = rows;
         if (e == k - 1) {
-          sl.off = as<int64_t>(h->off) + s0;
-          sl.col = reinterpret_cast<const int32_t*>(h->col.p);
+          sl.row = as<int32_t>(h->crow) + base;
+          sl.col = reinterpret_cast<const int32_t*>(h->col.p) + base;
+          sl.count = count;
+          sl.count_dev = nullptr;
         } else {
           DBM_TRY(launch_slab_counts(as<int32_t>(h->deg) + static_cast<int64_t>(e) * n, s0, rows,
                                      as<int32_t>(h->slab_counts), s));
           DBM_TRY(exclusive_scan_i32(as<int32_t>(h->slab_counts), as<int64_t>(h->slab_off), rows,
                                      h->scan_scratch.p, h->scan_scratch.bytes, s));
           DBM_TRY(launch_filter(as<int64_t>(h->off), as<uint32_t>(h->col), s0, rows, e,
-                                as<int64_t>(h->slab_off), as<int32_t>(h->slab_col), s));
-          sl.off = as<int64_t>(h->slab_off);
+                                as<int64_t>(h->slab_off), as<int32_t>(h->slab_col),
+                                as<int32_t>(h->slab_row), s));
+          sl.row = as<int32_t>(h->slab_row);
           sl.col = as<int32_t>(h->slab_col);
+          sl.count = count;                              // upper bound for the launch size
+          sl.count_dev = as<int64_t>(h->slab_off) + rows;  // exact, read on the device
         }
         DBM_TRY(launch_cc_batch(sl, n, l, e, as<int32_t>(h->cc) + static_cast<int64_t>(e) * n, nb == 1,
                                 as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
-                                as<int32_t>(h->cur), tag, as<int32_t>(h->err), s));
+                                as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, s));
       }
+      base += count;
     }
   }
 
@@ -629,9 +637,10 @@ void dbm_destroy(dbm_handle* h)
   cudaSetDevice(h->device);
   cudaStreamSynchronize(h->stream);
   dbm::Buffer* all[] = {&h->xt, &h->hist, &h->deg, &h->cc, &h->rowcnt, &h->off, &h->fill, &h->edges,
-                        &h->col, &h->minpts, &h->counters, &h->err, &h->slab_counts, &h->slab_off,
-                        &h->slab_col, &h->G, &h->L, &h->best, &h->cur, &h->flags, &h->rank,
-                        &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev, &h->core_dev};
+                        &h->col, &h->crow, &h->minpts, &h->counters, &h->err, &h->slab_counts,
+                        &h->slab_off, &h->slab_col, &h->slab_row, &h->G, &h->L, &h->best, &h->cur,
+                        &h->flags, &h->rank, &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev,
+                        &h->core_dev};
   for (auto* b : all)
     if (b->p) cudaFree(b->p);
   if (h->pinned) cudaFreeHost(h->pinned);

@@ -23,6 +23,8 @@
 // ascending, a point is core for config (e, m) iff m < corecnt[e][i].
 #include "dbm_internal.cuh"
 
+#include <algorithm>
+
 namespace dbm {
 
 
@@ -36,87 +38,83 @@ __global__ void cc_init_kernel(int64_t n, int64_t total, int32_t* __restrict__ G
   best[x] = ~0ull;
 }
 
-// L[cfg][v] = v for both endpoints of every slab edge (configs where v is core).
-__global__ void cc_touch_kernel(Slab sl, int64_t n, int l, int cfg0, const int32_t* __restrict__ cc,
+// Edge-parallel slab iteration: grid-stride over the entries, bounded by the device-side
+// count when the slab was compacted on the device.
+#define DBM_SLAB_LOOP(sl, q)                                                              \
+  const int64_t lim_ = (sl).count_dev ? *(sl).count_dev : (sl).count;                   \
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < lim_; \
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x)
+
+// L[cfg][v] = v for both endpoints of every slab entry (configs where v is core).
+__global__ void cc_touch_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __restrict__ cc,
                                 int32_t* __restrict__ L)
 {
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= sl.rows) return;
-  const int64_t r = sl.s0 + t;
-  const int cr = cc[r];
-  for (int m = 0; m < cr; ++m) L[static_cast<int64_t>(cfg0 + m) * n + r] = static_cast<int32_t>(r);
-  for (int64_t q = sl.off[t]; q < sl.off[t + 1]; ++q) {
+  DBM_SLAB_LOOP(sl, q)
+  {
+    const int32_t r = sl.row[q];
     const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
-    const int cj = cc[j];
+    const int cr = cc[r], cj = cc[j];
+    for (int m = 0; m < cr; ++m) L[static_cast<int64_t>(cfg0 + m) * n + r] = r;
     for (int m = 0; m < cj; ++m) L[static_cast<int64_t>(cfg0 + m) * n + j] = j;
   }
 }
 
-// unite(P[cfg], r, j) for every core-core slab edge
-__global__ void cc_union_kernel(Slab sl, int64_t n, int l, int cfg0, const int32_t* __restrict__ cc,
+// unite(P[cfg], r, j) for every core-core slab entry
+__global__ void cc_union_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __restrict__ cc,
                                 int32_t* __restrict__ P, int32_t* __restrict__ err)
 {
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= sl.rows) return;
-  const int64_t r = sl.s0 + t;
-  const int cr = cc[r];
-  if (cr == 0) return;
   bool ok = true;
-  for (int64_t q = sl.off[t]; q < sl.off[t + 1]; ++q) {
+  DBM_SLAB_LOOP(sl, q)
+  {
+    const int32_t r = sl.row[q];
     const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
-    const int mm = min(cr, cc[j]);
-    for (int m = 0; m < mm; ++m)
-      ok &= uf_unite(P + static_cast<int64_t>(cfg0 + m) * n, static_cast<int32_t>(r), j);
+    const int mm = min(cc[r], cc[j]);
+    for (int m = 0; m < mm; ++m) ok &= uf_unite(P + static_cast<int64_t>(cfg0 + m) * n, r, j);
   }
   if (!ok) atomicOr(err, kErrUnionLimit);
 }
 
-// For every slab edge with exactly one core endpoint c: best[p] = min(tag << 32 | find(P, c)).
-__global__ void cc_best_kernel(Slab sl, int64_t n, int l, int cfg0, const int32_t* __restrict__ cc,
+// For every slab entry with exactly one core endpoint c: best[p] = min(tag << 32 | find(P, c)).
+__global__ void cc_best_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __restrict__ cc,
                                int32_t* __restrict__ P, unsigned long long* __restrict__ best,
                                uint32_t tag)
 {
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= sl.rows) return;
-  const int64_t r = sl.s0 + t;
-  const int cr = cc[r];
-  for (int64_t q = sl.off[t]; q < sl.off[t + 1]; ++q) {
+  DBM_SLAB_LOOP(sl, q)
+  {
+    const int32_t r = sl.row[q];
     const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
-    const int cj = cc[j];
+    const int cr = cc[r], cj = cc[j];
     const int lo = min(cr, cj), hi = max(cr, cj);
     for (int m = lo; m < hi; ++m) {
       const bool r_core = m < cr;
-      const int32_t c = r_core ? static_cast<int32_t>(r) : j;
-      const int64_t p = r_core ? static_cast<int64_t>(j) : r;
+      const int32_t c = r_core ? r : j;
+      const int32_t pt = r_core ? j : r;
       const int64_t base = static_cast<int64_t>(cfg0 + m) * n;
       const int32_t root = uf_find(P + base, c);
-      atomicMin(best + base + p,
+      atomicMin(best + base + pt,
                 (static_cast<unsigned long long>(tag) << 32) | static_cast<uint32_t>(root));
     }
   }
 }
 
 // cur[p] = min(find(G, cur[p]), find(G, best[p])) for every border endpoint of the slab.
-__global__ void cc_border_kernel(Slab sl, int64_t n, int l, int cfg0, const int32_t* __restrict__ cc,
+__global__ void cc_border_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __restrict__ cc,
                                  int32_t* __restrict__ G, const unsigned long long* __restrict__ best,
                                  int32_t* __restrict__ cur, uint32_t tag)
 {
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= sl.rows) return;
-  const int64_t r = sl.s0 + t;
-  const int cr = cc[r];
-  for (int64_t q = sl.off[t]; q < sl.off[t + 1]; ++q) {
+  DBM_SLAB_LOOP(sl, q)
+  {
+    const int32_t r = sl.row[q];
     const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
-    const int cj = cc[j];
+    const int cr = cc[r], cj = cc[j];
     const int lo = min(cr, cj), hi = max(cr, cj);
     for (int m = lo; m < hi; ++m) {
-      const bool r_core = m < cr;
-      const int64_t p = r_core ? static_cast<int64_t>(j) : r;
+      const int32_t pt = (m < cr) ? j : r;
       const int64_t base = static_cast<int64_t>(cfg0 + m) * n;
-      const unsigned long long v = best[base + p];
+      const unsigned long long v = best[base + pt];
       if (static_cast<uint32_t>(v >> 32) != tag) continue;
       const int32_t cand = uf_find(G + base, static_cast<int32_t>(v & 0xffffffffu));
-      volatile int32_t* cp = cur + base + p;
+      volatile int32_t* cp = cur + base + pt;
       const int32_t old = *cp;
       const int32_t prev = (old == kNone) ? kNone : uf_find(G + base, old);
       *cp = prev < cand ? prev : cand;
@@ -189,28 +187,25 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 // candidates, global union, border fold.
 Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, const int32_t* cc_e, bool single_batch,
                        int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur, uint32_t tag,
-                       int32_t* err, cudaStream_t s)
+                       int32_t* err, int sm_count, cudaStream_t s)
 {
-  if (sl.rows <= 0) return Status::Ok();
+  if (sl.count <= 0) return Status::Ok();
   const int cfg0 = e * l;
-  const unsigned nb = blocks_for(sl.rows, 128);
+  const int64_t want = ceil_div(sl.count, 256);
+  const unsigned nb = static_cast<unsigned>(std::min<int64_t>(want, static_cast<int64_t>(sm_count) * 16));
   if (single_batch) {
-    count_launch();
-    cc_union_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, G, err);
-    count_launch();
-    cc_best_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, G, best, tag);
+    count_launch(2);
+    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, G, err);
+    cc_best_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, G, best, tag);
   } else {
-    count_launch();
-    cc_touch_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, L);
-    count_launch();
-    cc_union_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, L, err);
-    count_launch();
-    cc_best_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, L, best, tag);
-    count_launch();
-    cc_union_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, G, err);
+    count_launch(4);
+    cc_touch_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, L);
+    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, L, err);
+    cc_best_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, L, best, tag);
+    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, G, err);
   }
   count_launch();
-  cc_border_kernel<<<nb, 128, 0, s>>>(sl, n, l, cfg0, cc_e, G, best, cur, tag);
+  cc_border_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, G, best, cur, tag);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }

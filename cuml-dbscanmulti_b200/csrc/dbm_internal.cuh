@@ -141,12 +141,14 @@ __device__ __forceinline__ bool uf_unite(int32_t* parent, int32_t a, int32_t b)
 }
 
 // ---- launch descriptors shared by the orchestrator and the kernels ------------------------
-// One CSR slab: the rows [s0, s0 + rows) of a batch, entries col[off[t] .. off[t+1]) for row
-// s0 + t; only the low 28 bits of a column word are the neighbour id.
+// One slab of neighbour entries (the rows of one batch at one eps), processed edge-parallel:
+// entry q links row[q] and col[q] (low 28 bits significant).  `count` bounds q on the host
+// side; when `count_dev` is set the exact count is read on the device (no host sync).
 struct Slab {
-  const int64_t* off;
+  const int32_t* row;
   const int32_t* col;
-  int64_t s0, rows;
+  int64_t count;
+  const int64_t* count_dev;
 };
 
 struct DistLaunch {

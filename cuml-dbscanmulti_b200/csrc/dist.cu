@@ -33,18 +33,21 @@ constexpr int kDistThreads = 256;
 constexpr int kDimBox = 64;          // dims per TMA box
 constexpr uint32_t kWaitPolls = 1u << 24;
 
+
 struct DistParams {
   int64_t n;
   int32_t d;
   int32_t k;
   int32_t dbox;                      // dims per box actually used (<= kDimBox)
-  int32_t pad_;
+  int32_t nchunks;                   // ceil(d / dbox)
   int64_t tile_pairs;                // T(T+1)/2
   unsigned long long* counters;      // [0] edge cursor, [1] next tile pair
   uint64_t* edges;
   uint64_t edge_cap;
   int32_t* hist;                     // k x n
   int32_t* err;
+  const float* xt;                   // dp x npad (for re-evaluating neighbour pairs)
+  int64_t npad;
   float eps2[kMaxEps];
 };
 
@@ -58,127 +61,216 @@ __device__ __forceinline__ void tri_coords(long long c, long long& I, long long&
   I = c - j * (j + 1) / 2;
 }
 
+// ---- packed fp32 pairs (sm_100: .f32x2, each lane rounded exactly like the scalar op) ----------
+__device__ __forceinline__ uint64_t pack2(float lo, float hi)
+{
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi)
+{
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b)
+{
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sqacc2(uint64_t diff, uint64_t acc)
+{
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %1, %2;" : "=l"(d) : "l"(diff), "l"(acc));
+  return d;
+}
+
+// Shared-memory plan per CTA: two stages of {A tile, B tile}, each [dbox][128] floats.
+__host__ __device__ constexpr size_t dist_smem_bytes(int dbox)
+{
+  return static_cast<size_t>(dbox) * kTile * sizeof(float) * 4;
+}
+
 __global__ void __launch_bounds__(kDistThreads, 2)
 dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
 {
   extern __shared__ __align__(128) unsigned char dyn_smem[];
-  float* As = reinterpret_cast<float*>(dyn_smem);      // [dbox][128]
-  float* Bs = As + static_cast<size_t>(p.dbox) * kTile;  // [dbox][128]
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ long long s_tile;
+  const int box_floats = p.dbox * kTile;
+  float* As0 = reinterpret_cast<float*>(dyn_smem);
+  float* Bs0 = As0 + box_floats;
+  float* As1 = Bs0 + box_floats;
+  float* Bs1 = As1 + box_floats;
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ long long s_tile[2];  // tile pair index held by each stage (>= tile_pairs: none)
   __shared__ float s_eps2[kMaxEps];
 
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
+  const int lane = tid & 31;
   if (tid < kMaxEps) s_eps2[tid] = p.eps2[tid];
+  const uint32_t box_bytes = static_cast<uint32_t>(box_floats) * sizeof(float);
+
+  auto issue = [&](int stage, long long tile, int chunk) {
+    // one thread: record the item and start both tile loads of this stage
+    s_tile[stage] = tile;
+    if (tile >= p.tile_pairs) return;
+    long long I, J;
+    tri_coords(tile, I, J);
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(&full[stage], 2 * box_bytes);
+    float* a = stage ? As1 : As0;
+    float* b = stage ? Bs1 : Bs0;
+    tma_load_2d(a, &xt_map, static_cast<int32_t>(I * kTile), chunk * p.dbox, &full[stage]);
+    tma_load_2d(b, &xt_map, static_cast<int32_t>(J * kTile), chunk * p.dbox, &full[stage]);
+  };
+
   if (tid == 0) {
-    mbar_init(&bar, 1);
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
     mbar_fence_init();
+    issue(0, static_cast<long long>(atomicAdd(p.counters + 1, 1ULL)), 0);
   }
   __syncthreads();
 
   const int64_t n = p.n;
   const float cutoff = p.eps2[p.k - 1];
-  const uint32_t box_bytes = static_cast<uint32_t>(p.dbox) * kTile * sizeof(float);
-  uint32_t phase = 0;
-  const int lane = tid & 31;
+  uint32_t phase[2] = {0u, 0u};
+  int stage = 0, chunk = 0;
+  uint64_t acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
 
   for (;;) {
-    if (tid == 0) s_tile = static_cast<long long>(atomicAdd(p.counters + 1, 1ULL));
-    __syncthreads();
-    const long long c = s_tile;
+    const long long c = s_tile[stage];
     if (c >= p.tile_pairs) break;
-    long long I, J;
-    tri_coords(c, I, J);
-    const int64_t row0 = I * kTile, col0 = J * kTile;
-
-    float acc[8][8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
-
-    for (int d0 = 0; d0 < p.d; d0 += p.dbox) {
-      if (tid == 0) {
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&bar, 2 * box_bytes);
-        tma_load_2d(As, &xt_map, static_cast<int32_t>(row0), d0, &bar);
-        tma_load_2d(Bs, &xt_map, static_cast<int32_t>(col0), d0, &bar);
-      }
-      const bool ok = mbar_wait_bounded(&bar, phase, kWaitPolls);
-      if (__syncthreads_or(!ok)) {
-        if (tid == 0) atomicOr(p.err, kErrTmaTimeout);
-        mbar_wait_bounded(&bar, phase, kWaitPolls);  // let the copy in flight land
-        return;
-      }
-      phase ^= 1u;
-      const int dk = min(p.dbox, p.d - d0);
+    const bool ok = mbar_wait_bounded(&full[stage], phase[stage], kWaitPolls);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) atomicOr(p.err, kErrTmaTimeout);
+      mbar_wait_bounded(&full[stage], phase[stage], kWaitPolls);
+      mbar_wait_bounded(&full[stage ^ 1], phase[stage ^ 1], kWaitPolls);
+      return;
+    }
+    phase[stage] ^= 1u;
+    const bool last_chunk = (chunk + 1 == p.nchunks);
+    if (tid == 0) {
+      // prefetch the next item into the other stage (released by the previous iteration)
+      if (!last_chunk)
+        issue(stage ^ 1, c, chunk + 1);
+      else
+        issue(stage ^ 1, static_cast<long long>(atomicAdd(p.counters + 1, 1ULL)), 0);
+    }
+    const float* As = stage ? As1 : As0;
+    const float* Bs = stage ? Bs1 : Bs0;
+    const int dk = min(p.dbox, p.d - chunk * p.dbox);
 #pragma unroll 2
-      for (int t = 0; t < dk; ++t) {
-        const float* arow = As + t * kTile;
-        const float* brow = Bs + t * kTile;
-        const float4 a0 = *reinterpret_cast<const float4*>(arow + ty * 4);
-        const float4 a1 = *reinterpret_cast<const float4*>(arow + 64 + ty * 4);
-        const float4 b0 = *reinterpret_cast<const float4*>(brow + tx * 4);
-        const float4 b1 = *reinterpret_cast<const float4*>(brow + 64 + tx * 4);
-        const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    for (int t = 0; t < dk; ++t) {
+      uint64_t a[8];
+      // (a, a) operand pairs for the 8 rows; (b, b') pairs come straight from 16-byte loads
+      const float4 f0 = *reinterpret_cast<const float4*>(As + t * kTile + ty * 4);
+      const float4 f1 = *reinterpret_cast<const float4*>(As + t * kTile + 64 + ty * 4);
+      a[0] = pack2(f0.x, f0.x); a[1] = pack2(f0.y, f0.y); a[2] = pack2(f0.z, f0.z); a[3] = pack2(f0.w, f0.w);
+      a[4] = pack2(f1.x, f1.x); a[5] = pack2(f1.y, f1.y); a[6] = pack2(f1.z, f1.z); a[7] = pack2(f1.w, f1.w);
+      const ulonglong2 b01 = *reinterpret_cast<const ulonglong2*>(Bs + t * kTile + tx * 4);
+      const ulonglong2 b23 = *reinterpret_cast<const ulonglong2*>(Bs + t * kTile + 64 + tx * 4);
+      const uint64_t b[4] = {b01.x, b01.y, b23.x, b23.y};
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float diff = __fsub_rn(a[i], b[j]);
-            acc[i][j] = __fmaf_rn(diff, diff, acc[i][j]);
-          }
-      }
-      __syncthreads();  // all reads of this chunk done before the next TMA overwrites it
+        for (int j = 0; j < 4; ++j) acc[i][j] = sqacc2(sub2(a[i], b[j]), acc[i][j]);
     }
 
-    // ---- epilogue: neighbour pairs (i < j) within the largest eps --------------------
-    const bool diag = (I == J);
-    uint64_t nb = 0;
+    if (last_chunk) {
+      // ---- epilogue: neighbour pairs (i < j) within the largest eps -------------------
+      // Fast path: nothing to do unless some pair of the warp is within the cutoff.
+      float mn = INFINITY;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int64_t gi = row0 + ((i < 4) ? (ty * 4 + i) : (64 + ty * 4 + i - 4));
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int64_t gj = col0 + ((j < 4) ? (tx * 4 + j) : (64 + tx * 4 + j - 4));
-        const bool v = (gi < n) && (gj < n) && (!diag || gj > gi) && (acc[i][j] <= cutoff);
-        nb |= static_cast<uint64_t>(v) << (i * 8 + j);
-      }
-    }
-    const int cnt = __popcll(nb);
-    if (__any_sync(0xffffffffu, cnt != 0)) {
-      int incl = cnt;
+        for (int j = 0; j < 4; ++j) {
+          float lo, hi;
+          unpack2(acc[i][j], lo, hi);
+          mn = fminf(mn, fminf(lo, hi));
+        }
+      if (__any_sync(0xffffffffu, mn <= cutoff)) {
+        long long I, J;
+        tri_coords(c, I, J);
+        const int32_t row0 = static_cast<int32_t>(I) * kTile, col0 = static_cast<int32_t>(J) * kTile;
+        const int32_t n32 = static_cast<int32_t>(n);
+        const bool diag = (I == J);
+        uint64_t nb = 0;
 #pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += v;
-      }
-      const int total = __shfl_sync(0xffffffffu, incl, 31);
-      unsigned long long base = 0;
-      if (lane == 31) base = atomicAdd(p.counters, static_cast<unsigned long long>(total));
-      base = __shfl_sync(0xffffffffu, base, 31);
-      unsigned long long idx = base + static_cast<unsigned long long>(incl - cnt);
+        for (int i = 0; i < 8; ++i) {
+          const int32_t gi = row0 + ((i < 4) ? (ty * 4 + i) : (64 + ty * 4 + i - 4));
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+          for (int jp = 0; jp < 4; ++jp) {
+            float w[2];
+            unpack2(acc[i][jp], w[0], w[1]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (!((nb >> (i * 8 + j)) & 1ull)) continue;
-          const int64_t gi = row0 + ((i < 4) ? (ty * 4 + i) : (64 + ty * 4 + i - 4));
-          const int64_t gj = col0 + ((j < 4) ? (tx * 4 + j) : (64 + tx * 4 + j - 4));
-          const float v = acc[i][j];
+            for (int h = 0; h < 2; ++h) {
+              const int j = 2 * jp + h;
+              const int32_t gj = col0 + ((j < 4) ? (tx * 4 + j) : (64 + tx * 4 + j - 4));
+              const bool hit = (gi < n32) && (gj < n32) && (!diag || gj > gi) && (w[h] <= cutoff);
+              nb |= static_cast<uint64_t>(hit) << (i * 8 + j);
+            }
+          }
+        }
+        const int cnt = __popcll(nb);
+        int incl = cnt;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int u = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += u;
+        }
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        unsigned long long base = 0;
+        if (lane == 31 && total > 0) base = atomicAdd(p.counters, static_cast<unsigned long long>(total));
+        base = __shfl_sync(0xffffffffu, base, 31);
+        unsigned long long idx = base + static_cast<unsigned long long>(incl - cnt);
+        // Each (rare) neighbour pair is re-evaluated with the same sequential FMA chain -- from
+        // the tile still in shared memory when all dims fit one chunk, else from XT -- which is
+        // bit-identical to the packed lanes and keeps the register budget for the main loop.
+        while (nb) {
+          const int bit = __ffsll(static_cast<long long>(nb)) - 1;
+          nb &= nb - 1;
+          const int i = bit >> 3, j = bit & 7;
+          const int lr = (i < 4) ? (ty * 4 + i) : (64 + ty * 4 + i - 4);
+          const int lc = (j < 4) ? (tx * 4 + j) : (64 + tx * 4 + j - 4);
+          const int32_t gi = row0 + lr, gj = col0 + lc;
+          float w = 0.0f;
+          if (p.nchunks == 1) {
+            for (int t = 0; t < p.d; ++t) {
+              const float diff = __fsub_rn(As[t * kTile + lr], Bs[t * kTile + lc]);
+              w = __fmaf_rn(diff, diff, w);
+            }
+          } else {
+            const float* xt = p.xt;
+            for (int t = 0; t < p.d; ++t) {
+              const float* col = xt + static_cast<int64_t>(t) * p.npad;
+              const float diff = __fsub_rn(col[gi], col[gj]);
+              w = __fmaf_rn(diff, diff, w);
+            }
+          }
           int code = 0;
-          while (v > s_eps2[code]) ++code;  // terminates: v <= eps2[k-1]
+          while (w > s_eps2[code]) ++code;  // terminates: w <= eps2[k-1]
           if (idx < p.edge_cap)
             p.edges[idx] = (static_cast<uint64_t>(gi) << 32) |
                            (static_cast<uint64_t>(code) << kCodeShift) | static_cast<uint64_t>(gj);
           ++idx;
-          atomicAdd(p.hist + static_cast<int64_t>(code) * n + gi, 1);
-          atomicAdd(p.hist + static_cast<int64_t>(code) * n + gj, 1);
+          int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
+          atomicAdd(hrow + gi, 1);
+          atomicAdd(hrow + gj, 1);
         }
       }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
     }
+    __syncthreads();  // this stage's buffers are free; the next item's descriptor is visible
+    stage ^= 1;
+    chunk = last_chunk ? 0 : chunk + 1;
   }
 }
 
@@ -263,6 +355,7 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   p.d = a.d;
   p.k = a.k;
   p.dbox = dbox;
+  p.nchunks = static_cast<int32_t>(ceil_div(a.d, dbox));
   const int64_t T = ceil_div(a.n, kTile);
   p.tile_pairs = T * (T + 1) / 2;
   p.counters = a.counters;
@@ -270,9 +363,11 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   p.edge_cap = a.edge_cap;
   p.hist = a.hist;
   p.err = a.err;
+  p.xt = a.xt;
+  p.npad = npad;
   for (int e = 0; e < kMaxEps; ++e) p.eps2[e] = e < a.k ? a.eps2[e] : a.eps2[a.k - 1];
 
-  const size_t smem = 2ull * dbox * kTile * sizeof(float);
+  const size_t smem = dist_smem_bytes(dbox);
   DBM_CUDA(cudaFuncSetAttribute(dist_tri_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(smem)));
   int per_sm = 0;

@@ -176,7 +176,7 @@ Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minp
 // ---- max-eps CSR from the neighbour pairs ---------------------------------------------------
 __global__ void csr_scatter_kernel(const uint64_t* __restrict__ edges, int64_t m,
                                    const int64_t* __restrict__ off, int32_t* __restrict__ fill,
-                                   uint32_t* __restrict__ col)
+                                   uint32_t* __restrict__ col, int32_t* __restrict__ row)
 {
   const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (q >= m) return;
@@ -185,18 +185,20 @@ __global__ void csr_scatter_kernel(const uint64_t* __restrict__ edges, int64_t m
   const uint32_t lo = static_cast<uint32_t>(w);
   const uint32_t j = lo & kColMask;
   const uint32_t code = lo & ~kColMask;
-  const int32_t pi = atomicAdd(fill + i, 1);
-  col[off[i] + pi] = code | j;
-  const int32_t pj = atomicAdd(fill + j, 1);
-  col[off[j] + pj] = code | i;
+  const int64_t qi = off[i] + atomicAdd(fill + i, 1);
+  col[qi] = code | j;
+  row[qi] = static_cast<int32_t>(i);
+  const int64_t qj = off[j] + atomicAdd(fill + j, 1);
+  col[qj] = code | i;
+  row[qj] = static_cast<int32_t>(j);
 }
 
 Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, int32_t* fill,
-                          uint32_t* col, cudaStream_t s)
+                          uint32_t* col, int32_t* row, cudaStream_t s)
 {
   if (m <= 0) return Status::Ok();
   count_launch();
-  csr_scatter_kernel<<<static_cast<unsigned>(ceil_div(m, 256)), 256, 0, s>>>(edges, m, off, fill, col);
+  csr_scatter_kernel<<<static_cast<unsigned>(ceil_div(m, 256)), 256, 0, s>>>(edges, m, off, fill, col, row);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
@@ -233,7 +235,8 @@ __global__ void slab_counts_kernel(const int32_t* __restrict__ deg_e, int64_t s0
 // One warp per row: ballot over the row's entries keeps those with code <= e, in order.
 __global__ void filter_kernel(const int64_t* __restrict__ off, const uint32_t* __restrict__ col,
                               int64_t s0, int64_t rows, uint32_t e,
-                              const int64_t* __restrict__ off_e, int32_t* __restrict__ col_e)
+                              const int64_t* __restrict__ off_e, int32_t* __restrict__ col_e,
+                              int32_t* __restrict__ row_e)
 {
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -250,7 +253,11 @@ __global__ void filter_kernel(const int64_t* __restrict__ off, const uint32_t* _
       keep = (w >> kCodeShift) <= e;
     }
     const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-    if (keep) col_e[out + __popc(bal & ((1u << lane) - 1u))] = static_cast<int32_t>(w & kColMask);
+    if (keep) {
+      const int64_t dst = out + __popc(bal & ((1u << lane) - 1u));
+      col_e[dst] = static_cast<int32_t>(w & kColMask);
+      row_e[dst] = static_cast<int32_t>(r);
+    }
     out += __popc(bal);
   }
 }
@@ -265,12 +272,12 @@ Status launch_slab_counts(const int32_t* deg_e, int64_t s0, int64_t rows, int32_
 }
 
 Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int e,
-                     const int64_t* off_e, int32_t* col_e, cudaStream_t s)
+                     const int64_t* off_e, int32_t* col_e, int32_t* row_e, cudaStream_t s)
 {
   const int64_t threads = rows * 32;
   count_launch();
   filter_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(
-    off, col, s0, rows, static_cast<uint32_t>(e), off_e, col_e);
+    off, col, s0, rows, static_cast<uint32_t>(e), off_e, col_e, row_e);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
