@@ -55,6 +55,7 @@ EXPORTED = (
     "dbm_create", "dbm_destroy", "dbm_workspace_bytes", "dbm_set_phase_timing",
     "dbm_fit_multi", "dbm_fit_multi_host", "dbm_neighbor_counts", "dbm_batch_size", "dbm_max_bytes_for_batch_size",
     "dbm_annotate_pays", "dbm_auto_index_bits", "dbm_build_info_json",
+    "dbm_neighbor_counts_noalloc",
 )
 
 

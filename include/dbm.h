@@ -150,6 +150,21 @@ int dbm_neighbor_counts(dbm_handle* h, const float* x_dev, int64_t n, int64_t d,
                         const float* eps_host, int k, int32_t* deg_dev, void* stream, char* err,
                         size_t err_len);
 
+/* Allocation-free per-eps neighbourhood sizes.  No counterpart in the reference: it exists for
+ * callers that cannot call cudaMalloc -- code running while a stream is captured into a CUDA
+ * graph, code under an allocator that owns all device memory, latency-critical code that
+ * cannot take cudaMalloc's device-wide synchronisation.  Same output as dbm_neighbor_counts
+ * (deg_dev[e*n + i], int32, device), but every byte of scratch comes from one file-scope device
+ * array of 32 MiB (the padded dim-major copy of the points, 4*Dp*Npad bytes with Dp = d rounded
+ * up to 4 and Npad = n rounded up to 4, plus 4*k*n bytes of counts and 768 bytes of counters);
+ * larger inputs are rejected with DBM_ERR_TOO_LARGE.  The array is resident on every GPU that
+ * uses the library until the process exits.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current: make it before any stream
+ * capture.  Calls share the array, so calls that overlap on the GPU race; each call clears the
+ * parts that must start at zero.  No handle is needed; stream NULL = the legacy default stream. */
+int dbm_neighbor_counts_noalloc(const float* x_dev, int64_t n, int64_t d, const float* eps_host,
+                                int k, int32_t* deg_dev, void* stream, char* err, size_t err_len);
+
 /* ---- host-side rules (no device work) ---------------------------------------------- */
 /* Batch rows for a budget; returns DBM_OK or DBM_ERR_FIXED_BUFFERS / DBM_ERR_INDEX_OVERFLOW. */
 int dbm_batch_size(int64_t n, int k, int l, uint64_t max_bytes, int backend, int64_t neigh_per_row,
