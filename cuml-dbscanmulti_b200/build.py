@@ -33,13 +33,27 @@ def _nvcc() -> str:
     return cand
 
 
+def _source_hash() -> str:
+    """SHA-256 over the sources (used when no git revision is available)."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for f in sorted(CSRC.rglob("*")) + [ROOT / "include" / "dbm.h"]:
+        if f.is_file() and f.suffix in {".cu", ".cuh", ".cpp", ".h"}:
+            h.update(f.relative_to(ROOT).as_posix().encode())
+            h.update(f.read_bytes())
+    return h.hexdigest()
+
+
 def _git_sha() -> str:
     try:
         out = subprocess.run(["git", "-C", str(ROOT), "rev-parse", "HEAD"], capture_output=True,
                              text=True, check=True).stdout.strip()
-        return out if out else "unknown"
+        if out:
+            return out
     except Exception:
-        return "unknown"
+        pass
+    return _source_hash()
 
 
 def _sources() -> list[Path]:
@@ -76,8 +90,8 @@ def build_cli(force: bool = False) -> Path:
     if not force and not _stale(CLI, deps):
         return CLI
     CLI.parent.mkdir(parents=True, exist_ok=True)
-    cmd = ["g++", "-O2", "-std=c++17", "-o", str(CLI), str(src), f"-I{ROOT / 'include'}",
-           f"-L{LIB.parent}", "-ldbm", f"-Wl,-rpath,$ORIGIN/../dbscan_multi"]
+    cmd = [_nvcc(), *ARCH_FLAGS, "-O2", "-std=c++17", "-o", str(CLI), str(src), f"-I{ROOT / 'include'}",
+           f"-L{LIB.parent}", "-ldbm", "-Xlinker", "-rpath,$ORIGIN/../dbscan_multi"]
     subprocess.run(cmd, check=True)
     return CLI
 
