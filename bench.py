@@ -17,8 +17,11 @@ reference's unit; each distance evaluated here covers two ordered pairs).  `valu
 device-resident input with CUDA events; `e2e` times the host-buffer C-ABI entry point with
 the point copy in and the label copy out inside the timed region.
 
-Multi-GPU (torchrun, one process per GPU): each rank runs its own full replica of the
-workload ("replicas only" until the sharded path lands); value = all ranks' pairs / max time.
+Multi-GPU (torchrun, one process per GPU): the same grid, sharded -- each rank evaluates an
+equal share of the distance tile pairs, histograms are all-reduced and neighbour pairs
+all-gathered over NCCL, each rank labels a range of the k*l configurations and the labels are
+all-gathered (dbscan_multi.parallel).  value = N^2 pairs per grid / max-over-ranks grid time
+(fixed total work: strong scaling).
 """
 
 from __future__ import annotations
@@ -217,6 +220,29 @@ def e2e_leg(h, pts, eps, ms, kw, labels, flush, steps, ws, dev, torch, dist, pai
     return pairs * ws * steps / e2e_s, e2e_s
 
 
+def e2e_leg_sharded(one_fit, x, pts, labels, flush, steps, rank, dev, torch, dist, pairs, ws):
+    """Sharded e2e: every rank copies the pinned points in, the sharded fit runs, rank 0 copies
+    the gathered labels out; wall clock per step, max over ranks."""
+    xp = torch.from_numpy(pts).pin_memory()
+    lab_host = torch.empty(tuple(labels.shape), dtype=torch.int32).pin_memory()
+    ts = []
+    for _ in range(steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0 = time.perf_counter()
+        x.copy_(xp, non_blocking=True)
+        one_fit()
+        if rank == 0:
+            lab_host.copy_(labels, non_blocking=True)
+        torch.cuda.synchronize()
+        ts.append(time.perf_counter() - t0)
+    t = torch.tensor([float(np.sum(ts))], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_s = float(t.item())
+    return pairs * steps / e2e_s, e2e_s
+
+
 def run_reference(args, cfg) -> None:
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -293,8 +319,38 @@ def main() -> None:
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)  # > 126 MB L2
 
     h.set_phase_timing(True)
+    if ws > 1:
+        from dbscan_multi import parallel
+
+        stages = parallel.DeviceStages(h)
+        if "max_bytes_per_batch" not in kw:
+            kw["max_bytes_per_batch"] = stages.default_budget()
+        dist_ms_box = []
+        orig_shard = stages.distance_shard
+
+        def timed_shard(*a, **k2):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            out = orig_shard(*a, **k2)
+            e1.record(stream)
+            e1.synchronize()
+            dist_ms_box.append(e0.elapsed_time(e1))
+            return out
+
+        stages.distance_shard = timed_shard
+
+        def one_fit():
+            r = parallel.sharded_fit_multi(stages, x, eps, ms, **kw)
+            labels.copy_(r.labels)
+            r.stats["ms_distance"] = dist_ms_box[-1]
+            r.stats["launches"] = r.stats.get("launches", 0)
+            return r
+    else:
+        def one_fit():
+            return h.fit_multi(x, eps, ms, labels_out=labels, **kw)
     for _ in range(args.warmup):
-        h.fit_multi(x, eps, ms, labels_out=labels, **kw)
+        one_fit()
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
@@ -310,7 +366,7 @@ def main() -> None:
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        r = h.fit_multi(x, eps, ms, labels_out=labels, **kw)
+        r = one_fit()
         e1.record(stream)
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
@@ -327,17 +383,20 @@ def main() -> None:
         total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
     pairs = float(n) * float(n)
-    value = pairs * ws * args.steps / (total_ms * 1e-3)
+    value = pairs * (1 if ws > 1 else ws) * args.steps / (total_ms * 1e-3)
 
     # e2e through the host-buffer entry point: pinned points in, labels out, every step
     h.set_phase_timing(False)
     if args.no_e2e:
         e2e_value, e2e_s = None, None
+    elif ws > 1:
+        e2e_value, e2e_s = e2e_leg_sharded(one_fit, x, pts, labels, flush, args.steps, rank, dev, torch, dist,
+                                           pairs, ws)
     else:
         e2e_value, e2e_s = e2e_leg(h, pts, eps, ms, kw, labels, flush, args.steps, ws, dev, torch, dist,
                                    pairs)
-    # roofline of the dominant kernel (the distance pass): FP32 pipes
-    unique_pairs = n * (n - 1) / 2
+    # roofline of the dominant kernel (the distance pass): FP32 pipes (this rank's share)
+    unique_pairs = n * (n - 1) / 2 / ws
     flops = unique_pairs * 3.0 * d  # D FSUB + D FFMA (FMA = 2 flops)
     dms = float(np.mean(dist_ms)) if dist_ms else float("nan")
     achieved = flops / (dms * 1e-3) / 1e12
@@ -368,16 +427,16 @@ def main() -> None:
             "ms_per_step": ms_per_step,
             "grid_wall_s": ms_per_step / 1e3,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": "f32",
             "data": "synthetic (seeded numpy generator with the published configuration's shapes)",
             "config": {"workload": args.config, "desc": cfg["desc"], "n": n, "d": d, "eps": eps,
                        "min_samples": ms, "max_bytes_per_batch": cfg["budget"] or 0,
                        "neigh_per_row": cfg["npr"], "batches": stats["batches"],
-                       "batch_size": stats["batch_size"], "parallelism": f"replicas{ws}" if ws > 1 else "1gpu",
+                       "batch_size": stats["batch_size"], "parallelism": f"tile-pair shards x{ws} (NCCL)" if ws > 1 else "1gpu",
                        "l2": "flushed (256 MB write) between timed steps"},
-            "gpu_launches": int(stats["launches"]) * args.steps,
+            "gpu_launches": (int(stats.get("launches", 0)) + (2 if ws > 1 else 0)) * args.steps,
             "clocks": clk,
             "roofline": {"bound": "fp32", "kernel": "dist_tri_kernel", "achieved": achieved,
                          "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,

@@ -55,13 +55,13 @@ Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_
                      const int64_t* off_e, int32_t* col_e, int32_t* row_e, cudaStream_t s);
 Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigned long long* best,
                       cudaStream_t s);
-Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, const int32_t* cc_e, bool single_batch,
-                       int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur, uint32_t tag,
-                       int32_t* err, int sm_count, cudaStream_t s);
-Status launch_cc_roots(int64_t n, int k, int l, const int32_t* cc, int32_t* G, int32_t* flags,
-                       cudaStream_t s);
-Status launch_cc_labels(int64_t n, int k, int l, const int32_t* cc, int32_t* G, const int32_t* cur,
-                        const int64_t* rank, int32_t* labels, cudaStream_t s);
+Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, int m_lo, int m_hi, const int32_t* cc_e,
+                       bool single_batch, int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur,
+                       uint32_t tag, int32_t* err, int sm_count, cudaStream_t s);
+Status launch_cc_roots(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
+                       int32_t* flags, cudaStream_t s);
+Status launch_cc_labels(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
+                        const int32_t* cur, const int64_t* rank, int32_t* labels, cudaStream_t s);
 
 // ---- batch-size rules (runner_multi.cuh:79-119, 214-268, 437-499) --------------------------
 struct Plan {
@@ -315,7 +315,7 @@ static Status neighbor_counts(dbm_handle* h, const float* x, int64_t n, int64_t 
   DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 4 * sizeof(unsigned long long), s));
   DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s));
   DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
-               as<uint64_t>(h->edges), 0, as<int32_t>(h->hist), as<int32_t>(h->err), h->sm_count};
+               as<uint64_t>(h->edges), 0, as<int32_t>(h->hist), as<int32_t>(h->err), h->sm_count, 0, 1};
   DBM_TRY(launch_distance(a, s));
   DBM_TRY(launch_degrees(as<int32_t>(h->hist), n, k, as<int32_t>(h->minpts), 1, deg_out,
                          as<int32_t>(h->cc), as<int32_t>(h->rowcnt), nullptr, s));
@@ -329,16 +329,18 @@ static Status neighbor_counts(dbm_handle* h, const float* x, int64_t n, int64_t 
   return Status::Ok();
 }
 
-static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps, int k,
-                  const int32_t* minpts, int l, int32_t* labels, uint8_t* core_out,
-                  const dbm_options& opt, dbm_stats& st, std::vector<uint8_t>& routes, cudaStream_t s)
+static void square_eps(const float* eps, int k, float* eps2)
 {
-  DBM_TRY(validate(n, d, eps, k, minpts, l));
-  if (!x || !labels) return Status::Err(DBM_ERR_INVALID, "x and labels must be device pointers");
-  DBM_CUDA(cudaSetDevice(h->device));
+  for (int e = 0; e < k; ++e) {
+    volatile float v = eps[e] * eps[e];  // float product, as the reference's host does
+    eps2[e] = v;
+  }
+}
 
-  // ---- plan: budget and first batch size ----
-  Plan plan;
+// Budget, index width and the first batch-size check (runner_multi.cuh:1315-1337, 458-499).
+static Status plan_budget(dbm_handle* h, int64_t n, int k, int l, const dbm_options& opt, dbm_stats& st,
+                          Plan& plan)
+{
   plan.use_cuvs = opt.backend != DBM_BACKEND_CODES;
   plan.index_bits = opt.index_bits == 64 ? 64
                     : opt.index_bits == 32 ? 32
@@ -355,91 +357,88 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
   }
   st.max_bytes_per_batch = plan.budget;
   st.index_bits = plan.index_bits;
-  {
-    uint64_t bs0 = 0;
-    DBM_TRY(batch_size_rule(n, k, l, plan.budget, plan.use_cuvs, opt.neigh_per_row, plan.index_bits, &bs0));
-  }
+  uint64_t bs0 = 0;
+  return batch_size_rule(n, k, l, plan.budget, plan.use_cuvs, opt.neigh_per_row, plan.index_bits, &bs0);
+}
 
-  float eps2[kMaxEps];
-  for (int e = 0; e < k; ++e) {
-    volatile float v = eps[e] * eps[e];  // float product, as the reference's host does
-    eps2[e] = v;
-  }
-
+// Distance pass over one shard of the tile pairs into hist (zeroed here) and h->edges.
+static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps2, int k,
+                             int shard, int nshards, int32_t* hist, uint64_t cap_hint, uint64_t* found_out,
+                             dbm_stats& st, cudaStream_t s)
+{
   const int32_t di = static_cast<int32_t>(d);
-  const int32_t dp = padded_dims(di);
-  const int64_t npad = padded_points(n);
+  const int64_t kn = static_cast<int64_t>(k) * n;
+  DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(padded_dims(di)) * padded_points(n)));
+  DBM_TRY(ensure(h->counters, 4 * sizeof(unsigned long long)));
+  DBM_TRY(ensure(h->err, 16));
+  DBM_TRY(ensure_pinned(h, 16));
+  DBM_CUDA(cudaMemsetAsync(h->err.p, 0, 16, s));
+  PhaseTimer t(h, s, &st.ms_distance);
+  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s));
+  uint64_t cap = std::max<uint64_t>(h->edge_cap_hint, cap_hint);
+  uint64_t found = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    DBM_TRY(ensure(h->edges, sizeof(uint64_t) * std::max<uint64_t>(cap, 1)));
+    cap = h->edges.bytes / sizeof(uint64_t);
+    DBM_CUDA(cudaMemsetAsync(hist, 0, sizeof(int32_t) * kn, s));
+    DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 4 * sizeof(unsigned long long), s));
+    DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
+                 as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards};
+    DBM_TRY(launch_distance(a, s));
+    st.distance_passes = pass + 1;
+    h->pinned[0] = 0;
+    h->pinned[1] = 0;
+    DBM_CUDA(cudaMemcpyAsync(h->pinned, h->counters.p, sizeof(unsigned long long), cudaMemcpyDeviceToHost, s));
+    DBM_CUDA(cudaMemcpyAsync(h->pinned + 1, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    DBM_CUDA(cudaStreamSynchronize(s));
+    found = static_cast<uint64_t>(h->pinned[0]);
+    if (h->pinned[1] & kErrNonFinite) return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
+    if (h->pinned[1] & kErrTmaTimeout)
+      return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded TMA wait in the distance kernel ran out");
+    if (found <= cap) break;
+    if (pass == 1) return Status::Err(DBM_ERR_CUDA, "neighbour-pair buffer overflowed twice");
+    cap = found;
+  }
+  h->edge_cap_hint = std::max<uint64_t>(h->edge_cap_hint, found);
+  *found_out = found;
+  return Status::Ok();
+}
+
+// Everything after the distance pass, from the complete per-code histograms and the complete
+// list of neighbour pairs: degrees, core masks, CSR, batch plan, labelling of the configs
+// [cfg_begin, cfg_end).
+static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int32_t* minpts, int l,
+                          const int32_t* hist, const uint64_t* edges, uint64_t found, int cfg_begin,
+                          int cfg_end, int32_t* labels, uint8_t* core_out, const dbm_options& opt,
+                          const Plan& plan, dbm_stats& st, std::vector<uint8_t>& routes, cudaStream_t s)
+{
   const int64_t kn = static_cast<int64_t>(k) * n;
   const int64_t kln = kn * l;
-
-  // ---- buffers that do not depend on the graph ----
-  DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(dp) * npad));
-  DBM_TRY(ensure(h->hist, sizeof(int32_t) * kn));
+  st.unique_pairs = n * (n - 1) / 2;
+  st.edges = static_cast<int64_t>(found);
   DBM_TRY(ensure(h->deg, sizeof(int32_t) * kn));
   DBM_TRY(ensure(h->cc, sizeof(int32_t) * kn));
   DBM_TRY(ensure(h->rowcnt, sizeof(int32_t) * n));
   DBM_TRY(ensure(h->off, sizeof(int64_t) * (n + 1)));
   DBM_TRY(ensure(h->fill, sizeof(int32_t) * n));
   DBM_TRY(ensure(h->minpts, sizeof(int32_t) * l));
-  DBM_TRY(ensure(h->counters, 4 * sizeof(unsigned long long)));
   DBM_TRY(ensure(h->err, 16));
   DBM_TRY(ensure(h->scan_scratch, std::max(scan_scratch_bytes(n + 1), scan_scratch_bytes(kln + 1))));
   DBM_TRY(ensure_pinned(h, 16));
-
   DBM_CUDA(cudaMemcpyAsync(h->minpts.p, minpts, sizeof(int32_t) * l, cudaMemcpyHostToDevice, s));
-  DBM_CUDA(cudaMemsetAsync(h->err.p, 0, 16, s));
-
-  // ---- distance pass ----
-  uint64_t found = 0;
-  {
-    PhaseTimer t(h, s, &st.ms_distance);
-    DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s));
-    uint64_t cap = h->edge_cap_hint;
-    if (cap == 0) {
-      const int64_t guess = opt.neigh_per_row > 0 ? opt.neigh_per_row : 16;
-      cap = static_cast<uint64_t>(n) * static_cast<uint64_t>(guess) / 2 + 1024;
-    }
-    for (int pass = 0; pass < 2; ++pass) {
-      DBM_TRY(ensure(h->edges, sizeof(uint64_t) * cap));
-      cap = h->edges.bytes / sizeof(uint64_t);
-      DBM_CUDA(cudaMemsetAsync(h->hist.p, 0, sizeof(int32_t) * kn, s));
-      DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 4 * sizeof(unsigned long long), s));
-      DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
-                   as<uint64_t>(h->edges), cap, as<int32_t>(h->hist), as<int32_t>(h->err), h->sm_count};
-      DBM_TRY(launch_distance(a, s));
-      st.distance_passes = pass + 1;
-      h->pinned[0] = 0;
-      h->pinned[1] = 0;
-      DBM_CUDA(cudaMemcpyAsync(h->pinned, h->counters.p, sizeof(unsigned long long),
-                               cudaMemcpyDeviceToHost, s));
-      DBM_CUDA(cudaMemcpyAsync(h->pinned + 1, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-      DBM_CUDA(cudaStreamSynchronize(s));
-      found = static_cast<uint64_t>(h->pinned[0]);
-      if (h->pinned[1] & kErrNonFinite)
-        return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
-      if (h->pinned[1] & kErrTmaTimeout)
-        return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded TMA wait in the distance kernel ran out");
-      if (found <= cap) break;
-      if (pass == 1) return Status::Err(DBM_ERR_CUDA, "neighbour-pair buffer overflowed twice");
-      cap = found;
-    }
-    h->edge_cap_hint = std::max<uint64_t>(h->edge_cap_hint, found);
-  }
-  st.unique_pairs = n * (n - 1) / 2;
-  st.edges = static_cast<int64_t>(found);
 
   // ---- degrees, core counts, CSR ----
   {
     PhaseTimer t(h, s, &st.ms_graph);
-    DBM_TRY(launch_degrees(as<int32_t>(h->hist), n, k, as<int32_t>(h->minpts), l, as<int32_t>(h->deg),
-                           as<int32_t>(h->cc), as<int32_t>(h->rowcnt), core_out, s));
+    DBM_TRY(launch_degrees(hist, n, k, as<int32_t>(h->minpts), l, as<int32_t>(h->deg), as<int32_t>(h->cc),
+                           as<int32_t>(h->rowcnt), core_out, s));
     DBM_TRY(exclusive_scan_i32(as<int32_t>(h->rowcnt), as<int64_t>(h->off), n, h->scan_scratch.p,
                                h->scan_scratch.bytes, s));
     DBM_TRY(ensure(h->col, sizeof(uint32_t) * 2 * std::max<uint64_t>(found, 1)));
     DBM_TRY(ensure(h->crow, sizeof(int32_t) * 2 * std::max<uint64_t>(found, 1)));
     DBM_CUDA(cudaMemsetAsync(h->fill.p, 0, sizeof(int32_t) * n, s));
-    DBM_TRY(launch_csr_scatter(as<uint64_t>(h->edges), static_cast<int64_t>(found), as<int64_t>(h->off),
-                               as<int32_t>(h->fill), as<uint32_t>(h->col), as<int32_t>(h->crow), s));
+    DBM_TRY(launch_csr_scatter(edges, static_cast<int64_t>(found), as<int64_t>(h->off), as<int32_t>(h->fill),
+                               as<uint32_t>(h->col), as<int32_t>(h->crow), s));
   }
 
   // ---- batch plan with the reference's correction rule ----
@@ -514,7 +513,7 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
     }
   }
 
-  // ---- labelling ----
+  // ---- labelling of the configs [cfg_begin, cfg_end) ----
   {
     PhaseTimer t(h, s, &st.ms_label);
     int64_t max_slab = 0;
@@ -532,8 +531,7 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
       DBM_TRY(ensure(h->slab_col, sizeof(int32_t) * std::max<int64_t>(max_slab, 1)));
       DBM_TRY(ensure(h->slab_row, sizeof(int32_t) * std::max<int64_t>(max_slab, 1)));
     }
-    DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur),
-                           as<unsigned long long>(h->best), s));
+    DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur), as<unsigned long long>(h->best), s));
     int64_t base = 0;  // first max-eps CSR entry of the batch
     for (int64_t b = 0; b < nb; ++b) {
       const int64_t s0 = b * static_cast<int64_t>(bs);
@@ -541,6 +539,9 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
       const int64_t count = bnnz[b] - rows;  // entries without the self pairs
       const uint32_t tag = static_cast<uint32_t>(nb - 1 - b);
       for (int e = 0; e < k; ++e) {
+        const int m_lo = std::max(0, std::min(l, cfg_begin - e * l));
+        const int m_hi = std::max(0, std::min(l, cfg_end - e * l));
+        if (m_lo >= m_hi) continue;
         Slab sl;
         if (e == k - 1) {
           sl.row = as<int32_t>(h->crow) + base;
@@ -553,34 +554,54 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
           DBM_TRY(exclusive_scan_i32(as<int32_t>(h->slab_counts), as<int64_t>(h->slab_off), rows,
                                      h->scan_scratch.p, h->scan_scratch.bytes, s));
           DBM_TRY(launch_filter(as<int64_t>(h->off), as<uint32_t>(h->col), s0, rows, e,
-                                as<int64_t>(h->slab_off), as<int32_t>(h->slab_col),
-                                as<int32_t>(h->slab_row), s));
+                                as<int64_t>(h->slab_off), as<int32_t>(h->slab_col), as<int32_t>(h->slab_row), s));
           sl.row = as<int32_t>(h->slab_row);
           sl.col = as<int32_t>(h->slab_col);
-          sl.count = count;                              // upper bound for the launch size
+          sl.count = count;                                // upper bound for the launch size
           sl.count_dev = as<int64_t>(h->slab_off) + rows;  // exact, read on the device
         }
-        DBM_TRY(launch_cc_batch(sl, n, l, e, as<int32_t>(h->cc) + static_cast<int64_t>(e) * n, nb == 1,
-                                as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
+        DBM_TRY(launch_cc_batch(sl, n, l, e, m_lo, m_hi, as<int32_t>(h->cc) + static_cast<int64_t>(e) * n,
+                                nb == 1, as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
                                 as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, s));
       }
       base += count;
     }
   }
 
-  // ---- final relabel ----
+  // ---- final relabel of the configs [cfg_begin, cfg_end) ----
   {
     PhaseTimer t(h, s, &st.ms_relabel);
+    const int64_t x0 = static_cast<int64_t>(cfg_begin) * n, x1 = static_cast<int64_t>(cfg_end) * n;
     DBM_TRY(ensure(h->flags, sizeof(int32_t) * kln));
     DBM_TRY(ensure(h->rank, sizeof(int64_t) * (kln + 1)));
-    DBM_TRY(launch_cc_roots(n, k, l, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->flags), s));
-    DBM_TRY(exclusive_scan_i32(as<int32_t>(h->flags), as<int64_t>(h->rank), kln, h->scan_scratch.p,
+    DBM_TRY(launch_cc_roots(n, k, l, x0, x1, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->flags), s));
+    DBM_TRY(exclusive_scan_i32(as<int32_t>(h->flags) + x0, as<int64_t>(h->rank), x1 - x0, h->scan_scratch.p,
                                h->scan_scratch.bytes, s));
-    DBM_TRY(launch_cc_labels(n, k, l, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->cur),
+    DBM_TRY(launch_cc_labels(n, k, l, x0, x1, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->cur),
                              as<int64_t>(h->rank), labels, s));
   }
   DBM_TRY(read_err_flag(h, s));
   return Status::Ok();
+}
+
+static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps, int k,
+                  const int32_t* minpts, int l, int32_t* labels, uint8_t* core_out,
+                  const dbm_options& opt, dbm_stats& st, std::vector<uint8_t>& routes, cudaStream_t s)
+{
+  DBM_TRY(validate(n, d, eps, k, minpts, l));
+  if (!x || !labels) return Status::Err(DBM_ERR_INVALID, "x and labels must be device pointers");
+  DBM_CUDA(cudaSetDevice(h->device));
+  Plan plan;
+  DBM_TRY(plan_budget(h, n, k, l, opt, st, plan));
+  float eps2[kMaxEps];
+  square_eps(eps, k, eps2);
+  DBM_TRY(ensure(h->hist, sizeof(int32_t) * static_cast<size_t>(k) * n));
+  const uint64_t hint = static_cast<uint64_t>(n) *
+                        static_cast<uint64_t>(opt.neigh_per_row > 0 ? opt.neigh_per_row : 16) / 2 + 1024;
+  uint64_t found = 0;
+  DBM_TRY(distance_stage(h, x, n, d, eps2, k, 0, 1, as<int32_t>(h->hist), hint, &found, st, s));
+  return label_stage(h, n, d, k, minpts, l, as<int32_t>(h->hist), as<uint64_t>(h->edges), found, 0, k * l,
+                     labels, core_out, opt, plan, st, routes, s);
 }
 
 static dbm_options default_options()
@@ -736,6 +757,83 @@ int dbm_fit_multi_host(dbm_handle* h, const float* x_host, int64_t n, int64_t d,
     }
   }
   return DBM_OK;
+}
+
+int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host,
+                       int k, int shard, int nshards, int32_t* hist_dev, uint64_t* edges_dev,
+                       uint64_t edge_cap, uint64_t* edges_found, void* stream, char* err, size_t err_len)
+{
+  if (!h) {
+    dbm::set_err(err, err_len, "null handle");
+    return DBM_ERR_INVALID;
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  const int32_t one = 1;
+  dbm::Status r = dbm::validate(n, d, eps_host, k, &one, 1);
+  if (r.ok() && (!x_dev || !hist_dev || !edges_found || nshards < 1 || shard < 0 || shard >= nshards))
+    r = dbm::Status::Err(DBM_ERR_INVALID, "x, hist and edges_found are required and 0 <= shard < nshards");
+  if (r.ok()) {
+    cudaSetDevice(h->device);
+    float eps2[dbm::kMaxEps];
+    dbm::square_eps(eps_host, k, eps2);
+    dbm_stats st;
+    std::memset(&st, 0, sizeof(st));
+    uint64_t found = 0;
+    r = dbm::distance_stage(h, x_dev, n, d, eps2, k, shard, nshards, hist_dev, edge_cap, &found, st, s);
+    if (r.ok()) {
+      *edges_found = found;
+      if (found <= edge_cap && found > 0) {
+        const cudaError_t e = cudaMemcpyAsync(edges_dev, h->edges.p, found * sizeof(uint64_t),
+                                              cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess) cudaStreamSynchronize(s);
+        else r = dbm::Status::Err(DBM_ERR_CUDA, cudaGetErrorString(e));
+      }
+    }
+  }
+  dbm::set_err(err, err_len, r.msg);
+  return r.code;
+}
+
+int dbm_fit_multi_from_graph(dbm_handle* h, int64_t n, int64_t d, const float* eps_host, int k,
+                             const int32_t* min_pts_host, int l, const int32_t* hist_dev,
+                             const uint64_t* edges_dev, uint64_t m_edges, int cfg_begin, int cfg_end,
+                             int32_t* labels_dev, uint8_t* core_dev, const dbm_options* opt,
+                             dbm_stats* stats, uint8_t* batch_routes, int routes_len, void* stream,
+                             char* err, size_t err_len)
+{
+  if (!h) {
+    dbm::set_err(err, err_len, "null handle");
+    return DBM_ERR_INVALID;
+  }
+  const dbm_options o = opt ? *opt : dbm::default_options();
+  dbm_stats st;
+  std::memset(&st, 0, sizeof(st));
+  std::vector<uint8_t> routes;
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  const int64_t launches0 = dbm::launches_so_far();
+  dbm::Status r = dbm::validate(n, d, eps_host, k, min_pts_host, l);
+  if (r.ok() && (!hist_dev || (!edges_dev && m_edges > 0) || !labels_dev || cfg_begin < 0 ||
+                 cfg_end > k * l || cfg_begin > cfg_end))
+    r = dbm::Status::Err(DBM_ERR_INVALID, "hist, edges and labels are required and 0 <= cfg_begin <= cfg_end <= k*l");
+  if (r.ok()) {
+    cudaSetDevice(h->device);
+    dbm::Plan plan;
+    r = dbm::plan_budget(h, n, k, l, o, st, plan);
+    if (r.ok())
+      r = dbm::label_stage(h, n, d, k, min_pts_host, l, hist_dev, edges_dev, m_edges, cfg_begin, cfg_end,
+                           labels_dev, core_dev, o, plan, st, routes, s);
+    if (r.ok()) {
+      const cudaError_t e = cudaStreamSynchronize(s);
+      if (e != cudaSuccess) r = dbm::Status::Err(DBM_ERR_CUDA, cudaGetErrorString(e));
+    }
+  }
+  st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
+  if (stats) *stats = st;
+  if (batch_routes && routes_len > 0)
+    for (int i = 0; i < routes_len; ++i)
+      batch_routes[i] = i < static_cast<int>(routes.size()) ? routes[i] : DBM_BATCH_NOT_APPLICABLE;
+  dbm::set_err(err, err_len, r.msg);
+  return r.code;
 }
 
 int dbm_neighbor_counts(dbm_handle* h, const float* x_dev, int64_t n, int64_t d,

@@ -46,45 +46,46 @@ __global__ void cc_init_kernel(int64_t n, int64_t total, int32_t* __restrict__ G
        q += static_cast<int64_t>(gridDim.x) * blockDim.x)
 
 // L[cfg][v] = v for both endpoints of every slab entry (configs where v is core).
-__global__ void cc_touch_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __restrict__ cc,
-                                int32_t* __restrict__ L)
+__global__ void cc_touch_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_hi,
+                                const int32_t* __restrict__ cc, int32_t* __restrict__ L)
 {
   DBM_SLAB_LOOP(sl, q)
   {
     const int32_t r = sl.row[q];
     const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
-    const int cr = cc[r], cj = cc[j];
-    for (int m = 0; m < cr; ++m) L[static_cast<int64_t>(cfg0 + m) * n + r] = r;
-    for (int m = 0; m < cj; ++m) L[static_cast<int64_t>(cfg0 + m) * n + j] = j;
+    const int cr = min(cc[r], m_hi), cj = min(cc[j], m_hi);
+    for (int m = m_lo; m < cr; ++m) L[static_cast<int64_t>(cfg0 + m) * n + r] = r;
+    for (int m = m_lo; m < cj; ++m) L[static_cast<int64_t>(cfg0 + m) * n + j] = j;
   }
 }
 
 // unite(P[cfg], r, j) for every core-core slab entry
-__global__ void cc_union_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __restrict__ cc,
-                                int32_t* __restrict__ P, int32_t* __restrict__ err)
+__global__ void cc_union_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_hi,
+                                const int32_t* __restrict__ cc, int32_t* __restrict__ P,
+                                int32_t* __restrict__ err)
 {
   bool ok = true;
   DBM_SLAB_LOOP(sl, q)
   {
     const int32_t r = sl.row[q];
     const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
-    const int mm = min(cc[r], cc[j]);
-    for (int m = 0; m < mm; ++m) ok &= uf_unite(P + static_cast<int64_t>(cfg0 + m) * n, r, j);
+    const int mm = min(min(cc[r], cc[j]), m_hi);
+    for (int m = m_lo; m < mm; ++m) ok &= uf_unite(P + static_cast<int64_t>(cfg0 + m) * n, r, j);
   }
   if (!ok) atomicOr(err, kErrUnionLimit);
 }
 
 // For every slab entry with exactly one core endpoint c: best[p] = min(tag << 32 | find(P, c)).
-__global__ void cc_best_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __restrict__ cc,
-                               int32_t* __restrict__ P, unsigned long long* __restrict__ best,
-                               uint32_t tag)
+__global__ void cc_best_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_hi,
+                               const int32_t* __restrict__ cc, int32_t* __restrict__ P,
+                               unsigned long long* __restrict__ best, uint32_t tag)
 {
   DBM_SLAB_LOOP(sl, q)
   {
     const int32_t r = sl.row[q];
     const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
     const int cr = cc[r], cj = cc[j];
-    const int lo = min(cr, cj), hi = max(cr, cj);
+    const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
     for (int m = lo; m < hi; ++m) {
       const bool r_core = m < cr;
       const int32_t c = r_core ? r : j;
@@ -98,16 +99,17 @@ __global__ void cc_best_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __re
 }
 
 // cur[p] = min(find(G, cur[p]), find(G, best[p])) for every border endpoint of the slab.
-__global__ void cc_border_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __restrict__ cc,
-                                 int32_t* __restrict__ G, const unsigned long long* __restrict__ best,
-                                 int32_t* __restrict__ cur, uint32_t tag)
+__global__ void cc_border_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_hi,
+                                 const int32_t* __restrict__ cc, int32_t* __restrict__ G,
+                                 const unsigned long long* __restrict__ best, int32_t* __restrict__ cur,
+                                 uint32_t tag)
 {
   DBM_SLAB_LOOP(sl, q)
   {
     const int32_t r = sl.row[q];
     const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
     const int cr = cc[r], cj = cc[j];
-    const int lo = min(cr, cj), hi = max(cr, cj);
+    const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
     for (int m = lo; m < hi; ++m) {
       const int32_t pt = (m < cr) ? j : r;
       const int64_t base = static_cast<int64_t>(cfg0 + m) * n;
@@ -122,13 +124,14 @@ __global__ void cc_border_kernel(Slab sl, int64_t n, int cfg0, const int32_t* __
   }
 }
 
-// flags[cfg][i] = 1 for the root of every core component (compressing G on the way)
-__global__ void cc_roots_kernel(int64_t n, int k, int l, const int32_t* __restrict__ cc,
-                                int32_t* __restrict__ G, int32_t* __restrict__ flags)
+// flags[cfg][i] = 1 for the root of every core component (compressing G on the way); only the
+// configs [x0 / n, x1 / n) are touched.
+__global__ void cc_roots_kernel(int64_t n, int k, int l, int64_t x0, int64_t x1,
+                                const int32_t* __restrict__ cc, int32_t* __restrict__ G,
+                                int32_t* __restrict__ flags)
 {
-  const int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = n * k * l;
-  if (x >= total) return;
+  const int64_t x = x0 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (x >= x1) return;
   const int64_t cfg = x / n, i = x - cfg * n;
   const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
   int32_t f = 0;
@@ -140,28 +143,29 @@ __global__ void cc_roots_kernel(int64_t n, int k, int l, const int32_t* __restri
 }
 
 // cluster id = rank of the component root among the config's roots; -1 noise
-__global__ void cc_labels_kernel(int64_t n, int k, int l, const int32_t* __restrict__ cc,
-                                 int32_t* __restrict__ G, const int32_t* __restrict__ cur,
-                                 const int64_t* __restrict__ rank, int32_t* __restrict__ labels)
+__global__ void cc_labels_kernel(int64_t n, int k, int l, int64_t x0, int64_t x1,
+                                 const int32_t* __restrict__ cc, int32_t* __restrict__ G,
+                                 const int32_t* __restrict__ cur, const int64_t* __restrict__ rank,
+                                 int32_t* __restrict__ labels)
 {
-  const int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = n * k * l;
-  if (x >= total) return;
+  const int64_t x = x0 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (x >= x1) return;
   const int64_t cfg = x / n, i = x - cfg * n;
   const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
   int32_t* g = G + cfg * n;
-  const int64_t r0 = rank[cfg * n];
+  const int64_t rb = cfg * n - x0;  // rank holds the scan of flags[x0, x1)
+  const int64_t r0 = rank[rb];
   int32_t out;
   if (m < cc[static_cast<int64_t>(e) * n + i]) {
     const int32_t root = uf_find(g, static_cast<int32_t>(i));
-    out = static_cast<int32_t>(rank[cfg * n + root] - r0);
+    out = static_cast<int32_t>(rank[rb + root] - r0);
   } else {
     const int32_t v = cur[x];
     if (v == kNone) {
       out = -1;
     } else {
       const int32_t root = uf_find(g, v);
-      out = static_cast<int32_t>(rank[cfg * n + root] - r0);
+      out = static_cast<int32_t>(rank[rb + root] - r0);
     }
   }
   labels[x] = out;
@@ -185,45 +189,45 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 
 // One batch of one eps: local components (when there is more than one batch), border
 // candidates, global union, border fold.
-Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, const int32_t* cc_e, bool single_batch,
-                       int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur, uint32_t tag,
-                       int32_t* err, int sm_count, cudaStream_t s)
+Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, int m_lo, int m_hi, const int32_t* cc_e,
+                       bool single_batch, int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur,
+                       uint32_t tag, int32_t* err, int sm_count, cudaStream_t s)
 {
-  if (sl.count <= 0) return Status::Ok();
+  if (sl.count <= 0 || m_lo >= m_hi) return Status::Ok();
   const int cfg0 = e * l;
   const int64_t want = ceil_div(sl.count, 256);
   const unsigned nb = static_cast<unsigned>(std::min<int64_t>(want, static_cast<int64_t>(sm_count) * 16));
   if (single_batch) {
     count_launch(2);
-    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, G, err);
-    cc_best_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, G, best, tag);
+    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, G, err);
+    cc_best_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, G, best, tag);
   } else {
     count_launch(4);
-    cc_touch_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, L);
-    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, L, err);
-    cc_best_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, L, best, tag);
-    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, G, err);
+    cc_touch_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, L);
+    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, L, err);
+    cc_best_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, L, best, tag);
+    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, G, err);
   }
   count_launch();
-  cc_border_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, cc_e, G, best, cur, tag);
+  cc_border_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, G, best, cur, tag);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
 
-Status launch_cc_roots(int64_t n, int k, int l, const int32_t* cc, int32_t* G, int32_t* flags,
-                       cudaStream_t s)
+Status launch_cc_roots(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
+                       int32_t* flags, cudaStream_t s)
 {
   count_launch();
-  cc_roots_kernel<<<blocks_for(n * k * l, 256), 256, 0, s>>>(n, k, l, cc, G, flags);
+  cc_roots_kernel<<<blocks_for(x1 - x0, 256), 256, 0, s>>>(n, k, l, x0, x1, cc, G, flags);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
 
-Status launch_cc_labels(int64_t n, int k, int l, const int32_t* cc, int32_t* G, const int32_t* cur,
-                        const int64_t* rank, int32_t* labels, cudaStream_t s)
+Status launch_cc_labels(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
+                        const int32_t* cur, const int64_t* rank, int32_t* labels, cudaStream_t s)
 {
   count_launch();
-  cc_labels_kernel<<<blocks_for(n * k * l, 256), 256, 0, s>>>(n, k, l, cc, G, cur, rank, labels);
+  cc_labels_kernel<<<blocks_for(x1 - x0, 256), 256, 0, s>>>(n, k, l, x0, x1, cc, G, cur, rank, labels);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }

@@ -162,6 +162,8 @@ struct DistLaunch {
   int32_t* hist;                   // k x n
   int32_t* err;
   int sm_count;
+  int shard = 0;                   // evaluate the shard-th of nshards equal tile-pair ranges
+  int nshards = 1;
 };
 
 // ---- kernel launch accounting (host) --------------------------------------------------------

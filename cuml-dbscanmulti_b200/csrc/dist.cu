@@ -40,7 +40,8 @@ struct DistParams {
   int32_t k;
   int32_t dbox;                      // dims per box actually used (<= kDimBox)
   int32_t nchunks;                   // ceil(d / dbox)
-  int64_t tile_pairs;                // T(T+1)/2
+  int64_t tile_begin;                // this launch's share of the T(T+1)/2 tile pairs
+  int64_t tile_end;
   unsigned long long* counters;      // [0] edge cursor, [1] next tile pair
   uint64_t* edges;
   uint64_t edge_cap;
@@ -101,7 +102,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   float* As1 = Bs0 + box_floats;
   float* Bs1 = As1 + box_floats;
   __shared__ __align__(8) uint64_t full[2];
-  __shared__ long long s_tile[2];  // tile pair index held by each stage (>= tile_pairs: none)
+  __shared__ long long s_tile[2];  // tile pair index held by each stage (>= tile_end: none)
   __shared__ float s_eps2[kMaxEps];
 
   const int tid = threadIdx.x;
@@ -113,7 +114,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   auto issue = [&](int stage, long long tile, int chunk) {
     // one thread: record the item and start both tile loads of this stage
     s_tile[stage] = tile;
-    if (tile >= p.tile_pairs) return;
+    if (tile >= p.tile_end) return;
     long long I, J;
     tri_coords(tile, I, J);
     fence_proxy_async_smem();
@@ -128,7 +129,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
     mbar_init(&full[0], 1);
     mbar_init(&full[1], 1);
     mbar_fence_init();
-    issue(0, static_cast<long long>(atomicAdd(p.counters + 1, 1ULL)), 0);
+    issue(0, p.tile_begin + static_cast<long long>(atomicAdd(p.counters + 1, 1ULL)), 0);
   }
   __syncthreads();
 
@@ -144,7 +145,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
 
   for (;;) {
     const long long c = s_tile[stage];
-    if (c >= p.tile_pairs) break;
+    if (c >= p.tile_end) break;
     const bool ok = mbar_wait_bounded(&full[stage], phase[stage], kWaitPolls);
     if (__syncthreads_or(!ok)) {
       if (tid == 0) atomicOr(p.err, kErrTmaTimeout);
@@ -159,7 +160,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
       if (!last_chunk)
         issue(stage ^ 1, c, chunk + 1);
       else
-        issue(stage ^ 1, static_cast<long long>(atomicAdd(p.counters + 1, 1ULL)), 0);
+        issue(stage ^ 1, p.tile_begin + static_cast<long long>(atomicAdd(p.counters + 1, 1ULL)), 0);
     }
     const float* As = stage ? As1 : As0;
     const float* Bs = stage ? Bs1 : Bs0;
@@ -357,7 +358,10 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   p.dbox = dbox;
   p.nchunks = static_cast<int32_t>(ceil_div(a.d, dbox));
   const int64_t T = ceil_div(a.n, kTile);
-  p.tile_pairs = T * (T + 1) / 2;
+  const int64_t pairs = T * (T + 1) / 2;
+  const int shards = a.nshards > 0 ? a.nshards : 1;
+  p.tile_begin = pairs * a.shard / shards;
+  p.tile_end = pairs * (a.shard + 1) / shards;
   p.counters = a.counters;
   p.edges = a.edges;
   p.edge_cap = a.edge_cap;
@@ -375,7 +379,8 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
                                                          smem));
   if (per_sm < 1) per_sm = 1;
   int64_t grid = static_cast<int64_t>(a.sm_count) * per_sm;
-  if (grid > p.tile_pairs) grid = p.tile_pairs;
+  if (grid > p.tile_end - p.tile_begin) grid = p.tile_end - p.tile_begin;
+  if (grid < 1) return Status::Ok();
   count_launch();
   dist_tri_kernel<<<static_cast<unsigned>(grid), kDistThreads, smem, s>>>(map, p);
   DBM_CUDA(cudaGetLastError());

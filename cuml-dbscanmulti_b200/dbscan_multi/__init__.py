@@ -55,7 +55,7 @@ EXPORTED = (
     "dbm_create", "dbm_destroy", "dbm_workspace_bytes", "dbm_set_phase_timing",
     "dbm_fit_multi", "dbm_fit_multi_host", "dbm_neighbor_counts", "dbm_batch_size", "dbm_max_bytes_for_batch_size",
     "dbm_annotate_pays", "dbm_auto_index_bits", "dbm_build_info_json",
-    "dbm_neighbor_counts_noalloc",
+    "dbm_neighbor_counts_noalloc", "dbm_distance_shard", "dbm_fit_multi_from_graph",
 )
 
 
@@ -130,6 +130,11 @@ def load_library():
     lib.dbm_fit_multi.restype = i32
     lib.dbm_fit_multi_host.argtypes = fit_args + [cp, sz]
     lib.dbm_fit_multi_host.restype = i32
+    lib.dbm_distance_shard.argtypes = [p, p, i64, i64, p, i32, i32, i32, p, p, u64, ctypes.POINTER(u64), p, cp, sz]
+    lib.dbm_distance_shard.restype = i32
+    lib.dbm_fit_multi_from_graph.argtypes = [p, i64, i64, p, i32, p, i32, p, p, u64, i32, i32, p, p,
+                                             ctypes.POINTER(Options), ctypes.POINTER(Stats), p, i32, p, cp, sz]
+    lib.dbm_fit_multi_from_graph.restype = i32
     lib.dbm_neighbor_counts.argtypes = [p, p, i64, i64, p, i32, p, p, cp, sz]
     lib.dbm_neighbor_counts.restype = i32
     lib.dbm_batch_size.argtypes = [i64, i32, i32, u64, i32, i64, i32, ctypes.POINTER(u64), cp, sz]

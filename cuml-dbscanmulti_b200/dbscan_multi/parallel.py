@@ -1,0 +1,167 @@
+"""Multi-GPU fit_multi: one process per GPU, torch.distributed for the exchanges.
+
+The reference's fit_multi is single-GPU (runner_multi.cuh:15-16 removed cuML's multi-node
+path).  Here the work shards without changing a single label:
+
+1. every rank evaluates an equal share of the 128 x 128 tile pairs (i <= j) of the distance
+   pass (``dbm_distance_shard``): per-code histograms for all N rows and the neighbour pairs
+   found in its share;
+2. the histograms are summed across ranks (all-reduce) -- exact degrees everywhere -- and the
+   neighbour pairs are all-gathered (variable counts, padded);
+3. every rank labels a contiguous range of the k*l configurations from the complete graph
+   (``dbm_fit_multi_from_graph``), with a batch plan that is identical on all ranks because the
+   budget and the CSR memory cap are agreed first (minimum over ranks);
+4. the label rows are all-gathered, so every rank ends with the full (k*l, N) result.
+
+The collectives run on whatever backend the process group has (NCCL over NVLink on B200s,
+gloo for the CPU tests).  The kernel work sits behind a ``stages`` object so the tests can
+drive this exact orchestration with an oracle-backed fake on CPU ranks.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Any
+
+import numpy as np
+
+from . import (DBM_OK, DbmError, DbscanMulti, FitResult, Options, Stats, ROUTE_NAMES, BACKENDS,
+               INDEX, ROUTES, normalize_eps, normalize_min_samples)
+
+TILE = 128
+
+
+def tile_pair_range(n: int, shard: int, nshards: int) -> tuple[int, int]:
+    """The [begin, end) tile-pair indices a shard evaluates (same rule as dist.cu)."""
+    t = (n + TILE - 1) // TILE
+    pairs = t * (t + 1) // 2
+    return pairs * shard // nshards, pairs * (shard + 1) // nshards
+
+
+def config_range(c: int, rank: int, world: int) -> tuple[int, int]:
+    return c * rank // world, c * (rank + 1) // world
+
+
+class DeviceStages:
+    """The C-ABI stages on this rank's GPU."""
+
+    def __init__(self, handle: DbscanMulti):
+        self.h = handle
+        self.lib = handle._lib
+
+    def default_budget(self) -> int:
+        """80% of (free + this handle's reusable workspace), as the reference's fit_multi."""
+        import torch
+
+        free, total = torch.cuda.mem_get_info(self.h.device)
+        reusable = self.h.workspace_bytes
+        used = total - min(total, free)
+        available = total if reusable > used else min(total, free + reusable)
+        return 80 * available // 100
+
+    def free_bytes(self) -> int:
+        import torch
+
+        return int(torch.cuda.mem_get_info(self.h.device)[0])
+
+    def distance_shard(self, x, eps: np.ndarray, shard: int, nshards: int, cap_hint: int):
+        import torch
+
+        n, d = int(x.shape[0]), int(x.shape[1])
+        k = len(eps)
+        hist = torch.empty((k, n), dtype=torch.int32, device=x.device)
+        cap = max(int(cap_hint), 1024)
+        s = torch.cuda.current_stream(x.device).cuda_stream
+        err = ctypes.create_string_buffer(1024)
+        for _ in range(2):
+            edges = torch.empty(cap, dtype=torch.int64, device=x.device)
+            found = ctypes.c_uint64(0)
+            rc = self.lib.dbm_distance_shard(self.h._h, ctypes.c_void_p(x.data_ptr()), n, d,
+                                             eps.ctypes.data_as(ctypes.c_void_p), k, shard, nshards,
+                                             ctypes.c_void_p(hist.data_ptr()), ctypes.c_void_p(edges.data_ptr()),
+                                             cap, ctypes.byref(found), ctypes.c_void_p(s), err, len(err))
+            if rc != DBM_OK:
+                raise DbmError(rc, err.value.decode())
+            if found.value <= cap:
+                return hist, edges[: found.value]
+            cap = int(found.value)
+        raise DbmError(-5, "neighbour-pair buffer overflowed twice")
+
+    def fit_from_graph(self, n, d, eps, ms, hist, edges, cfg_begin, cfg_end, opt: Options):
+        import torch
+
+        k, l = len(eps), len(ms)
+        labels = torch.empty((k * l, n), dtype=torch.int32, device=hist.device)
+        st = Stats()
+        routes = (ctypes.c_uint8 * (n + 1))()
+        s = torch.cuda.current_stream(hist.device).cuda_stream
+        err = ctypes.create_string_buffer(1024)
+        edges = edges.contiguous()
+        rc = self.lib.dbm_fit_multi_from_graph(
+            self.h._h, n, d, eps.ctypes.data_as(ctypes.c_void_p), k, ms.ctypes.data_as(ctypes.c_void_p), l,
+            ctypes.c_void_p(hist.data_ptr()), ctypes.c_void_p(edges.data_ptr()) if edges.numel() else None,
+            int(edges.numel()), cfg_begin, cfg_end, ctypes.c_void_p(labels.data_ptr()), None,
+            ctypes.byref(opt), ctypes.byref(st), routes, n + 1, ctypes.c_void_p(s), err, len(err))
+        if rc != DBM_OK:
+            raise DbmError(rc, err.value.decode())
+        return labels, st.as_dict(), [ROUTE_NAMES[int(routes[i])] for i in range(int(st.batches))]
+
+
+def _all_gather_varlen(dist, t, group):
+    """All-gather 1-D tensors of different lengths (pads to the longest); returns the parts."""
+    import torch
+
+    world = dist.get_world_size(group)
+    cnt = torch.tensor([t.numel()], dtype=torch.int64, device=t.device)
+    counts = [torch.zeros_like(cnt) for _ in range(world)]
+    dist.all_gather(counts, cnt, group=group)
+    counts = [int(c.item()) for c in counts]
+    mx = max(counts) if counts else 0
+    buf = torch.zeros(max(mx, 1), dtype=t.dtype, device=t.device)
+    buf[: t.numel()] = t
+    out = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(out, buf, group=group)
+    return [o[:c] for o, c in zip(out, counts)]
+
+
+def sharded_fit_multi(stages, x, eps, min_samples, *, group=None, max_bytes_per_batch: int = 0,
+                      backend: str = "cuvs", index: str = "auto", route: str = "auto",
+                      neigh_per_row: int = 0, csr_cap_bytes: int = 0) -> FitResult:
+    """fit_multi over all ranks of ``group``; every rank returns the full (k*l, N) labels."""
+    import torch
+    import torch.distributed as dist
+
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    e = normalize_eps(eps)
+    m = normalize_min_samples(min_samples)
+    k, l = len(e), len(m)
+    n, d = int(x.shape[0]), int(x.shape[1])
+    if backend not in BACKENDS or index not in INDEX or route not in ROUTES:
+        raise DbmError(-1, "unknown backend, index or route")
+    if route != "auto" and backend != "cuvs":
+        raise DbmError(-1, "--route only applies to the cuvs backend")
+    dev = x.device
+
+    # identical batch plans on every rank: agree on the budget and the CSR memory cap
+    agree = torch.tensor([max_bytes_per_batch or stages.default_budget(), csr_cap_bytes or stages.free_bytes()],
+                         dtype=torch.int64, device=dev)
+    dist.all_reduce(agree, op=dist.ReduceOp.MIN, group=group)
+    budget, cap = int(agree[0].item()), int(agree[1].item())
+    opt = Options(BACKENDS[backend], INDEX[index], ROUTES[route], int(neigh_per_row), budget, cap)
+
+    hint = n * (neigh_per_row if neigh_per_row > 0 else 16) // (2 * world) + 1024
+    hist, edges = stages.distance_shard(x, e, rank, world, hint)
+    dist.all_reduce(hist, op=dist.ReduceOp.SUM, group=group)
+    parts = _all_gather_varlen(dist, edges, group)
+    all_edges = torch.cat(parts) if parts else edges
+
+    c0, c1 = config_range(k * l, rank, world)
+    labels, stats, routes = stages.fit_from_graph(n, d, e, m, hist, all_edges, c0, c1, opt)
+    mine = labels[c0:c1].reshape(-1)
+    rows = _all_gather_varlen(dist, mine, group)
+    full = torch.cat(rows).reshape(k * l, n)
+    stats = dict(stats)
+    stats["world_size"] = world
+    stats["edges"] = int(all_edges.numel())
+    return FitResult(labels=full, core=None, eps=e, min_samples=m, stats=stats, batch_routes=routes,
+                     index="int64" if stats.get("index_bits") == 64 else "int32", backend=backend)

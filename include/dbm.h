@@ -143,6 +143,34 @@ int dbm_fit_multi_host(dbm_handle* h, const float* x_host, int64_t n, int64_t d,
                        dbm_stats* stats, uint8_t* batch_routes, int routes_len, char* err,
                        size_t err_len);
 
+/* ---- multi-GPU stages (one process per GPU; the caller runs the collectives) ------------
+ * dbm_fit_multi = dbm_distance_shard(shard 0 of 1) + dbm_fit_multi_from_graph(all configs).
+ * With G ranks: rank r runs dbm_distance_shard(r, G); the hist arrays are summed across ranks
+ * (all-reduce) and the neighbour pairs concatenated (all-gather, any order); every rank then
+ * runs dbm_fit_multi_from_graph for its range of configs with the same options (an explicit
+ * budget and csr_cap_bytes agreed across ranks keep the batch plan identical). */
+
+/* Distance pass over the shard-th of nshards equal ranges of 128x128 tile pairs (i <= j).
+ * hist_dev: k*n int32 (zeroed here): pairs (i, j != i) of this shard per row and exact code.
+ * edges_dev: edge_cap 64-bit words, i << 32 | code << 28 | j, one per neighbour pair i < j within
+ * the largest eps found in this shard.  *edges_found receives the count; when it exceeds
+ * edge_cap nothing is copied and the call must be repeated with a larger buffer.
+ * Replaces the reference's pass-1 search over a row batch (runner_multi.cuh:627-655). */
+int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host,
+                       int k, int shard, int nshards, int32_t* hist_dev, uint64_t* edges_dev,
+                       uint64_t edge_cap, uint64_t* edges_found, void* stream, char* err, size_t err_len);
+
+/* Everything after the distance pass, from the complete per-code histograms (summed over all
+ * shards) and the complete list of neighbour pairs: degrees, core masks, CSR, batch plan and
+ * the labels of the configs [cfg_begin, cfg_end) (labels_dev rows outside the range are not
+ * written).  Replaces runner_multi.cuh:657-746 (CSR, weak CC, merge, relabel). */
+int dbm_fit_multi_from_graph(dbm_handle* h, int64_t n, int64_t d, const float* eps_host, int k,
+                             const int32_t* min_pts_host, int l, const int32_t* hist_dev,
+                             const uint64_t* edges_dev, uint64_t m_edges, int cfg_begin, int cfg_end,
+                             int32_t* labels_dev, uint8_t* core_dev, const dbm_options* opt,
+                             dbm_stats* stats, uint8_t* batch_routes, int routes_len, void* stream,
+                             char* err, size_t err_len);
+
 /* Per-eps neighbourhood sizes only (the point itself included): deg_dev[e*n + i] = #{j :
  * dist2(i, j) <= eps_e^2}, int32, device.  This is the degree vector the reference's
  * VertexDeg::run_multi produces per batch (src/multi/eps_neighborhood.cuh:440-479, vd[e]). */

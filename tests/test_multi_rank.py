@@ -1,0 +1,148 @@
+"""Multi-rank orchestration on CPU: gloo process groups (world size 2 and 3) run the real
+``dbscan_multi.parallel.sharded_fit_multi`` with an oracle-backed stand-in for the two
+device stages.  Checked: the tile-pair shards partition the triangle exactly, the summed
+histograms and gathered neighbour pairs equal the single-process graph, budget and CSR cap
+are agreed (minimum over ranks), every rank ends with the full, oracle-identical labels."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import batching
+import oracle
+from dbscan_multi import parallel
+
+TILE = parallel.TILE
+
+
+def tri_coords(c):
+    j = int((np.sqrt(8.0 * c + 1.0) - 1.0) * 0.5)
+    while j * (j + 1) // 2 > c:
+        j -= 1
+    while (j + 1) * (j + 2) // 2 <= c:
+        j += 1
+    return c - j * (j + 1) // 2, j
+
+
+def make_points(seed=4, n=700):
+    rng = np.random.default_rng(seed)
+    c = rng.uniform(-3, 3, size=(5, 2))
+    pts = c[rng.integers(0, 5, n - 60)] + rng.normal(0, 0.35, (n - 60, 2))
+    return np.vstack([pts, rng.uniform(-3, 3, (60, 2))]).astype(np.float32)
+
+
+EPS = [0.15, 0.25, 0.35]
+MS = [3, 6]
+
+
+class OracleStages:
+    """CPU stand-in for the C-ABI stages, computed from the oracle's per-pair codes."""
+
+    def __init__(self, pts, rank):
+        self.pts = pts
+        self.rank = rank
+        self.codes, self.deg = oracle.codes_degrees(pts, EPS)
+        self.seen_opt = None
+
+    def default_budget(self):
+        # ~150-row batches; ranks disagree and the minimum must win
+        return batching.max_bytes_for_batch_size(700, 3, 2, 150, True, 0, 32) + 1000 * self.rank
+
+    def free_bytes(self):
+        return 10**9 - self.rank
+
+    def distance_shard(self, x, eps, shard, nshards, cap_hint):
+        n = len(self.pts)
+        k = len(eps)
+        b, e = parallel.tile_pair_range(n, shard, nshards)
+        hist = np.zeros((k, n), np.int32)
+        words = []
+        for c in range(b, e):
+            ti, tj = tri_coords(c)
+            for i in range(ti * TILE, min(n, ti * TILE + TILE)):
+                for j in range(tj * TILE, min(n, tj * TILE + TILE)):
+                    if ti == tj and j <= i:
+                        continue
+                    code = int(self.codes[i, j])
+                    if code == 255:
+                        continue
+                    hist[code, i] += 1
+                    hist[code, j] += 1
+                    words.append((i << 32) | (code << 28) | j)
+        return torch.from_numpy(hist), torch.tensor(words, dtype=torch.int64)
+
+    def fit_from_graph(self, n, d, eps, ms, hist, edges, c0, c1, opt):
+        k, l = len(eps), len(ms)
+        # complete graph check: cumulative histograms are the oracle's degrees
+        deg = 1 + np.cumsum(hist.numpy(), axis=0)
+        assert np.array_equal(deg, self.deg)
+        iu, ju = np.nonzero(np.triu(self.codes != 255, 1))
+        want = set(((iu.astype(np.int64) << 32) | (self.codes[iu, ju].astype(np.int64) << 28) | ju).tolist())
+        got = edges.numpy().tolist()
+        assert len(got) == len(want) and set(got) == want
+        self.seen_opt = (opt.max_bytes_per_batch, opt.csr_cap_bytes)
+        bs = batching.compute_batch_size(n, k, l, opt.max_bytes_per_batch, True, 0, 32)
+        lab, _, _ = oracle.fit_multi(self.pts, eps, ms, bs)
+        out = np.full((k * l, n), -7, np.int32)
+        out[c0:c1] = lab[c0:c1]
+        return torch.from_numpy(out), {"batches": (n + bs - 1) // bs, "index_bits": 32}, []
+
+
+def _worker(rank, world, port, result_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        pts = make_points()
+        st = OracleStages(pts, rank)
+        res = parallel.sharded_fit_multi(st, torch.from_numpy(pts), EPS, MS, index="int32")
+        np.save(os.path.join(result_dir, f"labels_{rank}.npy"), res.labels.numpy())
+        np.save(os.path.join(result_dir, f"opt_{rank}.npy"), np.asarray(st.seen_opt, dtype=np.int64))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_tile_pair_shards_partition_the_triangle():
+    for n in (1, 127, 128, 129, 1000, 4097):
+        t = (n + TILE - 1) // TILE
+        for world in (1, 2, 3, 8):
+            ranges = [parallel.tile_pair_range(n, r, world) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == t * (t + 1) // 2
+            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+    assert [parallel.config_range(16, r, 8) for r in range(8)] == [(2 * r, 2 * r + 2) for r in range(8)]
+    for c in (1, 5, 9, 16, 100):
+        for world in (1, 2, 3, 8):
+            rs = [parallel.config_range(c, r, world) for r in range(world)]
+            assert rs[0][0] == 0 and rs[-1][1] == c and all(a[1] == b[0] for a, b in zip(rs, rs[1:]))
+            sizes = [b - a for a, b in rs]
+            assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_fit_on_gloo_ranks_equals_single_process(tmp_path, world):
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    pts = make_points()
+    opt0 = np.load(tmp_path / "opt_0.npy")
+    assert opt0[0] == batching.max_bytes_for_batch_size(700, 3, 2, 150, True, 0, 32)  # minimum over ranks
+    assert opt0[1] == 10**9 - (world - 1)
+    bs = batching.compute_batch_size(len(pts), len(EPS), len(MS), int(opt0[0]), True, 0, 32)
+    assert bs == 150  # the agreed budget really batches
+    want, _, _ = oracle.fit_multi(pts, EPS, MS, bs)
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"labels_{r}.npy"), want)
+        assert np.array_equal(np.load(tmp_path / f"opt_{r}.npy"), opt0)
