@@ -388,10 +388,21 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     st.distance_passes = pass + 1;
     h->pinned[0] = 0;
     h->pinned[1] = 0;
+    h->pinned[2] = 0;
     DBM_CUDA(cudaMemcpyAsync(h->pinned, h->counters.p, sizeof(unsigned long long), cudaMemcpyDeviceToHost, s));
     DBM_CUDA(cudaMemcpyAsync(h->pinned + 1, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    DBM_CUDA(cudaMemcpyAsync(h->pinned + 2, as<unsigned long long>(h->counters) + 2, sizeof(unsigned long long),
+                             cudaMemcpyDeviceToHost, s));
     DBM_CUDA(cudaStreamSynchronize(s));
     found = static_cast<uint64_t>(h->pinned[0]);
+    {
+      // 8 warps per 128 x 128 tile, each evaluating up to d dims for its 16 x 128 pairs
+      const int64_t T = ceil_div(n, 128);
+      const int64_t pairs = T * (T + 1) / 2;
+      const int64_t tiles = pairs * (shard + 1) / nshards - pairs * shard / nshards;
+      const double full = static_cast<double>(tiles) * 8.0 * static_cast<double>(d);
+      st.dist_work_fraction = full > 0 ? static_cast<double>(h->pinned[2]) / full : 1.0;
+    }
     if (h->pinned[1] & kErrNonFinite) return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
     if (h->pinned[1] & kErrTmaTimeout)
       return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded TMA wait in the distance kernel ran out");

@@ -32,6 +32,10 @@ constexpr int kTile = 128;
 constexpr int kDistThreads = 256;
 constexpr int kDimBox = 64;          // dims per TMA box
 constexpr uint32_t kWaitPolls = 1u << 24;
+#ifndef DBM_PROBE_DIMS
+#define DBM_PROBE_DIMS 8
+#endif
+constexpr int kProbeDims = DBM_PROBE_DIMS;  // dims between two early-exit checks
 
 
 struct DistParams {
@@ -143,9 +147,12 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
 
+  bool warp_done = false;      // this warp's pairs of the current tile are all beyond the cutoff
+  long long dims_done = 0;     // dims this warp evaluated, over all its tiles
   for (;;) {
     const long long c = s_tile[stage];
     if (c >= p.tile_end) break;
+    if (chunk == 0) warp_done = false;
     const bool ok = mbar_wait_bounded(&full[stage], phase[stage], kWaitPolls);
     if (__syncthreads_or(!ok)) {
       if (tid == 0) atomicOr(p.err, kErrTmaTimeout);
@@ -165,8 +172,11 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
     const float* As = stage ? As1 : As0;
     const float* Bs = stage ? Bs1 : Bs0;
     const int dk = min(p.dbox, p.d - chunk * p.dbox);
-#pragma unroll 2
-    for (int t = 0; t < dk; ++t) {
+    // Early exit, result-neutral: partial sums never decrease along the dims (fma(d, d, acc)
+    // >= acc in round-to-nearest), so once every pair this warp holds is above the largest
+    // eps^2 no code can change; the warp skips the remaining dims of the tile (the reference's
+    // generic kernel breaks the same way per pair, eps_neighborhood.cuh:247).
+    auto step = [&](int t) {
       uint64_t a[8];
       // (a, a) operand pairs for the 8 rows; (b, b') pairs come straight from 16-byte loads
       const float4 f0 = *reinterpret_cast<const float4*>(As + t * kTile + ty * 4);
@@ -180,6 +190,28 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
       for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = sqacc2(sub2(a[i], b[j]), acc[i][j]);
+    };
+    for (int t0 = 0; t0 < dk && !warp_done; t0 += kProbeDims) {
+      const int tn = min(kProbeDims, dk - t0);
+      if (tn == kProbeDims) {
+#pragma unroll
+        for (int u = 0; u < kProbeDims; ++u) step(t0 + u);
+      } else {
+        for (int u = 0; u < tn; ++u) step(t0 + u);
+      }
+      dims_done += tn;
+      if (t0 + tn < dk || !last_chunk) {
+        float mn = INFINITY;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float lo, hi;
+            unpack2(acc[i][j], lo, hi);
+            mn = fminf(mn, fminf(lo, hi));
+          }
+        warp_done = __all_sync(0xffffffffu, mn > cutoff);
+      }
     }
 
     if (last_chunk) {
@@ -273,6 +305,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
     stage ^= 1;
     chunk = last_chunk ? 0 : chunk + 1;
   }
+  if (lane == 0 && dims_done) atomicAdd(p.counters + 2, static_cast<unsigned long long>(dims_done));
 }
 
 // X (n x d, row-major) -> XT (dp x npad, dim-major), zero padded.

@@ -97,6 +97,7 @@ class Stats(ctypes.Structure):
         ("ms_graph", ctypes.c_double),
         ("ms_label", ctypes.c_double),
         ("ms_relabel", ctypes.c_double),
+        ("dist_work_fraction", ctypes.c_double),
     ]
 
     def as_dict(self) -> dict[str, Any]:
