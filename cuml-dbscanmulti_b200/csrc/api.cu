@@ -34,14 +34,19 @@
 namespace dbm {
 
 static std::atomic<int64_t> g_launches{0};
+constexpr int64_t kOrderMinPoints = 4096;  // below this the spatial ordering does not pay
 int64_t count_launch(int64_t n) { return g_launches.fetch_add(n) + n; }
 int64_t launches_so_far() { return g_launches.load(); }
 
 // launchers defined in dist.cu / graph.cu / cc.cu
 Status launch_distance(const DistLaunch& a, cudaStream_t s);
-Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s);
+Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s,
+                     const int32_t* perm = nullptr);
 int32_t padded_dims(int32_t d);
 int64_t padded_points(int64_t n);
+size_t order_scratch_bytes(int64_t n);
+Status spatial_order(const float* x, int64_t n, int32_t d, int32_t* perm, void* scratch, size_t scratch_bytes,
+                     cudaStream_t s);
 Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
                       int32_t* deg, int32_t* corecnt, int32_t* rowcnt, uint8_t* core_out,
                       cudaStream_t s);
@@ -184,6 +189,7 @@ struct dbm_handle {
   uint64_t edge_cap_hint = 0;
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
+  dbm::Buffer perm, order_scratch;
   dbm::Buffer xdev, labels_dev, core_dev;  // host-buffer entry point only
   int64_t* pinned = nullptr;               // small D2H staging
   size_t pinned_count = 0;
@@ -192,7 +198,8 @@ struct dbm_handle {
   {
     const dbm::Buffer* all[] = {&xt, &hist, &deg, &cc, &rowcnt, &off, &fill, &edges, &col, &crow,
                                 &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
-                                &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz};
+                                &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz,
+                                &perm, &order_scratch};
     uint64_t s = 0;
     for (auto* b : all) s += b->bytes;
     return s;
@@ -374,7 +381,16 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
   DBM_TRY(ensure_pinned(h, 16));
   DBM_CUDA(cudaMemsetAsync(h->err.p, 0, 16, s));
   PhaseTimer t(h, s, &st.ms_distance);
-  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s));
+  // Z-order of the leading coordinates makes tiles spatially coherent, which lets whole warps
+  // stop early in the distance kernel; results do not depend on the order.
+  const int32_t* perm = nullptr;
+  if (n >= kOrderMinPoints) {
+    DBM_TRY(ensure(h->perm, sizeof(int32_t) * n));
+    DBM_TRY(ensure(h->order_scratch, order_scratch_bytes(n)));
+    DBM_TRY(spatial_order(x, n, di, as<int32_t>(h->perm), h->order_scratch.p, h->order_scratch.bytes, s));
+    perm = as<int32_t>(h->perm);
+  }
+  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, perm));
   uint64_t cap = std::max<uint64_t>(h->edge_cap_hint, cap_hint);
   uint64_t found = 0;
   for (int pass = 0; pass < 2; ++pass) {
@@ -383,7 +399,7 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     DBM_CUDA(cudaMemsetAsync(hist, 0, sizeof(int32_t) * kn, s));
     DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 4 * sizeof(unsigned long long), s));
     DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
-                 as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards};
+                 as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards, perm};
     DBM_TRY(launch_distance(a, s));
     st.distance_passes = pass + 1;
     h->pinned[0] = 0;
@@ -672,7 +688,7 @@ void dbm_destroy(dbm_handle* h)
                         &h->col, &h->crow, &h->minpts, &h->counters, &h->err, &h->slab_counts,
                         &h->slab_off, &h->slab_col, &h->slab_row, &h->G, &h->L, &h->best, &h->cur,
                         &h->flags, &h->rank, &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev,
-                        &h->core_dev};
+                        &h->core_dev, &h->perm, &h->order_scratch};
   for (auto* b : all)
     if (b->p) cudaFree(b->p);
   if (h->pinned) cudaFreeHost(h->pinned);

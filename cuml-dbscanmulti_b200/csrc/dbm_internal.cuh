@@ -164,6 +164,7 @@ struct DistLaunch {
   int sm_count;
   int shard = 0;                   // evaluate the shard-th of nshards equal tile-pair ranges
   int nshards = 1;
+  const int32_t* perm = nullptr;   // XT column r holds point perm[r] (nullptr: identity)
 };
 
 // ---- kernel launch accounting (host) --------------------------------------------------------

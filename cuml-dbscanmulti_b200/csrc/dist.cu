@@ -53,6 +53,7 @@ struct DistParams {
   int32_t* err;
   const float* xt;                   // dp x npad (for re-evaluating neighbour pairs)
   int64_t npad;
+  const int32_t* perm;               // original index of each XT column (nullptr: identity)
   float eps2[kMaxEps];
 };
 
@@ -287,13 +288,19 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
           }
           int code = 0;
           while (w > s_eps2[code]) ++code;  // terminates: w <= eps2[k-1]
+          int32_t oi = gi, oj = gj;  // original point indices
+          if (p.perm) {
+            oi = p.perm[gi];
+            oj = p.perm[gj];
+          }
+          const int32_t lo = min(oi, oj), hi = max(oi, oj);
           if (idx < p.edge_cap)
-            p.edges[idx] = (static_cast<uint64_t>(gi) << 32) |
-                           (static_cast<uint64_t>(code) << kCodeShift) | static_cast<uint64_t>(gj);
+            p.edges[idx] = (static_cast<uint64_t>(lo) << 32) |
+                           (static_cast<uint64_t>(code) << kCodeShift) | static_cast<uint64_t>(hi);
           ++idx;
           int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
-          atomicAdd(hrow + gi, 1);
-          atomicAdd(hrow + gj, 1);
+          atomicAdd(hrow + oi, 1);
+          atomicAdd(hrow + oj, 1);
         }
       }
 #pragma unroll
@@ -311,7 +318,8 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
 // X (n x d, row-major) -> XT (dp x npad, dim-major), zero padded.
 // Also flags NaN/Inf inputs, which the reference rejects before fitting (src/main.cu:1419-1423).
 __global__ void transpose_pad_kernel(const float* __restrict__ x, float* __restrict__ xt, int64_t n,
-                                     int32_t d, int32_t dp, int64_t npad, int32_t* __restrict__ err)
+                                     int32_t d, int32_t dp, int64_t npad, int32_t* __restrict__ err,
+                                     const int32_t* __restrict__ perm)
 {
   __shared__ float tile[32][33];
   const int64_t i0 = static_cast<int64_t>(blockIdx.x) * 32;
@@ -320,7 +328,8 @@ __global__ void transpose_pad_kernel(const float* __restrict__ x, float* __restr
   for (int r = threadIdx.y; r < 32; r += blockDim.y) {
     const int64_t i = i0 + r;
     const int32_t t = t0 + static_cast<int32_t>(threadIdx.x);
-    const float v = (i < n && t < d) ? x[i * d + t] : 0.0f;
+    const int64_t src = (perm && i < n) ? static_cast<int64_t>(perm[i]) : i;
+    const float v = (i < n && t < d) ? x[src * d + t] : 0.0f;
     bad |= !isfinite(v);
     tile[r][threadIdx.x] = v;
   }
@@ -352,13 +361,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn()
 int32_t padded_dims(int32_t d) { return (d + 3) / 4 * 4; }
 int64_t padded_points(int64_t n) { return (n + 3) / 4 * 4; }
 
-Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s)
+Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s,
+                     const int32_t* perm)
 {
   const int32_t dp = padded_dims(d);
   const int64_t npad = padded_points(n);
   dim3 grid(static_cast<unsigned>(ceil_div(npad, 32)), static_cast<unsigned>(ceil_div(dp, 32)));
   count_launch();
-  transpose_pad_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xt, n, d, dp, npad, err);
+  transpose_pad_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xt, n, d, dp, npad, err, perm);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
@@ -402,6 +412,7 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   p.err = a.err;
   p.xt = a.xt;
   p.npad = npad;
+  p.perm = a.perm;
   for (int e = 0; e < kMaxEps; ++e) p.eps2[e] = e < a.k ? a.eps2[e] : a.eps2[a.k - 1];
 
   const size_t smem = dist_smem_bytes(dbox);
