@@ -30,7 +30,6 @@ import argparse
 import json
 import os
 import sys
-import threading
 import time
 from pathlib import Path
 
@@ -78,61 +77,67 @@ def make_points(cfg: dict, seed: int = 0) -> np.ndarray:
     return pts
 
 
-# ---- clocks during the timed region (NVML reads only) -------------------------------------------
+# ---- clocks during the timed region: a separate nvidia-smi process (reads only) ----------------
 class ClockSampler:
+    """Samples SM clocks and throttle reasons every 50 ms in a child nvidia-smi process, so the
+    sampling never competes with this process for the interpreter lock."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,utilization.gpu,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
     def __init__(self, device: int):
-        self.samples, self.reasons, self.ok = [], set(), False
-        self.max_mhz = None
-        try:
-            import pynvml
+        import shutil
+        import tempfile
 
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.hdl = pynvml.nvmlDeviceGetHandleByIndex(device)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.hdl, pynvml.NVML_CLOCK_SM)
-            self.ok = True
-        except Exception:
-            self.ok = False
-        self._stop = threading.Event()
-        self._t = None
-
-    def _run(self):
-        nv = self.nv
-        names = {
-            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
-            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
-            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
-            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
-            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
-        }
-        while not self._stop.is_set():
-            try:
-                mhz = nv.nvmlDeviceGetClockInfo(self.hdl, nv.NVML_CLOCK_SM)
-                util = nv.nvmlDeviceGetUtilizationRates(self.hdl).gpu
-                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.hdl)
-                if util > 50:
-                    self.samples.append(mhz)
-                    for k, bit in names.items():
-                        if mask & bit:
-                            self.reasons.add(k)
-            except Exception:
-                pass
-            time.sleep(0.1)
+        self.device = device
+        self.proc = None
+        self.path = None
+        self.smi = shutil.which("nvidia-smi")
+        self.tmp = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
 
     def start(self):
-        if self.ok:
-            self._t = threading.Thread(target=self._run, daemon=True)
-            self._t.start()
+        import subprocess
+
+        if not self.smi:
+            return
+        self.proc = subprocess.Popen([self.smi, "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits", "-lms", "50"],
+                                     stdout=self.tmp, stderr=subprocess.DEVNULL)
 
     def stop(self) -> dict:
-        if not self.ok:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml-unavailable"]}
-        self._stop.set()
-        if self._t:
-            self._t.join()
-        med = float(np.median(self.samples)) if self.samples else None
-        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                "samples_under_load": len(self.samples)}
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi-unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.tmp.flush()
+        self.tmp.seek(0)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        clocks, reasons, max_mhz, rows = [], set(), None, 0
+        for line in self.tmp.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                mhz, mx, util = float(parts[0]), float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            rows += 1
+            max_mhz = mx
+            if util > 50:
+                clocks.append(mhz)
+                for nm, flag in zip(names, parts[3:7]):
+                    if flag.lower() == "active":
+                        reasons.add(nm)
+        try:
+            os.unlink(self.tmp.name)
+        except OSError:
+            pass
+        return {"sm_mhz": float(np.median(clocks)) if clocks else None, "sm_max_mhz": max_mhz,
+                "reasons": sorted(reasons), "samples_under_load": len(clocks), "samples": rows}
 
 
 def measured_peaks() -> dict:
@@ -276,8 +281,8 @@ def run_reference(args, cfg) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c4", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

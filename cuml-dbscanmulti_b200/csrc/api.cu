@@ -45,6 +45,13 @@ Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* e
 int32_t padded_dims(int32_t d);
 int64_t padded_points(int64_t n);
 size_t order_scratch_bytes(int64_t n);
+int64_t prune_blocks(int64_t pairs);
+Status launch_tile_boxes(const float* xt, int64_t n, int64_t npad, int32_t d, float* lo, float* hi, cudaStream_t s);
+Status launch_prune_count(int64_t pairs, const float* lo, const float* hi, int32_t d, float cutoff,
+                          int32_t* counts, int64_t* offsets, void* scan_scratch, size_t scan_bytes,
+                          cudaStream_t s);
+Status launch_prune_write(int64_t pairs, const float* lo, const float* hi, int32_t d, float cutoff,
+                          const int64_t* offsets, long long* work, cudaStream_t s);
 Status spatial_order(const float* x, int64_t n, int32_t d, int32_t* perm, void* scratch, size_t scratch_bytes,
                      cudaStream_t s);
 Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
@@ -54,6 +61,8 @@ Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, 
                           uint32_t* col, int32_t* row, cudaStream_t s);
 Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, int64_t* out,
                         cudaStream_t s);
+Status launch_label_range(const int32_t* labels, int64_t total, int64_t n, unsigned long long* first_bad,
+                          int sm_count, cudaStream_t s);
 Status launch_slab_counts(const int32_t* deg_e, int64_t s0, int64_t rows, int32_t* counts,
                           cudaStream_t s);
 Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int e,
@@ -189,7 +198,7 @@ struct dbm_handle {
   uint64_t edge_cap_hint = 0;
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
-  dbm::Buffer perm, order_scratch;
+  dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_counts, prune_off, work;
   dbm::Buffer xdev, labels_dev, core_dev;  // host-buffer entry point only
   int64_t* pinned = nullptr;               // small D2H staging
   size_t pinned_count = 0;
@@ -199,7 +208,8 @@ struct dbm_handle {
     const dbm::Buffer* all[] = {&xt, &hist, &deg, &cc, &rowcnt, &off, &fill, &edges, &col, &crow,
                                 &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
                                 &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz,
-                                &perm, &order_scratch};
+                                &perm, &order_scratch, &box_lo, &box_hi, &prune_counts, &prune_off,
+                                &work};
     uint64_t s = 0;
     for (auto* b : all) s += b->bytes;
     return s;
@@ -391,6 +401,35 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     perm = as<int32_t>(h->perm);
   }
   DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, perm));
+  // Exact tile-pair pruning by per-tile bounding boxes (prune.cu): only tile pairs that may hold
+  // a neighbour pair are evaluated.  Every rank builds the same worklist and takes its slice.
+  const int64_t T = ceil_div(n, 128);
+  const int64_t pairs = T * (T + 1) / 2;
+  const long long* work = nullptr;
+  int64_t work_count = 0;
+  if (perm) {
+    const int64_t nb = prune_blocks(pairs);
+    DBM_TRY(ensure(h->box_lo, sizeof(float) * static_cast<size_t>(T) * di));
+    DBM_TRY(ensure(h->box_hi, sizeof(float) * static_cast<size_t>(T) * di));
+    DBM_TRY(ensure(h->prune_counts, sizeof(int32_t) * nb));
+    DBM_TRY(ensure(h->prune_off, sizeof(int64_t) * (nb + 1)));
+    DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(nb + 1)));
+    DBM_TRY(launch_tile_boxes(as<float>(h->xt), n, padded_points(n), di, as<float>(h->box_lo), as<float>(h->box_hi), s));
+    DBM_TRY(launch_prune_count(pairs, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1],
+                               as<int32_t>(h->prune_counts), as<int64_t>(h->prune_off), h->scan_scratch.p,
+                               h->scan_scratch.bytes, s));
+    h->pinned[0] = 0;
+    DBM_CUDA(cudaMemcpyAsync(h->pinned, as<int64_t>(h->prune_off) + nb, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    DBM_CUDA(cudaStreamSynchronize(s));
+    work_count = h->pinned[0];
+    DBM_TRY(ensure(h->work, sizeof(long long) * std::max<int64_t>(work_count, 1)));
+    DBM_TRY(launch_prune_write(pairs, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1],
+                               as<int64_t>(h->prune_off), as<long long>(h->work), s));
+    work = as<long long>(h->work);
+    st.tile_pairs_kept = pairs > 0 ? static_cast<double>(work_count) / static_cast<double>(pairs) : 1.0;
+  } else {
+    st.tile_pairs_kept = 1.0;
+  }
   uint64_t cap = std::max<uint64_t>(h->edge_cap_hint, cap_hint);
   uint64_t found = 0;
   for (int pass = 0; pass < 2; ++pass) {
@@ -399,7 +438,8 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     DBM_CUDA(cudaMemsetAsync(hist, 0, sizeof(int32_t) * kn, s));
     DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 4 * sizeof(unsigned long long), s));
     DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
-                 as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards, perm};
+                 as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards, perm,
+                 work, work_count};
     DBM_TRY(launch_distance(a, s));
     st.distance_passes = pass + 1;
     h->pinned[0] = 0;
@@ -412,11 +452,9 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     DBM_CUDA(cudaStreamSynchronize(s));
     found = static_cast<uint64_t>(h->pinned[0]);
     {
-      // 8 warps per 128 x 128 tile, each evaluating up to d dims for its 16 x 128 pairs
-      const int64_t T = ceil_div(n, 128);
-      const int64_t pairs = T * (T + 1) / 2;
-      const int64_t tiles = pairs * (shard + 1) / nshards - pairs * shard / nshards;
-      const double full = static_cast<double>(tiles) * 8.0 * static_cast<double>(d);
+      // 8 warps per 128 x 128 tile, each evaluating up to d dims for its 16 x 128 pairs; the
+      // reference is this shard's share of all tile pairs (pruned ones count as zero)
+      const double full = static_cast<double>(pairs) / nshards * 8.0 * static_cast<double>(d);
       st.dist_work_fraction = full > 0 ? static_cast<double>(h->pinned[2]) / full : 1.0;
     }
     if (h->pinned[1] & kErrNonFinite) return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
@@ -688,7 +726,8 @@ void dbm_destroy(dbm_handle* h)
                         &h->col, &h->crow, &h->minpts, &h->counters, &h->err, &h->slab_counts,
                         &h->slab_off, &h->slab_col, &h->slab_row, &h->G, &h->L, &h->best, &h->cur,
                         &h->flags, &h->rank, &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev,
-                        &h->core_dev, &h->perm, &h->order_scratch};
+                        &h->core_dev, &h->perm, &h->order_scratch, &h->box_lo, &h->box_hi,
+                        &h->prune_counts, &h->prune_off, &h->work};
   for (auto* b : all)
     if (b->p) cudaFree(b->p);
   if (h->pinned) cudaFreeHost(h->pinned);
@@ -767,21 +806,29 @@ int dbm_fit_multi_host(dbm_handle* h, const float* x_host, int64_t n, int64_t d,
                          core_host ? static_cast<uint8_t*>(h->core_dev.p) : nullptr, opt, stats,
                          batch_routes, routes_len, h->stream, err, err_len);
   if (rc != DBM_OK) return rc;
-  if (cudaMemcpyAsync(labels_host, h->labels_dev.p, lb, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess ||
+  // range check on the device (-1 <= label < n), then the copies back
+  const size_t total = static_cast<size_t>(n) * k * l;
+  unsigned long long* first_bad = dbm::as<unsigned long long>(h->counters) + 3;
+  if (cudaMemsetAsync(first_bad, 0xff, sizeof(unsigned long long), h->stream) != cudaSuccess ||
+      !dbm::launch_label_range(static_cast<const int32_t*>(h->labels_dev.p), static_cast<int64_t>(total), n,
+                               first_bad, h->sm_count, h->stream).ok()) {
+    dbm::set_err(err, err_len, "label range check failed to launch");
+    return DBM_ERR_CUDA;
+  }
+  unsigned long long bad = 0;
+  if (cudaMemcpyAsync(&bad, first_bad, sizeof bad, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess ||
+      cudaMemcpyAsync(labels_host, h->labels_dev.p, lb, cudaMemcpyDeviceToHost, h->stream) != cudaSuccess ||
       (core_host && cudaMemcpyAsync(core_host, h->core_dev.p, static_cast<size_t>(n) * k * l,
                                     cudaMemcpyDeviceToHost, h->stream) != cudaSuccess) ||
       cudaStreamSynchronize(h->stream) != cudaSuccess) {
     dbm::set_err(err, err_len, "device-to-host copy of the labels failed");
     return DBM_ERR_CUDA;
   }
-  const size_t total = static_cast<size_t>(n) * k * l;
-  for (size_t i = 0; i < total; ++i) {
-    if (labels_host[i] < -1 || labels_host[i] >= n) {
-      dbm::set_err(err, err_len, "invalid CUDA label at position " + std::to_string(i) + ": " +
-                                   std::to_string(labels_host[i]) + " (expected -1 <= label < " +
-                                   std::to_string(n) + ")");
-      return DBM_ERR_CUDA;
-    }
+  if (bad != ~0ull) {
+    dbm::set_err(err, err_len, "invalid CUDA label at position " + std::to_string(bad) + ": " +
+                                 std::to_string(labels_host[bad]) + " (expected -1 <= label < " +
+                                 std::to_string(n) + ")");
+    return DBM_ERR_CUDA;
   }
   return DBM_OK;
 }

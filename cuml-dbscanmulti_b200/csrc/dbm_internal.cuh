@@ -165,6 +165,8 @@ struct DistLaunch {
   int shard = 0;                   // evaluate the shard-th of nshards equal tile-pair ranges
   int nshards = 1;
   const int32_t* perm = nullptr;   // XT column r holds point perm[r] (nullptr: identity)
+  const long long* work = nullptr; // surviving tile pairs (nullptr: every tile pair)
+  int64_t work_count = 0;
 };
 
 // ---- kernel launch accounting (host) --------------------------------------------------------

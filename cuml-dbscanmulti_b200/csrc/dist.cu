@@ -44,8 +44,9 @@ struct DistParams {
   int32_t k;
   int32_t dbox;                      // dims per box actually used (<= kDimBox)
   int32_t nchunks;                   // ceil(d / dbox)
-  int64_t tile_begin;                // this launch's share of the T(T+1)/2 tile pairs
-  int64_t tile_end;
+  int64_t item_begin;                // this launch's share [item_begin, item_begin + item_count)
+  int64_t item_count;                // of the work items: tile pairs, or worklist entries
+  const long long* work;             // worklist of tile-pair indices (nullptr: item = tile pair)
   unsigned long long* counters;      // [0] edge cursor, [1] next tile pair
   uint64_t* edges;
   uint64_t edge_cap;
@@ -107,7 +108,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   float* As1 = Bs0 + box_floats;
   float* Bs1 = As1 + box_floats;
   __shared__ __align__(8) uint64_t full[2];
-  __shared__ long long s_tile[2];  // tile pair index held by each stage (>= tile_end: none)
+  __shared__ long long s_tile[2];  // tile pair index held by each stage (< 0: none)
   __shared__ float s_eps2[kMaxEps];
 
   const int tid = threadIdx.x;
@@ -116,10 +117,15 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   if (tid < kMaxEps) s_eps2[tid] = p.eps2[tid];
   const uint32_t box_bytes = static_cast<uint32_t>(box_floats) * sizeof(float);
 
+  auto next_tile = [&]() -> long long {
+    const long long i = static_cast<long long>(atomicAdd(p.counters + 1, 1ULL));
+    if (i >= p.item_count) return -1;
+    return p.work ? p.work[p.item_begin + i] : p.item_begin + i;
+  };
   auto issue = [&](int stage, long long tile, int chunk) {
     // one thread: record the item and start both tile loads of this stage
     s_tile[stage] = tile;
-    if (tile >= p.tile_end) return;
+    if (tile < 0) return;
     long long I, J;
     tri_coords(tile, I, J);
     fence_proxy_async_smem();
@@ -134,7 +140,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
     mbar_init(&full[0], 1);
     mbar_init(&full[1], 1);
     mbar_fence_init();
-    issue(0, p.tile_begin + static_cast<long long>(atomicAdd(p.counters + 1, 1ULL)), 0);
+    issue(0, next_tile(), 0);
   }
   __syncthreads();
 
@@ -152,7 +158,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   long long dims_done = 0;     // dims this warp evaluated, over all its tiles
   for (;;) {
     const long long c = s_tile[stage];
-    if (c >= p.tile_end) break;
+    if (c < 0) break;
     if (chunk == 0) warp_done = false;
     const bool ok = mbar_wait_bounded(&full[stage], phase[stage], kWaitPolls);
     if (__syncthreads_or(!ok)) {
@@ -168,7 +174,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
       if (!last_chunk)
         issue(stage ^ 1, c, chunk + 1);
       else
-        issue(stage ^ 1, p.tile_begin + static_cast<long long>(atomicAdd(p.counters + 1, 1ULL)), 0);
+        issue(stage ^ 1, next_tile(), 0);
     }
     const float* As = stage ? As1 : As0;
     const float* Bs = stage ? Bs1 : Bs0;
@@ -401,10 +407,11 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   p.dbox = dbox;
   p.nchunks = static_cast<int32_t>(ceil_div(a.d, dbox));
   const int64_t T = ceil_div(a.n, kTile);
-  const int64_t pairs = T * (T + 1) / 2;
+  const int64_t items = a.work ? a.work_count : T * (T + 1) / 2;
   const int shards = a.nshards > 0 ? a.nshards : 1;
-  p.tile_begin = pairs * a.shard / shards;
-  p.tile_end = pairs * (a.shard + 1) / shards;
+  p.item_begin = items * a.shard / shards;
+  p.item_count = items * (a.shard + 1) / shards - p.item_begin;
+  p.work = a.work;
   p.counters = a.counters;
   p.edges = a.edges;
   p.edge_cap = a.edge_cap;
@@ -423,7 +430,7 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
                                                          smem));
   if (per_sm < 1) per_sm = 1;
   int64_t grid = static_cast<int64_t>(a.sm_count) * per_sm;
-  if (grid > p.tile_end - p.tile_begin) grid = p.tile_end - p.tile_begin;
+  if (grid > p.item_count) grid = p.item_count;
   if (grid < 1) return Status::Ok();
   count_launch();
   dist_tri_kernel<<<static_cast<unsigned>(grid), kDistThreads, smem, s>>>(map, p);

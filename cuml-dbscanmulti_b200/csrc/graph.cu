@@ -16,6 +16,8 @@
 //   batch_nnz_kernel     per-batch nnz at the largest eps (runner_multi.cuh:898-904).
 #include "dbm_internal.cuh"
 
+#include <algorithm>
+
 namespace dbm {
 
 // ---- scan ---------------------------------------------------------------------------------
@@ -278,6 +280,27 @@ Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_
   count_launch();
   filter_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(
     off, col, s0, rows, static_cast<uint32_t>(e), off_e, col_e, row_e);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// Label range check on the device (-1 <= label < n, src/main.cu:589-597): first bad position.
+__global__ void label_range_kernel(const int32_t* __restrict__ labels, int64_t total, int64_t n,
+                                   unsigned long long* __restrict__ first_bad)
+{
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t v = labels[i];
+    if (v < -1 || v >= n) atomicMin(first_bad, static_cast<unsigned long long>(i));
+  }
+}
+
+Status launch_label_range(const int32_t* labels, int64_t total, int64_t n, unsigned long long* first_bad,
+                          int sm_count, cudaStream_t s)
+{
+  count_launch();
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(total, 256), int64_t(sm_count) * 8));
+  label_range_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(labels, total, n, first_bad);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }

@@ -98,6 +98,7 @@ class Stats(ctypes.Structure):
         ("ms_label", ctypes.c_double),
         ("ms_relabel", ctypes.c_double),
         ("dist_work_fraction", ctypes.c_double),
+        ("tile_pairs_kept", ctypes.c_double),
     ]
 
     def as_dict(self) -> dict[str, Any]:
@@ -324,8 +325,7 @@ class DbscanMulti:
             xh = np.ascontiguousarray(x, dtype=np.float32)
             if xh.ndim != 2:
                 raise DbmError(-1, "x must be two-dimensional")
-            if not np.all(np.isfinite(xh)):
-                raise DbmError(-10, "the input contains NaN or infinity")
+            # NaN/Inf are detected on the device (DBM_ERR_NONFINITE)
             n, d = xh.shape
             maxb = n + 1
             routes = (ctypes.c_uint8 * maxb)()

@@ -101,9 +101,10 @@ typedef struct dbm_stats {
   double ms_graph;              /* degrees, masks, CSR build */
   double ms_label;              /* per-batch compaction, connected components, merge */
   double ms_relabel;            /* final relabel */
-  double dist_work_fraction;    /* fraction of the pair-dims of the evaluated tiles that the
-                                   distance kernel computed (warps whose pairs all exceed the
-                                   largest eps stop early; 1.0 = no early exit) */
+  double dist_work_fraction;    /* fraction of all pair-dims (this shard's share of the tile
+                                   pairs x D) the distance kernel computed: pruned tile pairs
+                                   and warps whose pairs all exceed the largest eps stop early */
+  double tile_pairs_kept;       /* fraction of tile pairs that survived the bounding-box bound */
 } dbm_stats;
 
 typedef struct dbm_handle dbm_handle;
