@@ -63,15 +63,16 @@ Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, i
                         cudaStream_t s);
 Status launch_label_range(const int32_t* labels, int64_t total, int64_t n, unsigned long long* first_bad,
                           int sm_count, cudaStream_t s);
-Status launch_slab_counts(const int32_t* deg_e, int64_t s0, int64_t rows, int32_t* counts,
-                          cudaStream_t s);
-Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int e,
-                     const int64_t* off_e, int32_t* col_e, int32_t* row_e, cudaStream_t s);
 Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigned long long* best,
                       cudaStream_t s);
-Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, int m_lo, int m_hi, const int32_t* cc_e,
-                       bool single_batch, int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur,
-                       uint32_t tag, int32_t* err, int sm_count, cudaStream_t s);
+Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int k, int l, int cfg_begin,
+                       int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
+                       unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
+                       cudaStream_t s);
+Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0, int64_t rows, int32_t* counts,
+                              cudaStream_t s);
+Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int ne,
+                         const int64_t* off_flat, int32_t* col_flat, int32_t* row_flat, cudaStream_t s);
 Status launch_cc_roots(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
                        int32_t* flags, cudaStream_t s);
 Status launch_cc_labels(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
@@ -195,6 +196,11 @@ struct dbm_handle {
   bool own_stream = false;
   int sm_count = 148;
   bool timing = false;
+  struct PendingTimer {
+    cudaEvent_t a, b;
+    double* out;
+  };
+  std::vector<PendingTimer> pending_timers;  // phase events read after the call's final sync
   uint64_t edge_cap_hint = 0;
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
@@ -238,6 +244,8 @@ static Status ensure_pinned(dbm_handle* h, size_t count)
   return Status::Ok();
 }
 
+// Phase timing without extra synchronisation: events are recorded around a phase and read
+// back after the call's final stream sync (resolve_phase_timers).
 struct PhaseTimer {
   dbm_handle* h;
   cudaStream_t s;
@@ -246,22 +254,31 @@ struct PhaseTimer {
   PhaseTimer(dbm_handle* h_, cudaStream_t s_, double* out_) : h(h_), s(s_), out(out_)
   {
     if (!h->timing || !out) return;
-    cudaEventCreate(&a);
-    cudaEventCreate(&b);
+    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) {
+      a = b = nullptr;
+      return;
+    }
     cudaEventRecord(a, s);
   }
   ~PhaseTimer()
   {
     if (!a) return;
     cudaEventRecord(b, s);
-    cudaEventSynchronize(b);
-    float ms = 0;
-    cudaEventElapsedTime(&ms, a, b);
-    *out += ms;
-    cudaEventDestroy(a);
-    cudaEventDestroy(b);
+    h->pending_timers.push_back({a, b, out});
   }
 };
+
+static void resolve_phase_timers(dbm_handle* h)
+{
+  for (auto& t : h->pending_timers) {
+    float ms = 0;
+    if (cudaEventSynchronize(t.b) == cudaSuccess && cudaEventElapsedTime(&ms, t.a, t.b) == cudaSuccess)
+      *t.out += ms;
+    cudaEventDestroy(t.a);
+    cudaEventDestroy(t.b);
+  }
+  h->pending_timers.clear();
+}
 
 static Status validate(int64_t n, int64_t d, const float* eps, int k, const int32_t* minpts, int l)
 {
@@ -590,11 +607,13 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
     DBM_TRY(ensure(h->cur, sizeof(int32_t) * kln));
     DBM_TRY(ensure(h->best, sizeof(unsigned long long) * kln));
     if (nb > 1) DBM_TRY(ensure(h->L, sizeof(int32_t) * kln));
-    if (k > 1) {
-      DBM_TRY(ensure(h->slab_counts, sizeof(int32_t) * bs));
-      DBM_TRY(ensure(h->slab_off, sizeof(int64_t) * (bs + 1)));
-      DBM_TRY(ensure(h->slab_col, sizeof(int32_t) * std::max<int64_t>(max_slab, 1)));
-      DBM_TRY(ensure(h->slab_row, sizeof(int32_t) * std::max<int64_t>(max_slab, 1)));
+    const int ne = k - 1;  // smaller eps, compacted on the annotated route
+    if (ne > 0) {
+      DBM_TRY(ensure(h->slab_counts, sizeof(int32_t) * bs * ne));
+      DBM_TRY(ensure(h->slab_off, sizeof(int64_t) * (bs * ne + 1)));
+      DBM_TRY(ensure(h->slab_col, sizeof(int32_t) * std::max<int64_t>(max_slab * ne, 1)));
+      DBM_TRY(ensure(h->slab_row, sizeof(int32_t) * std::max<int64_t>(max_slab * ne, 1)));
+      DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(static_cast<int64_t>(bs) * ne + 1)));
     }
     DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur), as<unsigned long long>(h->best), s));
     int64_t base = 0;  // first max-eps CSR entry of the batch
@@ -603,32 +622,37 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
       const int64_t rows = std::min<int64_t>(n - s0, static_cast<int64_t>(bs));
       const int64_t count = bnnz[b] - rows;  // entries without the self pairs
       const uint32_t tag = static_cast<uint32_t>(nb - 1 - b);
-      for (int e = 0; e < k; ++e) {
-        const int m_lo = std::max(0, std::min(l, cfg_begin - e * l));
-        const int m_hi = std::max(0, std::min(l, cfg_end - e * l));
-        if (m_lo >= m_hi) continue;
-        Slab sl;
-        if (e == k - 1) {
-          sl.row = as<int32_t>(h->crow) + base;
-          sl.col = reinterpret_cast<const int32_t*>(h->col.p) + base;
-          sl.count = count;
-          sl.count_dev = nullptr;
-        } else {
-          DBM_TRY(launch_slab_counts(as<int32_t>(h->deg) + static_cast<int64_t>(e) * n, s0, rows,
-                                     as<int32_t>(h->slab_counts), s));
-          DBM_TRY(exclusive_scan_i32(as<int32_t>(h->slab_counts), as<int64_t>(h->slab_off), rows,
-                                     h->scan_scratch.p, h->scan_scratch.bytes, s));
-          DBM_TRY(launch_filter(as<int64_t>(h->off), as<uint32_t>(h->col), s0, rows, e,
-                                as<int64_t>(h->slab_off), as<int32_t>(h->slab_col), as<int32_t>(h->slab_row), s));
-          sl.row = as<int32_t>(h->slab_row);
-          sl.col = as<int32_t>(h->slab_col);
-          sl.count = count;                                // upper bound for the launch size
-          sl.count_dev = as<int64_t>(h->slab_off) + rows;  // exact, read on the device
+      SlabRef max_eps;
+      max_eps.row = as<int32_t>(h->crow) + base;
+      max_eps.col = reinterpret_cast<const int32_t*>(h->col.p) + base;
+      max_eps.count = count;
+      MultiSlab ms;
+      if (routes[b] == DBM_BATCH_DENSE || ne == 0) {
+        // direct: eps membership straight from each max-eps entry's code, no per-eps copies
+        ms.direct = 1;
+        ms.nslabs = 1;
+        ms.s[0] = max_eps;
+      } else {
+        // annotated: one pass compacts every smaller eps (order-preserving), then all slabs
+        DBM_TRY(launch_slab_counts_all(as<int32_t>(h->deg), n, ne, s0, rows, as<int32_t>(h->slab_counts), s));
+        DBM_TRY(exclusive_scan_i32(as<int32_t>(h->slab_counts), as<int64_t>(h->slab_off), rows * ne,
+                                   h->scan_scratch.p, h->scan_scratch.bytes, s));
+        DBM_TRY(launch_filter_all(as<int64_t>(h->off), as<uint32_t>(h->col), s0, rows, ne, as<int64_t>(h->slab_off),
+                                  as<int32_t>(h->slab_col), as<int32_t>(h->slab_row), s));
+        ms.direct = 0;
+        ms.nslabs = k;
+        for (int e = 0; e < ne; ++e) {
+          ms.s[e].row = as<int32_t>(h->slab_row);
+          ms.s[e].col = as<int32_t>(h->slab_col);
+          ms.s[e].count = count;
+          ms.s[e].begin_dev = as<int64_t>(h->slab_off) + static_cast<int64_t>(e) * rows;
+          ms.s[e].end_dev = as<int64_t>(h->slab_off) + static_cast<int64_t>(e + 1) * rows;
         }
-        DBM_TRY(launch_cc_batch(sl, n, l, e, m_lo, m_hi, as<int32_t>(h->cc) + static_cast<int64_t>(e) * n,
-                                nb == 1, as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
-                                as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, s));
+        ms.s[ne] = max_eps;
       }
+      DBM_TRY(launch_cc_batch(ms, count, n, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc), nb == 1,
+                              as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
+                              as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, s));
       base += count;
     }
   }
@@ -764,6 +788,7 @@ int dbm_fit_multi(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) r = dbm::Status::Err(DBM_ERR_CUDA, cudaGetErrorString(e));
   }
+  dbm::resolve_phase_timers(h);
   if (stats) *stats = st;
   if (batch_routes && routes_len > 0) {
     for (int i = 0; i < routes_len; ++i)
@@ -854,6 +879,7 @@ int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, 
     std::memset(&st, 0, sizeof(st));
     uint64_t found = 0;
     r = dbm::distance_stage(h, x_dev, n, d, eps2, k, shard, nshards, hist_dev, edge_cap, &found, st, s);
+    dbm::resolve_phase_timers(h);
     if (r.ok()) {
       *edges_found = found;
       if (found <= edge_cap && found > 0) {
@@ -901,6 +927,7 @@ int dbm_fit_multi_from_graph(dbm_handle* h, int64_t n, int64_t d, const float* e
       if (e != cudaSuccess) r = dbm::Status::Err(DBM_ERR_CUDA, cudaGetErrorString(e));
     }
   }
+  dbm::resolve_phase_timers(h);
   st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
   if (stats) *stats = st;
   if (batch_routes && routes_len > 0)

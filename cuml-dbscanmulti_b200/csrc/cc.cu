@@ -38,81 +38,110 @@ __global__ void cc_init_kernel(int64_t n, int64_t total, int32_t* __restrict__ G
   best[x] = ~0ull;
 }
 
-// Edge-parallel slab iteration: grid-stride over the entries, bounded by the device-side
-// count when the slab was compacted on the device.
-#define DBM_SLAB_LOOP(sl, q)                                                              \
-  const int64_t lim_ = (sl).count_dev ? *(sl).count_dev : (sl).count;                   \
-  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < lim_; \
-       q += static_cast<int64_t>(gridDim.x) * blockDim.x)
+// ---- one batch, all eps at once ---------------------------------------------------------------
+// Each kernel walks every neighbour entry of the batch's rows once per eps it belongs to and does
+// its work for the minPts configs of that eps that this call owns ([cfg_begin, cfg_end)):
+//   annotated route: slab e holds the entries of eps e (compacted), e = 0..k-1;
+//   direct route:    slab 0 holds the max-eps entries with their codes (col >> 28), and an
+//                    entry belongs to every eps e >= its code (no per-eps copies).
+struct CcArgs {
+  MultiSlab ms;
+  int64_t n;
+  int k, l, cfg_begin, cfg_end;
+  const int32_t* cc;  // k x n: core iff m < cc[e*n + i]
+};
 
-// L[cfg][v] = v for both endpoints of every slab entry (configs where v is core).
-__global__ void cc_touch_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_hi,
-                                const int32_t* __restrict__ cc, int32_t* __restrict__ L)
+__device__ __forceinline__ void cfg_range(const CcArgs& a, int e, int& m_lo, int& m_hi)
 {
-  DBM_SLAB_LOOP(sl, q)
-  {
-    const int32_t r = sl.row[q];
-    const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
-    const int cr = min(cc[r], m_hi), cj = min(cc[j], m_hi);
-    for (int m = m_lo; m < cr; ++m) L[static_cast<int64_t>(cfg0 + m) * n + r] = r;
-    for (int m = m_lo; m < cj; ++m) L[static_cast<int64_t>(cfg0 + m) * n + j] = j;
+  m_lo = max(0, min(a.l, a.cfg_begin - e * a.l));
+  m_hi = max(0, min(a.l, a.cfg_end - e * a.l));
+}
+
+template <class F>
+__device__ __forceinline__ void for_each_entry(const CcArgs& a, F&& f)
+{
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (a.ms.direct) {
+    const SlabRef& s = a.ms.s[0];
+    for (int64_t q = t0; q < s.count; q += stride) {
+      const uint32_t w = static_cast<uint32_t>(s.col[q]);
+      const int32_t j = static_cast<int32_t>(w & kColMask);
+      const int32_t r = s.row[q];
+      for (int e = static_cast<int>(w >> kCodeShift); e < a.k; ++e) f(e, r, j);
+    }
+  } else {
+    for (int e = 0; e < a.ms.nslabs; ++e) {
+      const SlabRef& s = a.ms.s[e];
+      const int64_t b = s.begin_dev ? *s.begin_dev : 0;
+      const int64_t lim = s.end_dev ? *s.end_dev : s.count;
+      for (int64_t q = b + t0; q < lim; q += stride) f(e, s.row[q], s.col[q] & static_cast<int32_t>(kColMask));
+    }
   }
 }
 
-// unite(P[cfg], r, j) for every core-core slab entry
-__global__ void cc_union_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_hi,
-                                const int32_t* __restrict__ cc, int32_t* __restrict__ P,
-                                int32_t* __restrict__ err)
+// L[cfg][v] = v for both endpoints of every entry (configs where v is core).
+__global__ void cc_touch_kernel(const CcArgs a, int32_t* __restrict__ L)
+{
+  for_each_entry(a, [&](int e, int32_t r, int32_t j) {
+    int m_lo, m_hi;
+    cfg_range(a, e, m_lo, m_hi);
+    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
+    const int cr = min(cc[r], m_hi), cj = min(cc[j], m_hi);
+    for (int m = m_lo; m < cr; ++m) L[static_cast<int64_t>(e * a.l + m) * a.n + r] = r;
+    for (int m = m_lo; m < cj; ++m) L[static_cast<int64_t>(e * a.l + m) * a.n + j] = j;
+  });
+}
+
+// unite(P[cfg], r, j) for every core-core entry
+__global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t* __restrict__ err)
 {
   bool ok = true;
-  DBM_SLAB_LOOP(sl, q)
-  {
-    const int32_t r = sl.row[q];
-    const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
+  for_each_entry(a, [&](int e, int32_t r, int32_t j) {
+    int m_lo, m_hi;
+    cfg_range(a, e, m_lo, m_hi);
+    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
     const int mm = min(min(cc[r], cc[j]), m_hi);
-    for (int m = m_lo; m < mm; ++m) ok &= uf_unite(P + static_cast<int64_t>(cfg0 + m) * n, r, j);
-  }
+    for (int m = m_lo; m < mm; ++m) ok &= uf_unite(P + static_cast<int64_t>(e * a.l + m) * a.n, r, j);
+  });
   if (!ok) atomicOr(err, kErrUnionLimit);
 }
 
-// For every slab entry with exactly one core endpoint c: best[p] = min(tag << 32 | find(P, c)).
-__global__ void cc_best_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_hi,
-                               const int32_t* __restrict__ cc, int32_t* __restrict__ P,
-                               unsigned long long* __restrict__ best, uint32_t tag)
+// For every entry with exactly one core endpoint c: best[p] = min(tag << 32 | find(P, c)).
+__global__ void cc_best_kernel(const CcArgs a, int32_t* __restrict__ P, unsigned long long* __restrict__ best,
+                               uint32_t tag)
 {
-  DBM_SLAB_LOOP(sl, q)
-  {
-    const int32_t r = sl.row[q];
-    const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
+  for_each_entry(a, [&](int e, int32_t r, int32_t j) {
+    int m_lo, m_hi;
+    cfg_range(a, e, m_lo, m_hi);
+    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
     const int cr = cc[r], cj = cc[j];
     const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
     for (int m = lo; m < hi; ++m) {
       const bool r_core = m < cr;
       const int32_t c = r_core ? r : j;
       const int32_t pt = r_core ? j : r;
-      const int64_t base = static_cast<int64_t>(cfg0 + m) * n;
+      const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
       const int32_t root = uf_find(P + base, c);
-      atomicMin(best + base + pt,
-                (static_cast<unsigned long long>(tag) << 32) | static_cast<uint32_t>(root));
+      atomicMin(best + base + pt, (static_cast<unsigned long long>(tag) << 32) | static_cast<uint32_t>(root));
     }
-  }
+  });
 }
 
-// cur[p] = min(find(G, cur[p]), find(G, best[p])) for every border endpoint of the slab.
-__global__ void cc_border_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_hi,
-                                 const int32_t* __restrict__ cc, int32_t* __restrict__ G,
+// cur[p] = min(find(G, cur[p]), find(G, best[p])) for every border endpoint.
+__global__ void cc_border_kernel(const CcArgs a, int32_t* __restrict__ G,
                                  const unsigned long long* __restrict__ best, int32_t* __restrict__ cur,
                                  uint32_t tag)
 {
-  DBM_SLAB_LOOP(sl, q)
-  {
-    const int32_t r = sl.row[q];
-    const int32_t j = sl.col[q] & static_cast<int32_t>(kColMask);
+  for_each_entry(a, [&](int e, int32_t r, int32_t j) {
+    int m_lo, m_hi;
+    cfg_range(a, e, m_lo, m_hi);
+    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
     const int cr = cc[r], cj = cc[j];
     const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
     for (int m = lo; m < hi; ++m) {
       const int32_t pt = (m < cr) ? j : r;
-      const int64_t base = static_cast<int64_t>(cfg0 + m) * n;
+      const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
       const unsigned long long v = best[base + pt];
       if (static_cast<uint32_t>(v >> 32) != tag) continue;
       const int32_t cand = uf_find(G + base, static_cast<int32_t>(v & 0xffffffffu));
@@ -121,7 +150,7 @@ __global__ void cc_border_kernel(Slab sl, int64_t n, int cfg0, int m_lo, int m_h
       const int32_t prev = (old == kNone) ? kNone : uf_find(G + base, old);
       *cp = prev < cand ? prev : cand;
     }
-  }
+  });
 }
 
 // flags[cfg][i] = 1 for the root of every core component (compressing G on the way); only the
@@ -187,29 +216,30 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
   return Status::Ok();
 }
 
-// One batch of one eps: local components (when there is more than one batch), border
+// One batch, every eps: local components (when there is more than one batch), border
 // candidates, global union, border fold.
-Status launch_cc_batch(const Slab& sl, int64_t n, int l, int e, int m_lo, int m_hi, const int32_t* cc_e,
-                       bool single_batch, int32_t* G, int32_t* L, unsigned long long* best, int32_t* cur,
-                       uint32_t tag, int32_t* err, int sm_count, cudaStream_t s)
+Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int k, int l, int cfg_begin,
+                       int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
+                       unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
+                       cudaStream_t s)
 {
-  if (sl.count <= 0 || m_lo >= m_hi) return Status::Ok();
-  const int cfg0 = e * l;
-  const int64_t want = ceil_div(sl.count, 256);
-  const unsigned nb = static_cast<unsigned>(std::min<int64_t>(want, static_cast<int64_t>(sm_count) * 16));
+  if (upper_entries <= 0 || cfg_begin >= cfg_end) return Status::Ok();
+  const CcArgs a{ms, n, k, l, cfg_begin, cfg_end, cc};
+  const int64_t want = ceil_div(upper_entries, 256);
+  const unsigned nb = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sm_count) * 16)));
   if (single_batch) {
     count_launch(2);
-    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, G, err);
-    cc_best_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, G, best, tag);
+    cc_union_kernel<<<nb, 256, 0, s>>>(a, G, err);
+    cc_best_kernel<<<nb, 256, 0, s>>>(a, G, best, tag);
   } else {
     count_launch(4);
-    cc_touch_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, L);
-    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, L, err);
-    cc_best_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, L, best, tag);
-    cc_union_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, G, err);
+    cc_touch_kernel<<<nb, 256, 0, s>>>(a, L);
+    cc_union_kernel<<<nb, 256, 0, s>>>(a, L, err);
+    cc_best_kernel<<<nb, 256, 0, s>>>(a, L, best, tag);
+    cc_union_kernel<<<nb, 256, 0, s>>>(a, G, err);
   }
   count_launch();
-  cc_border_kernel<<<nb, 256, 0, s>>>(sl, n, cfg0, m_lo, m_hi, cc_e, G, best, cur, tag);
+  cc_border_kernel<<<nb, 256, 0, s>>>(a, G, best, cur, tag);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }

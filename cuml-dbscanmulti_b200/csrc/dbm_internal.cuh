@@ -141,14 +141,23 @@ __device__ __forceinline__ bool uf_unite(int32_t* parent, int32_t a, int32_t b)
 }
 
 // ---- launch descriptors shared by the orchestrator and the kernels ------------------------
-// One slab of neighbour entries (the rows of one batch at one eps), processed edge-parallel:
-// entry q links row[q] and col[q] (low 28 bits significant).  `count` bounds q on the host
-// side; when `count_dev` is set the exact count is read on the device (no host sync).
-struct Slab {
-  const int32_t* row;
-  const int32_t* col;
-  int64_t count;
-  const int64_t* count_dev;
+// A slab of neighbour entries: entry q in [begin, end) links row[q] and col[q] (low 28 bits;
+// the top 4 bits carry the entry's code in max-eps slabs).  begin/end are read on the device
+// when begin_dev/end_dev are set (slabs compacted on the device), else begin = 0, end = count.
+struct SlabRef {
+  const int32_t* row = nullptr;
+  const int32_t* col = nullptr;
+  int64_t count = 0;
+  const int64_t* begin_dev = nullptr;
+  const int64_t* end_dev = nullptr;
+};
+
+// The slabs of one batch: annotated route, slab e = the entries of eps e (nslabs = k); direct
+// route, slab 0 = the max-eps entries and an entry belongs to every eps >= its code.
+struct MultiSlab {
+  SlabRef s[kMaxEps];
+  int nslabs = 0;
+  int direct = 0;
 };
 
 struct DistLaunch {

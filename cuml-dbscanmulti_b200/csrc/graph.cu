@@ -11,8 +11,9 @@
 //                        adj_to_csr + annotateKernel (adjgraph/algo.cuh:56-57,
 //                        csr_multi_eps.cuh:93-185); here it is filled straight from the
 //                        neighbour pairs the distance kernel emitted, both directions.
-//   filter_kernel        order-preserving per-row compaction of the max-eps CSR to eps_e
-//                        (filterKernel, csr_multi_eps.cuh:194-234): the annotated route.
+//   filter_all_kernel    order-preserving per-row compaction of the max-eps CSR to every
+//                        smaller eps in one pass (filterKernel, csr_multi_eps.cuh:194-234,
+//                        runs once per eps): the annotated route.
 //   batch_nnz_kernel     per-batch nnz at the largest eps (runner_multi.cuh:898-904).
 #include "dbm_internal.cuh"
 
@@ -225,61 +226,69 @@ Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, i
   return Status::Ok();
 }
 
-// ---- per-eps compaction of a batch slab (annotated route) ----------------------------------
-// counts[r] = deg[e][s+r] - 1 for the batch rows
-__global__ void slab_counts_kernel(const int32_t* __restrict__ deg_e, int64_t s0, int64_t rows,
-                                   int32_t* __restrict__ counts)
+// ---- all smaller eps of a batch at once (annotated route) -------------------------------------
+// counts[e*rows + r] = deg[e][s0 + r] - 1, e < ne (= k - 1)
+__global__ void slab_counts_all_kernel(const int32_t* __restrict__ deg, int64_t n, int ne, int64_t s0,
+                                       int64_t rows, int32_t* __restrict__ counts)
 {
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (r < rows) counts[r] = deg_e[s0 + r] - 1;
+  const int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (x >= rows * ne) return;
+  const int64_t e = x / rows, r = x - e * rows;
+  counts[x] = deg[e * n + s0 + r] - 1;
 }
 
-// One warp per row: ballot over the row's entries keeps those with code <= e, in order.
-__global__ void filter_kernel(const int64_t* __restrict__ off, const uint32_t* __restrict__ col,
-                              int64_t s0, int64_t rows, uint32_t e,
-                              const int64_t* __restrict__ off_e, int32_t* __restrict__ col_e,
-                              int32_t* __restrict__ row_e)
+// One warp per batch row: one pass over its max-eps entries writes every smaller-eps slab e
+// (entries with code <= e), order-preserving, at off_flat[e*rows + r].
+__global__ void filter_all_kernel(const int64_t* __restrict__ off, const uint32_t* __restrict__ col, int64_t s0,
+                                  int64_t rows, int ne, const int64_t* __restrict__ off_flat,
+                                  int32_t* __restrict__ col_flat, int32_t* __restrict__ row_flat)
 {
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const int64_t r = s0 + warp;
   const int64_t beg = off[r], end = off[r + 1];
-  int64_t out = off_e[warp];
+  int64_t out[kMaxEps];
+  for (int e = 0; e < ne; ++e) out[e] = off_flat[static_cast<int64_t>(e) * rows + warp];
+  const uint32_t below = (1u << lane) - 1u;
   for (int64_t q0 = beg; q0 < end; q0 += 32) {
     const int64_t q = q0 + lane;
-    uint32_t w = 0;
-    bool keep = false;
+    uint32_t code = 0xffu, j = 0;
     if (q < end) {
-      w = col[q];
-      keep = (w >> kCodeShift) <= e;
+      const uint32_t w = col[q];
+      code = w >> kCodeShift;
+      j = w & kColMask;
     }
-    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-    if (keep) {
-      const int64_t dst = out + __popc(bal & ((1u << lane) - 1u));
-      col_e[dst] = static_cast<int32_t>(w & kColMask);
-      row_e[dst] = static_cast<int32_t>(r);
+    for (int e = 0; e < ne; ++e) {
+      const bool keep = code <= static_cast<uint32_t>(e);
+      const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+      if (keep) {
+        const int64_t dst = out[e] + __popc(bal & below);
+        col_flat[dst] = static_cast<int32_t>(j);
+        row_flat[dst] = static_cast<int32_t>(r);
+      }
+      out[e] += __popc(bal);
     }
-    out += __popc(bal);
   }
 }
 
-Status launch_slab_counts(const int32_t* deg_e, int64_t s0, int64_t rows, int32_t* counts,
-                          cudaStream_t s)
+Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0, int64_t rows, int32_t* counts,
+                              cudaStream_t s)
 {
+  if (ne <= 0 || rows <= 0) return Status::Ok();
   count_launch();
-  slab_counts_kernel<<<static_cast<unsigned>(ceil_div(rows, 256)), 256, 0, s>>>(deg_e, s0, rows, counts);
+  slab_counts_all_kernel<<<static_cast<unsigned>(ceil_div(rows * ne, 256)), 256, 0, s>>>(deg, n, ne, s0, rows, counts);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
 
-Status launch_filter(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int e,
-                     const int64_t* off_e, int32_t* col_e, int32_t* row_e, cudaStream_t s)
+Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int ne,
+                         const int64_t* off_flat, int32_t* col_flat, int32_t* row_flat, cudaStream_t s)
 {
-  const int64_t threads = rows * 32;
+  if (ne <= 0 || rows <= 0) return Status::Ok();
   count_launch();
-  filter_kernel<<<static_cast<unsigned>(ceil_div(threads, 256)), 256, 0, s>>>(
-    off, col, s0, rows, static_cast<uint32_t>(e), off_e, col_e, row_e);
+  filter_all_kernel<<<static_cast<unsigned>(ceil_div(rows * 32, 256)), 256, 0, s>>>(off, col, s0, rows, ne, off_flat,
+                                                                                  col_flat, row_flat);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
