@@ -413,7 +413,7 @@ def main() -> None:
     lane_frac = (unique_pairs * 2.0 * d * work_frac) / (dms * 1e-3) / (148 * 128 * sm_mhz * 1e6)
     traffic_path = ROOT / "profiles" / "dist_tri_kernel_traffic.json"
     traffic = None
-    if traffic_path.exists():
+    if traffic_path.exists() and not args.n and ws == 1:
         try:
             traffic = json.loads(traffic_path.read_text()).get(args.config)
         except Exception:
