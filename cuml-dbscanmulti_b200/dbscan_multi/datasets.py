@@ -1,0 +1,130 @@
+"""The reference's on-disk dataset format: ``<base>.f32`` + ``<base>.labels.i32`` + ``<base>.json``.
+
+Written by the reference's generator (tools/gerar_datasets.py:648-706) and read by its tools
+(tools/bench_vs_cuml.py ``--meta``): float32 points, row-major, no header; int32 ground-truth
+labels; a JSON document with the shape, the grid (``eps`` and ``min_samples`` already sorted,
+eps-major configuration order), the protocol tag and SHA-256 digests of the files.
+
+``load_dataset(meta_path)`` checks what the reference's tools check before a run (protocol,
+dtype, layout, sizes, digests) and returns the points and the grid, ready for
+``fit_multi(points, ds.eps, ds.min_samples)``; ``write_dataset`` writes the same layout.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Sequence
+
+import numpy as np
+
+PROTOCOL = "knn-sample-rank-v2"
+
+
+class DatasetError(ValueError):
+    pass
+
+
+@dataclass
+class Dataset:
+    points: np.ndarray          # (n, d) float32
+    eps: list[float]
+    min_samples: list[int]
+    labels_true: np.ndarray | None
+    meta: dict[str, Any] = field(default_factory=dict)
+
+    @property
+    def n(self) -> int:
+        return int(self.points.shape[0])
+
+    @property
+    def d(self) -> int:
+        return int(self.points.shape[1])
+
+
+def sha256_file(path: Path) -> str:
+    h = hashlib.sha256()
+    with Path(path).open("rb") as f:
+        for block in iter(lambda: f.read(1 << 20), b""):
+            h.update(block)
+    return h.hexdigest()
+
+
+def load_dataset(meta_path: str | Path, *, verify: bool = True, require_protocol: bool = True) -> Dataset:
+    meta_path = Path(meta_path)
+    meta = json.loads(meta_path.read_text(encoding="utf-8"))
+    if require_protocol and meta.get("protocolo_dataset") != PROTOCOL:
+        raise DatasetError(f"{meta_path}: dataset protocol {meta.get('protocolo_dataset')!r}, expected {PROTOCOL!r}")
+    if meta.get("dtype", "float32") != "float32" or meta.get("layout", "row-major") != "row-major":
+        raise DatasetError(f"{meta_path}: only float32 row-major points are supported")
+    n, d = int(meta["n"]), int(meta["d"])
+    files = meta.get("arquivos", {})
+    points_path = meta_path.parent / files.get("points", meta_path.with_suffix(".f32").name)
+    if not points_path.exists():
+        raise DatasetError(f"points file {points_path} is missing")
+    if points_path.stat().st_size != n * d * 4:
+        raise DatasetError(f"{points_path} has {points_path.stat().st_size} bytes, expected {n * d * 4}")
+    digests = meta.get("sha256", {})
+    if verify and "points" in digests and sha256_file(points_path) != digests["points"]:
+        raise DatasetError(f"{points_path}: SHA-256 does not match the metadata")
+    points = np.fromfile(points_path, dtype=np.float32).reshape(n, d)
+    labels = None
+    lab_name = files.get("labels_verdadeiros")
+    if lab_name:
+        lab_path = meta_path.parent / lab_name
+        if lab_path.exists():
+            if verify and "labels_verdadeiros" in digests and sha256_file(lab_path) != digests["labels_verdadeiros"]:
+                raise DatasetError(f"{lab_path}: SHA-256 does not match the metadata")
+            labels = np.fromfile(lab_path, dtype=np.int32)
+            if labels.size != n:
+                raise DatasetError(f"{lab_path} holds {labels.size} labels, expected {n}")
+    eps = [float(v) for v in meta["eps"]]
+    min_samples = [int(v) for v in meta["min_samples"]]
+    if eps != sorted(set(eps)) or min_samples != sorted(set(min_samples)):
+        raise DatasetError(f"{meta_path}: the grid must be sorted and without duplicates")
+    if meta.get("config_order", "eps_major") != "eps_major":
+        raise DatasetError(f"{meta_path}: only eps-major configuration order is defined")
+    return Dataset(points=points, eps=eps, min_samples=min_samples, labels_true=labels, meta=meta)
+
+
+def write_dataset(base: str | Path, points: np.ndarray, eps: Sequence[float], min_samples: Sequence[int],
+                  labels_true: np.ndarray | None = None, name: str | None = None,
+                  extra: dict[str, Any] | None = None) -> Path:
+    """Writes ``<base>.f32``, optionally ``<base>.labels.i32``, and ``<base>.json``."""
+    base = Path(base)
+    base.parent.mkdir(parents=True, exist_ok=True)
+    x = np.ascontiguousarray(points, dtype=np.float32)
+    if x.ndim != 2:
+        raise DatasetError("points must be (n, d)")
+    e = sorted({float(v) for v in eps})
+    m = sorted({int(v) for v in min_samples})
+    pts_path = base.with_name(base.name + ".f32")
+    x.tofile(pts_path)
+    files = {"points": pts_path.name}
+    digests = {"points": sha256_file(pts_path)}
+    if labels_true is not None:
+        lab_path = base.with_name(base.name + ".labels.i32")
+        np.ascontiguousarray(labels_true, dtype=np.int32).tofile(lab_path)
+        files["labels_verdadeiros"] = lab_path.name
+        digests["labels_verdadeiros"] = sha256_file(lab_path)
+    meta = {
+        "protocolo_dataset": PROTOCOL,
+        "dataset": name or base.name,
+        "n": int(x.shape[0]),
+        "d": int(x.shape[1]),
+        "dtype": "float32",
+        "layout": "row-major",
+        "eps": e,
+        "min_samples": m,
+        "configuration_count": len(e) * len(m),
+        "config_order": "eps_major",
+        "arquivos": files,
+        "sha256": digests,
+    }
+    if extra:
+        meta.update(extra)
+    meta_path = base.with_name(base.name + ".json")
+    meta_path.write_text(json.dumps(meta, indent=2, ensure_ascii=False), encoding="utf-8")
+    return meta_path

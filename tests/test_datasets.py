@@ -1,0 +1,67 @@
+"""The reference's dataset format (points .f32 + labels .i32 + metadata .json)."""
+
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from dbscan_multi import datasets
+
+
+def test_round_trip(tmp_path):
+    rng = np.random.default_rng(0)
+    x = rng.normal(size=(500, 3)).astype(np.float32)
+    y = rng.integers(-1, 4, 500).astype(np.int32)
+    meta = datasets.write_dataset(tmp_path / "blobs_n500", x, [0.5, 0.2], [10, 5], y)
+    ds = datasets.load_dataset(meta)
+    assert np.array_equal(ds.points, x) and np.array_equal(ds.labels_true, y)
+    assert ds.eps == [pytest.approx(0.2), pytest.approx(0.5)] and ds.min_samples == [5, 10]
+    assert ds.meta["configuration_count"] == 4 and ds.meta["config_order"] == "eps_major"
+
+
+def test_rejects_corruption_and_wrong_protocol(tmp_path):
+    x = np.zeros((10, 2), np.float32)
+    meta = datasets.write_dataset(tmp_path / "z", x, [0.1], [2])
+    pts = tmp_path / "z.f32"
+    raw = bytearray(pts.read_bytes())
+    raw[0] ^= 1
+    pts.write_bytes(bytes(raw))
+    with pytest.raises(datasets.DatasetError, match="SHA-256"):
+        datasets.load_dataset(meta)
+    assert datasets.load_dataset(meta, verify=False).n == 10
+    m = json.loads(meta.read_text())
+    m["protocolo_dataset"] = "historico"
+    meta.write_text(json.dumps(m))
+    with pytest.raises(datasets.DatasetError, match="protocol"):
+        datasets.load_dataset(meta, verify=False)
+    m["protocolo_dataset"] = datasets.PROTOCOL
+    m["n"] = 11
+    meta.write_text(json.dumps(m))
+    with pytest.raises(datasets.DatasetError, match="bytes"):
+        datasets.load_dataset(meta, verify=False)
+
+
+def test_unsorted_grid_is_rejected(tmp_path):
+    meta = datasets.write_dataset(tmp_path / "u", np.zeros((4, 1), np.float32), [0.1, 0.2], [2])
+    m = json.loads(meta.read_text())
+    m["eps"] = [0.2, 0.1]
+    meta.write_text(json.dumps(m))
+    with pytest.raises(datasets.DatasetError, match="sorted"):
+        datasets.load_dataset(meta)
+
+
+@pytest.mark.gpu
+def test_fit_a_written_dataset_through_the_api(tmp_path):
+    import dbscan_multi as dm
+    import oracle
+
+    rng = np.random.default_rng(5)
+    x = np.vstack([rng.normal(c, 0.2, (300, 2)) for c in (0, 2, 4)]).astype(np.float32)
+    meta = datasets.write_dataset(tmp_path / "three_n900", x, [0.15, 0.3], [5, 12])
+    ds = datasets.load_dataset(meta)
+    with dm.DbscanMulti(0) as h:
+        r = h.fit_multi(ds.points, ds.eps, ds.min_samples)
+    want, _, _ = oracle.fit_multi(ds.points, ds.eps, ds.min_samples)
+    assert np.array_equal(r.labels, want)

@@ -342,3 +342,48 @@ def test_multi_both_large_properties(h, torch_mod):
     r = sampled_checks(h, torch_mod, pts, [3.0, 3.5, 4.0, 4.5], [5, 10, 20, 40], 16,
                        max_bytes_per_batch=budget, neigh_per_row=64)
     assert r.stats["batches"] >= 4
+
+
+@pytest.mark.parametrize("route", ["annotated", "dense"])
+@pytest.mark.parametrize("rows", [None, 1500, 400])
+def test_routes_and_batches_match_oracle_on_medium_case(h, torch_mod, route, rows):
+    """Both routes (compacted per-eps slabs vs eps read from the max-eps codes) with one and
+    several batches, on a case dense enough that every eps has many edges."""
+    rng = np.random.default_rng(321)
+    n = 6000
+    pts = blobs(rng, n, 5, centers=8, spread=0.6, noise_frac=0.08, box=4.0)
+    eps, ms = [0.45, 0.6, 0.8, 1.0], [3, 8, 20]
+    kw = dict(route=route, index="int32")
+    if rows:
+        kw["max_bytes_per_batch"] = dm.max_bytes_for_batch_size(n, 4, 3, rows, "cuvs", 0, "int32")
+    labels, core, r = gpu_fit(h, torch_mod, pts, eps, ms, **kw)
+    assert set(r.batch_routes) == {route}
+    ol, oc, _ = oracle.fit_multi(pts, eps, ms, r.stats["batch_size"])
+    assert np.array_equal(labels, ol) and np.array_equal(core, oc)
+
+
+def test_config_range_fit_from_graph_matches_full_fit(h, torch_mod):
+    """dbm_distance_shard over all shards + dbm_fit_multi_from_graph on config sub-ranges gives
+    the rows of the full fit (the multi-GPU building blocks, exercised on one GPU)."""
+    from dbscan_multi import parallel
+
+    rng = np.random.default_rng(99)
+    pts = blobs(rng, 9000, 6, centers=12, spread=0.7, noise_frac=0.05, box=6.0)
+    x = torch_mod.from_numpy(pts).cuda()
+    eps, ms = [0.6, 0.9, 1.2], [4, 9]
+    budget = dm.max_bytes_for_batch_size(9000, 3, 2, 2500, "cuvs")
+    full = h.fit_multi(x, eps, ms, max_bytes_per_batch=budget).labels.cpu().numpy()
+    st = parallel.DeviceStages(h)
+    e = dm.normalize_eps(eps)
+    m = dm.normalize_min_samples(ms)
+    hists, parts = [], []
+    for shard in range(3):
+        hh, ee = st.distance_shard(x, e, shard, 3, 1024)
+        hists.append(hh.clone())
+        parts.append(ee.clone())
+    hist = sum(hists)
+    edges = torch_mod.cat(parts)
+    opt = dm.Options(0, 0, 0, 0, budget, 0)
+    for c0, c1 in [(0, 2), (2, 5), (5, 6), (0, 6)]:
+        lab, stats, _ = st.fit_from_graph(9000, 6, e, m, hist, edges, c0, c1, opt)
+        assert np.array_equal(lab[c0:c1].cpu().numpy(), full[c0:c1])

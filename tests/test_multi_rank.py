@@ -146,3 +146,46 @@ def test_sharded_fit_on_gloo_ranks_equals_single_process(tmp_path, world):
     for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"labels_{r}.npy"), want)
         assert np.array_equal(np.load(tmp_path / f"opt_{r}.npy"), opt0)
+
+
+class FailingStages(OracleStages):
+    """Rank 1 fails inside its distance stage (an injected host-side fault)."""
+
+    def distance_shard(self, x, eps, shard, nshards, cap_hint):
+        if self.rank == 1:
+            raise RuntimeError("injected failure on rank 1")
+        return super().distance_shard(x, eps, shard, nshards, cap_hint)
+
+
+def _failing_worker(rank, world, port, result_dir):
+    import datetime
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    outcome = "ok"
+    try:
+        parallel.sharded_fit_multi(FailingStages(make_points(), rank), torch.from_numpy(make_points()), EPS, MS)
+    except Exception as exc:  # the failing rank raises; the survivor's collective times out
+        outcome = type(exc).__name__ + ": " + str(exc)[:200]
+    with open(os.path.join(result_dir, f"outcome_{rank}.txt"), "w") as f:
+        f.write(outcome)
+    os._exit(0)  # leave without a final barrier on the broken group
+
+
+def test_a_failing_rank_is_detected_by_the_others(tmp_path):
+    """Failure detection across ranks on the host: rank 1 raises before its collectives; rank 0
+    must come back with an error from its next collective (process-group timeout) instead of
+    hanging, and both processes exit."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert not p.is_alive(), "a rank hung"
+    o0 = (tmp_path / "outcome_0.txt").read_text()
+    o1 = (tmp_path / "outcome_1.txt").read_text()
+    assert "injected failure" in o1
+    assert o0 != "ok"
