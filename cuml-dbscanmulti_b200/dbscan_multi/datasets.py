@@ -6,8 +6,10 @@ labels; a JSON document with the shape, the grid (``eps`` and ``min_samples`` al
 eps-major configuration order), the protocol tag and SHA-256 digests of the files.
 
 ``load_dataset(meta_path)`` checks what the reference's tools check before a run (protocol,
-dtype, layout, sizes, digests) and returns the points and the grid, ready for
-``fit_multi(points, ds.eps, ds.min_samples)``; ``write_dataset`` writes the same layout.
+dtype, layout, sizes, digests; optionally the dataset name, N, the eps count and the eps
+quantiles, as tools/gerar_datasets.py:617-645 does) and returns the points and the grid,
+ready for ``fit_multi(points, ds.eps, ds.min_samples)``; ``write_dataset`` writes the same
+layout, and ``normalize_minmax`` is the generator's per-column scaling (:131-138).
 """
 
 from __future__ import annotations
@@ -52,11 +54,30 @@ def sha256_file(path: Path) -> str:
     return h.hexdigest()
 
 
-def load_dataset(meta_path: str | Path, *, verify: bool = True, require_protocol: bool = True) -> Dataset:
+def normalize_minmax(x: np.ndarray) -> np.ndarray:
+    """Each column scaled to [0, 1] in float32; a constant column keeps span 1 (becomes 0)."""
+    x = np.asarray(x, dtype=np.float32)
+    lo = x.min(axis=0)
+    span = x.max(axis=0) - lo
+    span[span == 0.0] = 1.0
+    return ((x - lo) / span).astype(np.float32)
+
+
+def load_dataset(meta_path: str | Path, *, verify: bool = True, require_protocol: bool = True,
+                 dataset: str | None = None, n: int | None = None, eps_count: int | None = None,
+                 eps_quantiles: Sequence[float] | None = None) -> Dataset:
     meta_path = Path(meta_path)
     meta = json.loads(meta_path.read_text(encoding="utf-8"))
     if require_protocol and meta.get("protocolo_dataset") != PROTOCOL:
         raise DatasetError(f"{meta_path}: dataset protocol {meta.get('protocolo_dataset')!r}, expected {PROTOCOL!r}")
+    if dataset is not None and meta.get("dataset") != dataset:
+        raise DatasetError(f"{meta_path}: dataset {meta.get('dataset')!r}, expected {dataset!r}")
+    if n is not None and meta.get("n") != n:
+        raise DatasetError(f"{meta_path}: N {meta.get('n')!r}, expected {n}")
+    if eps_count is not None and len(meta.get("eps", [])) != eps_count:
+        raise DatasetError(f"{meta_path}: {len(meta.get('eps', []))} eps values, expected {eps_count}")
+    if eps_quantiles is not None and tuple(map(float, meta.get("quantis_eps", []))) != tuple(map(float, eps_quantiles)):
+        raise DatasetError(f"{meta_path}: eps quantiles {meta.get('quantis_eps')!r}, expected {list(eps_quantiles)!r}")
     if meta.get("dtype", "float32") != "float32" or meta.get("layout", "row-major") != "row-major":
         raise DatasetError(f"{meta_path}: only float32 row-major points are supported")
     n, d = int(meta["n"]), int(meta["d"])

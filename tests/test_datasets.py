@@ -65,3 +65,24 @@ def test_fit_a_written_dataset_through_the_api(tmp_path):
         r = h.fit_multi(ds.points, ds.eps, ds.min_samples)
     want, _, _ = oracle.fit_multi(ds.points, ds.eps, ds.min_samples)
     assert np.array_equal(r.labels, want)
+
+
+def test_normalize_minmax():
+    x = np.array([[1.0, 5.0, -2.0], [3.0, 5.0, 2.0], [2.0, 5.0, 0.0]], np.float32)
+    got = datasets.normalize_minmax(x)
+    assert got.dtype == np.float32
+    assert np.array_equal(got, np.array([[0, 0, 0], [1, 0, 1], [0.5, 0, 0.5]], np.float32))
+    rng = np.random.default_rng(3)
+    y = (rng.normal(size=(1000, 4)) * [1, 1e-3, 1e3, 0]).astype(np.float32)
+    want = (y - y.min(0)) / np.where(np.ptp(y, 0) == 0, np.float32(1), np.ptp(y, 0))
+    assert np.array_equal(datasets.normalize_minmax(y), want.astype(np.float32))
+
+
+def test_metadata_expectations(tmp_path):
+    meta = datasets.write_dataset(tmp_path / "m_n6", np.zeros((6, 2), np.float32), [0.1, 0.2], [3],
+                                  name="moons_2d", extra={"quantis_eps": [0.5, 0.7]})
+    assert datasets.load_dataset(meta, dataset="moons_2d", n=6, eps_count=2, eps_quantiles=(0.5, 0.7)).n == 6
+    for kw, msg in (({"dataset": "rings_2d"}, "dataset"), ({"n": 7}, "N "), ({"eps_count": 3}, "eps values"),
+                    ({"eps_quantiles": (0.5, 0.85)}, "quantiles")):
+        with pytest.raises(datasets.DatasetError, match=msg):
+            datasets.load_dataset(meta, **kw)
