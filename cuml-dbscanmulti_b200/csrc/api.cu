@@ -41,7 +41,7 @@ int64_t launches_so_far() { return g_launches.load(); }
 // launchers defined in dist.cu / graph.cu / cc.cu
 Status launch_distance(const DistLaunch& a, cudaStream_t s);
 Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s,
-                     const int32_t* perm = nullptr);
+                     const int32_t* perm = nullptr, int32_t rows = 0);
 int32_t padded_dims(int32_t d);
 int64_t padded_points(int64_t n);
 size_t order_scratch_bytes(int64_t n);
@@ -204,7 +204,8 @@ struct dbm_handle {
   uint64_t edge_cap_hint = 0;
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
-  dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_counts, prune_off, work;
+  dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_counts, prune_off, work, fallback;
+  int distance_mode = DBM_DISTANCE_AUTO;
   dbm::Buffer xdev, labels_dev, core_dev;  // host-buffer entry point only
   int64_t* pinned = nullptr;               // small D2H staging
   size_t pinned_count = 0;
@@ -215,7 +216,7 @@ struct dbm_handle {
                                 &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
                                 &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz,
                                 &perm, &order_scratch, &box_lo, &box_hi, &prune_counts, &prune_off,
-                                &work};
+                                &work, &fallback};
     uint64_t s = 0;
     for (auto* b : all) s += b->bytes;
     return s;
@@ -402,8 +403,14 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
 {
   const int32_t di = static_cast<int32_t>(d);
   const int64_t kn = static_cast<int64_t>(k) * n;
-  DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(padded_dims(di)) * padded_points(n)));
-  DBM_TRY(ensure(h->counters, 4 * sizeof(unsigned long long)));
+  // Screened pass (dist_tc.cu) when the worklist exists (ordered points) and the bound applies;
+  // the exact tile kernel takes the tile pairs it hands back, or everything when it is off.
+  const bool screen = n >= kOrderMinPoints && h->distance_mode != DBM_DISTANCE_EXACT && screen_supported(di, eps2[k - 1]);
+  if (h->distance_mode == DBM_DISTANCE_SCREENED && !screen)
+    return Status::Err(DBM_ERR_INVALID, "the screened distance pass needs N >= 4096, D <= 64 and eps^2 >= 1e-20");
+  const int32_t xt_rows = screen ? std::max(padded_dims(di), screen_rows(di)) : padded_dims(di);
+  DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(xt_rows) * padded_points(n)));
+  DBM_TRY(ensure(h->counters, 8 * sizeof(unsigned long long)));
   DBM_TRY(ensure(h->err, 16));
   DBM_TRY(ensure_pinned(h, 16));
   DBM_CUDA(cudaMemsetAsync(h->err.p, 0, 16, s));
@@ -417,7 +424,7 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     DBM_TRY(spatial_order(x, n, di, as<int32_t>(h->perm), h->order_scratch.p, h->order_scratch.bytes, s));
     perm = as<int32_t>(h->perm);
   }
-  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, perm));
+  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, perm, xt_rows));
   // Exact tile-pair pruning by per-tile bounding boxes (prune.cu): only tile pairs that may hold
   // a neighbour pair are evaluated.  Every rank builds the same worklist and takes its slice.
   const int64_t T = ceil_div(n, 128);
@@ -447,36 +454,48 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
   } else {
     st.tile_pairs_kept = 1.0;
   }
+  if (screen) DBM_TRY(ensure(h->fallback, sizeof(long long) * std::max<int64_t>(work_count, 1)));
   uint64_t cap = std::max<uint64_t>(h->edge_cap_hint, cap_hint);
   uint64_t found = 0;
   for (int pass = 0; pass < 2; ++pass) {
     DBM_TRY(ensure(h->edges, sizeof(uint64_t) * std::max<uint64_t>(cap, 1)));
     cap = h->edges.bytes / sizeof(uint64_t);
     DBM_CUDA(cudaMemsetAsync(hist, 0, sizeof(int32_t) * kn, s));
-    DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 4 * sizeof(unsigned long long), s));
+    DBM_CUDA(cudaMemsetAsync(h->counters.p, 0, 8 * sizeof(unsigned long long), s));
     DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
                  as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards, perm,
                  work, work_count};
-    DBM_TRY(launch_distance(a, s));
+    if (screen) {
+      DBM_TRY(launch_screened_distance(a, as<float>(h->box_lo), as<float>(h->box_hi), as<long long>(h->fallback), s));
+      DistLaunch f = a;
+      f.shard = 0;
+      f.nshards = 1;
+      f.work = as<long long>(h->fallback);
+      f.work_count = 0;
+      f.work_count_dev = as<unsigned long long>(h->counters) + 5;
+      DBM_TRY(launch_distance(f, s));
+    } else {
+      DBM_TRY(launch_distance(a, s));
+    }
     st.distance_passes = pass + 1;
-    h->pinned[0] = 0;
-    h->pinned[1] = 0;
-    h->pinned[2] = 0;
-    DBM_CUDA(cudaMemcpyAsync(h->pinned, h->counters.p, sizeof(unsigned long long), cudaMemcpyDeviceToHost, s));
-    DBM_CUDA(cudaMemcpyAsync(h->pinned + 1, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-    DBM_CUDA(cudaMemcpyAsync(h->pinned + 2, as<unsigned long long>(h->counters) + 2, sizeof(unsigned long long),
-                             cudaMemcpyDeviceToHost, s));
+    for (int w = 0; w < 8; ++w) h->pinned[w] = 0;
+    DBM_CUDA(cudaMemcpyAsync(h->pinned, h->counters.p, 8 * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s));
+    DBM_CUDA(cudaMemcpyAsync(h->pinned + 8, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     DBM_CUDA(cudaStreamSynchronize(s));
     found = static_cast<uint64_t>(h->pinned[0]);
     {
-      // 8 warps per 128 x 128 tile, each evaluating up to d dims for its 16 x 128 pairs; the
-      // reference is this shard's share of all tile pairs (pruned ones count as zero)
+      // exact-kernel work: 8 warps per 128 x 128 tile, each evaluating up to d dims for its
+      // 16 x 128 pairs; the reference is this shard's share of all tile pairs
       const double full = static_cast<double>(pairs) / nshards * 8.0 * static_cast<double>(d);
       st.dist_work_fraction = full > 0 ? static_cast<double>(h->pinned[2]) / full : 1.0;
     }
-    if (h->pinned[1] & kErrNonFinite) return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
-    if (h->pinned[1] & kErrTmaTimeout)
-      return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded TMA wait in the distance kernel ran out");
+    st.screened_tile_pairs = screen ? h->pinned[7] : 0;
+    st.fallback_tile_pairs = screen ? h->pinned[5] : 0;
+    st.screen_candidates = screen ? h->pinned[6] : 0;
+    const int64_t flags = h->pinned[8] & 0xffffffff;
+    if (flags & kErrNonFinite) return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
+    if (flags & kErrTmaTimeout)
+      return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded wait in the distance kernels ran out");
     if (found <= cap) break;
     if (pass == 1) return Status::Err(DBM_ERR_CUDA, "neighbour-pair buffer overflowed twice");
     cap = found;
@@ -764,6 +783,13 @@ uint64_t dbm_workspace_bytes(const dbm_handle* h) { return h ? h->workspace_byte
 void dbm_set_phase_timing(dbm_handle* h, int enabled)
 {
   if (h) h->timing = enabled != 0;
+}
+
+int dbm_set_distance_mode(dbm_handle* h, int mode)
+{
+  if (!h || mode < DBM_DISTANCE_AUTO || mode > DBM_DISTANCE_SCREENED) return DBM_ERR_INVALID;
+  h->distance_mode = mode;
+  return DBM_OK;
 }
 
 int dbm_fit_multi(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host,

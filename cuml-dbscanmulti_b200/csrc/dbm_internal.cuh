@@ -176,7 +176,18 @@ struct DistLaunch {
   const int32_t* perm = nullptr;   // XT column r holds point perm[r] (nullptr: identity)
   const long long* work = nullptr; // surviving tile pairs (nullptr: every tile pair)
   int64_t work_count = 0;
+  const unsigned long long* work_count_dev = nullptr;  // count of `work` read on the device
+                                                       // (the whole list, no sharding)
 };
+
+// Screened distance pass (dist_tc.cu): tensor-core bound + exact chain for the candidates;
+// tile pairs it cannot screen are appended to `fallback` (count in counters[5]) for
+// launch_distance.  counters must hold 8 words: [0] edge cursor, [4] item cursor,
+// [5] fallback count, [6] candidates, [7] screened tile pairs.
+bool screen_supported(int32_t d, float eps2_max);
+int32_t screen_rows(int32_t d);  // XT rows the screened pass reads (zero beyond d)
+Status launch_screened_distance(const DistLaunch& a, const float* box_lo, const float* box_hi, long long* fallback,
+                                cudaStream_t s);
 
 // ---- kernel launch accounting (host) --------------------------------------------------------
 // Every kernel launch site calls count_launch(); dbm_stats.launches reports the difference

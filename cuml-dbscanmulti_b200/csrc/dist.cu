@@ -47,6 +47,7 @@ struct DistParams {
   int64_t item_begin;                // this launch's share [item_begin, item_begin + item_count)
   int64_t item_count;                // of the work items: tile pairs, or worklist entries
   const long long* work;             // worklist of tile-pair indices (nullptr: item = tile pair)
+  const unsigned long long* count_dev;  // when set, item_count is read here on the device
   unsigned long long* counters;      // [0] edge cursor, [1] next tile pair
   uint64_t* edges;
   uint64_t edge_cap;
@@ -66,6 +67,17 @@ __device__ __forceinline__ void tri_coords(long long c, long long& I, long long&
   while ((j + 1) * (j + 2) / 2 <= c) ++j;
   J = j;
   I = c - j * (j + 1) / 2;
+}
+
+// A work item: a worklist entry (J << 32 | I) or, without a worklist, a tile-pair index.
+__device__ __forceinline__ void item_coords(const DistParams& p, long long e, long long& I, long long& J)
+{
+  if (p.work) {
+    I = e & 0xffffffffLL;
+    J = e >> 32;
+  } else {
+    tri_coords(e, I, J);
+  }
 }
 
 // ---- packed fp32 pairs (sm_100: .f32x2, each lane rounded exactly like the scalar op) ----------
@@ -119,7 +131,8 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
 
   auto next_tile = [&]() -> long long {
     const long long i = static_cast<long long>(atomicAdd(p.counters + 1, 1ULL));
-    if (i >= p.item_count) return -1;
+    const long long limit = p.count_dev ? static_cast<long long>(*p.count_dev) : p.item_count;
+    if (i >= limit) return -1;
     return p.work ? p.work[p.item_begin + i] : p.item_begin + i;
   };
   auto issue = [&](int stage, long long tile, int chunk) {
@@ -127,7 +140,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
     s_tile[stage] = tile;
     if (tile < 0) return;
     long long I, J;
-    tri_coords(tile, I, J);
+    item_coords(p, tile, I, J);
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(&full[stage], 2 * box_bytes);
     float* a = stage ? As1 : As0;
@@ -235,7 +248,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
         }
       if (__any_sync(0xffffffffu, mn <= cutoff)) {
         long long I, J;
-        tri_coords(c, I, J);
+        item_coords(p, c, I, J);
         const int32_t row0 = static_cast<int32_t>(I) * kTile, col0 = static_cast<int32_t>(J) * kTile;
         const int32_t n32 = static_cast<int32_t>(n);
         const bool diag = (I == J);
@@ -321,7 +334,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   if (lane == 0 && dims_done) atomicAdd(p.counters + 2, static_cast<unsigned long long>(dims_done));
 }
 
-// X (n x d, row-major) -> XT (dp x npad, dim-major), zero padded.
+// X (n x d, row-major) -> XT (rows x npad, dim-major), zero padded (rows >= d).
 // Also flags NaN/Inf inputs, which the reference rejects before fitting (src/main.cu:1419-1423).
 __global__ void transpose_pad_kernel(const float* __restrict__ x, float* __restrict__ xt, int64_t n,
                                      int32_t d, int32_t dp, int64_t npad, int32_t* __restrict__ err,
@@ -368,9 +381,9 @@ int32_t padded_dims(int32_t d) { return (d + 3) / 4 * 4; }
 int64_t padded_points(int64_t n) { return (n + 3) / 4 * 4; }
 
 Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s,
-                     const int32_t* perm)
+                     const int32_t* perm, int32_t rows)
 {
-  const int32_t dp = padded_dims(d);
+  const int32_t dp = rows > padded_dims(d) ? rows : padded_dims(d);
   const int64_t npad = padded_points(n);
   dim3 grid(static_cast<unsigned>(ceil_div(npad, 32)), static_cast<unsigned>(ceil_div(dp, 32)));
   count_launch();
@@ -380,25 +393,33 @@ Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* e
 }
 
 
-Status launch_distance(const DistLaunch& a, cudaStream_t s)
+// Tensor map over XT (dp x npad fp32, dim-major): boxes of {128 points, dbox dims}.
+Status make_xt_map(const float* xt, int64_t n, int32_t d, CUtensorMap* map, int32_t* dbox_out)
 {
   auto encode = get_encode_fn();
   if (!encode) return Status::Err(DBM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  const int32_t dp = padded_dims(a.d);
-  const int64_t npad = padded_points(a.n);
+  const int32_t dp = padded_dims(d);
+  const int64_t npad = padded_points(n);
   const int32_t dbox = dp < kDimBox ? dp : kDimBox;
-
-  CUtensorMap map;
-  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(a.n), static_cast<cuuint64_t>(dp)};
+  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(dp)};
   const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(npad) * sizeof(float)};
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTile), static_cast<cuuint32_t>(dbox)};
   const cuuint32_t estride[2] = {1, 1};
-  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(a.xt), gdim,
-                      gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(xt), gdim, gstride, box,
+                      estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return Status::Err(DBM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  *dbox_out = dbox;
+  return Status::Ok();
+}
+
+Status launch_distance(const DistLaunch& a, cudaStream_t s)
+{
+  const int64_t npad = padded_points(a.n);
+  CUtensorMap map;
+  int32_t dbox = 0;
+  DBM_TRY(make_xt_map(a.xt, a.n, a.d, &map, &dbox));
 
   DistParams p{};
   p.n = a.n;
@@ -412,6 +433,11 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   p.item_begin = items * a.shard / shards;
   p.item_count = items * (a.shard + 1) / shards - p.item_begin;
   p.work = a.work;
+  p.count_dev = a.work_count_dev;
+  if (a.work_count_dev) {
+    p.item_begin = 0;
+    p.item_count = 0;
+  }
   p.counters = a.counters;
   p.edges = a.edges;
   p.edge_cap = a.edge_cap;
@@ -430,7 +456,7 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
                                                          smem));
   if (per_sm < 1) per_sm = 1;
   int64_t grid = static_cast<int64_t>(a.sm_count) * per_sm;
-  if (grid > p.item_count) grid = p.item_count;
+  if (!a.work_count_dev && grid > p.item_count) grid = p.item_count;
   if (grid < 1) return Status::Ok();
   count_launch();
   dist_tri_kernel<<<static_cast<unsigned>(grid), kDistThreads, smem, s>>>(map, p);

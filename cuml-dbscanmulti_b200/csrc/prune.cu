@@ -11,7 +11,7 @@
 //
 // Surviving tile pairs go to a worklist in tile-pair order (two passes: per-block counts,
 // scan, ordered write), so every rank of a sharded run sees the same list and takes an equal
-// slice of it.
+// slice of it.  Entries are the tile coordinates packed as J << 32 | I.
 #include "dbm_internal.cuh"
 
 #include <algorithm>
@@ -61,11 +61,9 @@ __device__ __forceinline__ void prune_tri_coords(long long c, long long& I, long
 }
 
 // true when some pair of the tile pair may be within cutoff
-__device__ __forceinline__ bool tile_pair_survives(long long c, const float* __restrict__ lo,
+__device__ __forceinline__ bool tile_pair_survives(long long I, long long J, const float* __restrict__ lo,
                                                    const float* __restrict__ hi, int32_t d, float cutoff)
 {
-  long long I, J;
-  prune_tri_coords(c, I, J);
   if (I == J) return true;
   const float* loI = lo + I * d;
   const float* hiI = hi + I * d;
@@ -93,7 +91,9 @@ __global__ void tile_prune_kernel(int64_t pairs, const float* __restrict__ lo, c
   // items are taken in tile-pair order: round q covers [b0 + q*256, b0 + (q+1)*256)
   for (int q = 0; q < kPruneItems; ++q) {
     const long long c = b0 + static_cast<int64_t>(q) * kPruneThreads + threadIdx.x;
-    const bool keep = c < pairs && tile_pair_survives(c, lo, hi, d, cutoff);
+    long long I = 0, J = 0;
+    if (c < pairs) prune_tri_coords(c, I, J);
+    const bool keep = c < pairs && tile_pair_survives(I, J, lo, hi, d, cutoff);
     const uint32_t bal = __ballot_sync(0xffffffffu, keep);
     if (lane == 0) warp_tot[warp] = __popc(bal);
     __syncthreads();
@@ -102,7 +102,7 @@ __global__ void tile_prune_kernel(int64_t pairs, const float* __restrict__ lo, c
       if (w2 < warp) before += warp_tot[w2];
       round += warp_tot[w2];
     }
-    if (WRITE && keep) work[base + total + before + __popc(bal & ((1u << lane) - 1u))] = c;
+    if (WRITE && keep) work[base + total + before + __popc(bal & ((1u << lane) - 1u))] = (J << 32) | I;
     total += round;
     __syncthreads();
   }

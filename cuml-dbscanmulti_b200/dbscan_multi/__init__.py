@@ -51,8 +51,10 @@ ROUTE_NAMES = {0: "not-applicable", 1: "annotated", 2: "dense"}
 MAX_EPS = 16
 
 # every symbol include/dbm.h declares
+DISTANCE_MODES = {"auto": 0, "exact": 1, "screened": 2}
+
 EXPORTED = (
-    "dbm_create", "dbm_destroy", "dbm_workspace_bytes", "dbm_set_phase_timing",
+    "dbm_create", "dbm_destroy", "dbm_workspace_bytes", "dbm_set_phase_timing", "dbm_set_distance_mode",
     "dbm_fit_multi", "dbm_fit_multi_host", "dbm_neighbor_counts", "dbm_batch_size", "dbm_max_bytes_for_batch_size",
     "dbm_annotate_pays", "dbm_auto_index_bits", "dbm_build_info_json",
     "dbm_neighbor_counts_noalloc", "dbm_distance_shard", "dbm_fit_multi_from_graph",
@@ -99,6 +101,9 @@ class Stats(ctypes.Structure):
         ("ms_relabel", ctypes.c_double),
         ("dist_work_fraction", ctypes.c_double),
         ("tile_pairs_kept", ctypes.c_double),
+        ("screened_tile_pairs", ctypes.c_int64),
+        ("fallback_tile_pairs", ctypes.c_int64),
+        ("screen_candidates", ctypes.c_int64),
     ]
 
     def as_dict(self) -> dict[str, Any]:
@@ -126,6 +131,8 @@ def load_library():
     lib.dbm_workspace_bytes.restype = u64
     lib.dbm_set_phase_timing.argtypes = [p, i32]
     lib.dbm_set_phase_timing.restype = None
+    lib.dbm_set_distance_mode.argtypes = [p, i32]
+    lib.dbm_set_distance_mode.restype = i32
     fit_args = [p, p, i64, i64, p, i32, p, i32, p, p, ctypes.POINTER(Options), ctypes.POINTER(Stats),
                 p, i32]
     lib.dbm_fit_multi.argtypes = fit_args + [p, cp, sz]
@@ -259,6 +266,13 @@ class DbscanMulti:
 
     def set_phase_timing(self, enabled: bool) -> None:
         self._lib.dbm_set_phase_timing(self._h, 1 if enabled else 0)
+
+    def set_distance_mode(self, mode: str) -> None:
+        """'auto' (tensor-core screen where it applies), 'exact' (exact tile kernel only) or
+        'screened' (require the screen).  Labels are identical in every mode."""
+        rc = self._lib.dbm_set_distance_mode(self._h, DISTANCE_MODES[mode])
+        if rc != DBM_OK:
+            raise DbmError(rc, f"bad distance mode {mode!r}")
 
     def _options(self, backend, index, route, neigh_per_row, max_bytes_per_batch, csr_cap_bytes):
         if backend not in BACKENDS:

@@ -105,6 +105,9 @@ typedef struct dbm_stats {
                                    pairs x D) the distance kernel computed: pruned tile pairs
                                    and warps whose pairs all exceed the largest eps stop early */
   double tile_pairs_kept;       /* fraction of tile pairs that survived the bounding-box bound */
+  int64_t screened_tile_pairs;  /* tile pairs bounded by the tensor-core screen */
+  int64_t fallback_tile_pairs;  /* of those and the unscreenable ones, handed to the exact tile kernel */
+  int64_t screen_candidates;    /* pairs the screen could not exclude (each re-evaluated exactly) */
 } dbm_stats;
 
 typedef struct dbm_handle dbm_handle;
@@ -119,6 +122,17 @@ void dbm_destroy(dbm_handle* h);
 uint64_t dbm_workspace_bytes(const dbm_handle* h);
 /* Record per-phase device times into dbm_stats.ms_* (adds stream syncs; off by default). */
 void dbm_set_phase_timing(dbm_handle* h, int enabled);
+
+/* Distance pass selection (no counterpart in the reference, whose only path is the exact
+ * per-pair search).  AUTO: the tensor-core screen bounds every surviving tile pair and the
+ * exact fp32 chain re-evaluates each candidate, whenever N >= 4096, D <= 64 and
+ * eps_max^2 >= 1e-20; otherwise the exact tile kernel.  EXACT: exact tile kernel only.
+ * SCREENED: require the screen (DBM_ERR_INVALID when it does not apply).  Results are
+ * identical in all modes. */
+#define DBM_DISTANCE_AUTO 0
+#define DBM_DISTANCE_EXACT 1
+#define DBM_DISTANCE_SCREENED 2
+int dbm_set_distance_mode(dbm_handle* h, int mode);
 
 /* ---- the fit ------------------------------------------------------------------------ */
 /*
