@@ -45,13 +45,14 @@ Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* e
 int32_t padded_dims(int32_t d);
 int64_t padded_points(int64_t n);
 size_t order_scratch_bytes(int64_t n);
-int64_t prune_blocks(int64_t pairs);
+size_t prune_scratch_bytes(int64_t tiles, int32_t d);
+int64_t prune_units(int64_t tiles);
 Status launch_tile_boxes(const float* xt, int64_t n, int64_t npad, int32_t d, float* lo, float* hi, cudaStream_t s);
-Status launch_prune_count(int64_t pairs, const float* lo, const float* hi, int32_t d, float cutoff,
-                          int32_t* counts, int64_t* offsets, void* scan_scratch, size_t scan_bytes,
+Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
+                          size_t scratch_bytes, void* scan_scratch, size_t scan_bytes, const int64_t** count_out_dev,
                           cudaStream_t s);
-Status launch_prune_write(int64_t pairs, const float* lo, const float* hi, int32_t d, float cutoff,
-                          const int64_t* offsets, long long* work, cudaStream_t s);
+Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
+                          long long* work, cudaStream_t s);
 Status spatial_order(const float* x, int64_t n, int32_t d, int32_t* perm, void* scratch, size_t scratch_bytes,
                      cudaStream_t s);
 Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
@@ -204,7 +205,7 @@ struct dbm_handle {
   uint64_t edge_cap_hint = 0;
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
-  dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_counts, prune_off, work, fallback;
+  dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_scratch, work, fallback;
   int distance_mode = DBM_DISTANCE_AUTO;
   dbm::Buffer xdev, labels_dev, core_dev;  // host-buffer entry point only
   int64_t* pinned = nullptr;               // small D2H staging
@@ -215,7 +216,7 @@ struct dbm_handle {
     const dbm::Buffer* all[] = {&xt, &hist, &deg, &cc, &rowcnt, &off, &fill, &edges, &col, &crow,
                                 &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
                                 &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz,
-                                &perm, &order_scratch, &box_lo, &box_hi, &prune_counts, &prune_off,
+                                &perm, &order_scratch, &box_lo, &box_hi, &prune_scratch,
                                 &work, &fallback};
     uint64_t s = 0;
     for (auto* b : all) s += b->bytes;
@@ -432,23 +433,21 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
   const long long* work = nullptr;
   int64_t work_count = 0;
   if (perm) {
-    const int64_t nb = prune_blocks(pairs);
     DBM_TRY(ensure(h->box_lo, sizeof(float) * static_cast<size_t>(T) * di));
     DBM_TRY(ensure(h->box_hi, sizeof(float) * static_cast<size_t>(T) * di));
-    DBM_TRY(ensure(h->prune_counts, sizeof(int32_t) * nb));
-    DBM_TRY(ensure(h->prune_off, sizeof(int64_t) * (nb + 1)));
-    DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(nb + 1)));
+    DBM_TRY(ensure(h->prune_scratch, prune_scratch_bytes(T, di)));
+    DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(prune_units(T) + 1)));
     DBM_TRY(launch_tile_boxes(as<float>(h->xt), n, padded_points(n), di, as<float>(h->box_lo), as<float>(h->box_hi), s));
-    DBM_TRY(launch_prune_count(pairs, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1],
-                               as<int32_t>(h->prune_counts), as<int64_t>(h->prune_off), h->scan_scratch.p,
-                               h->scan_scratch.bytes, s));
+    const int64_t* count_dev = nullptr;
+    DBM_TRY(launch_prune_count(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
+                               h->prune_scratch.bytes, h->scan_scratch.p, h->scan_scratch.bytes, &count_dev, s));
     h->pinned[0] = 0;
-    DBM_CUDA(cudaMemcpyAsync(h->pinned, as<int64_t>(h->prune_off) + nb, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    DBM_CUDA(cudaMemcpyAsync(h->pinned, count_dev, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     DBM_CUDA(cudaStreamSynchronize(s));
     work_count = h->pinned[0];
     DBM_TRY(ensure(h->work, sizeof(long long) * std::max<int64_t>(work_count, 1)));
-    DBM_TRY(launch_prune_write(pairs, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1],
-                               as<int64_t>(h->prune_off), as<long long>(h->work), s));
+    DBM_TRY(launch_prune_write(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
+                               as<long long>(h->work), s));
     work = as<long long>(h->work);
     st.tile_pairs_kept = pairs > 0 ? static_cast<double>(work_count) / static_cast<double>(pairs) : 1.0;
   } else {
@@ -770,7 +769,7 @@ void dbm_destroy(dbm_handle* h)
                         &h->slab_off, &h->slab_col, &h->slab_row, &h->G, &h->L, &h->best, &h->cur,
                         &h->flags, &h->rank, &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev,
                         &h->core_dev, &h->perm, &h->order_scratch, &h->box_lo, &h->box_hi,
-                        &h->prune_counts, &h->prune_off, &h->work};
+                        &h->prune_scratch, &h->work, &h->fallback};
   for (auto* b : all)
     if (b->p) cudaFree(b->p);
   if (h->pinned) cudaFreeHost(h->pinned);

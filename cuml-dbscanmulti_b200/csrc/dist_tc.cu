@@ -81,8 +81,9 @@ struct ScreenParams {
   int32_t* hist;
   int32_t* err;
   const int32_t* perm;
-  const float* box_lo;  // tiles x d
+  const float* box_lo;  // d x tiles (dim-major)
   const float* box_hi;
+  int64_t tiles;
   long long* fallback;
   float sqrt_e;         // s of the bound, rounded up
   float eps2[kMaxEps];
@@ -316,7 +317,7 @@ dist_screen_kernel(const ScreenParams p)
     // ---- tile J (operand B, fp32 copy, centre) when it changes ----
     if (J != curJ) {
       __syncthreads();  // the previous item's readers of xJ / s_c are done
-      if (tid < KP) s_c[tid] = tid < d ? 0.5f * (p.box_lo[J * d + tid] + p.box_hi[J * d + tid]) : 0.0f;
+      if (tid < KP) s_c[tid] = tid < d ? 0.5f * (p.box_lo[tid * p.tiles + J] + p.box_hi[tid * p.tiles + J]) : 0.0f;
       const bool valid = tid < cols_j;
       float xj[KP];
       load_row<KP>(p.xt, p.npad, J * kScreenTile + tid, valid, xj);
@@ -560,6 +561,7 @@ Status launch_screened_distance(const DistLaunch& a, const float* box_lo, const 
   p.perm = a.perm;
   p.box_lo = box_lo;
   p.box_hi = box_hi;
+  p.tiles = ceil_div(a.n, kScreenTile);
   p.fallback = fallback;
   for (int e = 0; e < kMaxEps; ++e) p.eps2[e] = e < a.k ? a.eps2[e] : a.eps2[a.k - 1];
   {

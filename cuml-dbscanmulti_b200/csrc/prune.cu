@@ -9,20 +9,19 @@
 // at every prefix.  Once lb > eps2[k-1] no pair of the tile pair can be a neighbour under any
 // eps: the tile pair is skipped without evaluating a single pair, and nothing else changes.
 //
-// Surviving tile pairs go to a worklist in tile-pair order (two passes: per-block counts,
-// scan, ordered write), so every rank of a sharded run sees the same list and takes an equal
-// slice of it.  Entries are the tile coordinates packed as J << 32 | I.
+// Surviving tile pairs form a worklist ordered by J, then I (one bound pass writing per-unit keep
+// masks and counts, a scan, an ordered expansion of the masks), so every rank of a sharded run sees the same list and takes an equal slice
+// of it.  Entries are the tile coordinates packed as J << 32 | I.  Boxes are stored dim-major
+// (lo[t * tiles + I]) so that the 32 lanes of a warp, testing 32 consecutive tiles I against
+// one J, read consecutive addresses.
 #include "dbm_internal.cuh"
 
 #include <algorithm>
 
 namespace dbm {
 
-constexpr int kPruneThreads = 256;
-constexpr int kPruneItems = 16;  // tile pairs per thread per block pass
-constexpr int64_t kPruneBlock = static_cast<int64_t>(kPruneThreads) * kPruneItems;
-
-// One warp per (tile, dim): min / max over the tile's valid points (columns < n of XT).
+// One warp per (tile, dim): min / max over the tile's valid points (columns < n of XT),
+// written dim-major: lo[t * tiles + tile].
 __global__ void tile_box_kernel(const float* __restrict__ xt, int64_t n, int64_t npad, int32_t d,
                                 int64_t tiles, float* __restrict__ lo, float* __restrict__ hi)
 {
@@ -46,70 +45,112 @@ __global__ void tile_box_kernel(const float* __restrict__ xt, int64_t n, int64_t
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
   }
   if (lane == 0) {
-    lo[tile * d + t] = mn;
-    hi[tile * d + t] = mx;
+    lo[static_cast<int64_t>(t) * tiles + tile] = mn;
+    hi[static_cast<int64_t>(t) * tiles + tile] = mx;
   }
 }
 
-__device__ __forceinline__ void prune_tri_coords(long long c, long long& I, long long& J)
+// Work units: (J, block of kUnitTiles consecutive tiles I <= J), J-major, blocks ascending, so
+// that the units' outputs concatenated in unit order are the worklist (J, then I ascending).
+constexpr int64_t kUnitTiles = 128;
+
+// units before tile J: sum over j < J of (j / kUnitTiles + 1), in closed form
+__host__ __device__ __forceinline__ int64_t units_before(int64_t J)
 {
-  long long j = static_cast<long long>((sqrt(8.0 * static_cast<double>(c) + 1.0) - 1.0) * 0.5);
-  while (j * (j + 1) / 2 > c) --j;
-  while ((j + 1) * (j + 2) / 2 <= c) ++j;
-  J = j;
-  I = c - j * (j + 1) / 2;
+  const int64_t q = J / kUnitTiles, r = J % kUnitTiles;
+  return J + kUnitTiles * q * (q - 1) / 2 + q * r;
 }
 
-// true when some pair of the tile pair may be within cutoff
-__device__ __forceinline__ bool tile_pair_survives(long long I, long long J, const float* __restrict__ lo,
-                                                   const float* __restrict__ hi, int32_t d, float cutoff)
+__device__ __forceinline__ void unit_coords(int64_t u, int64_t tiles, int64_t& J, int64_t& blk)
 {
-  if (I == J) return true;
-  const float* loI = lo + I * d;
-  const float* hiI = hi + I * d;
-  const float* loJ = lo + J * d;
-  const float* hiJ = hi + J * d;
-  float lb = 0.0f;
-  for (int32_t t = 0; t < d; ++t) {
-    const float g = fmaxf(0.0f, fmaxf(__fsub_rn(loJ[t], hiI[t]), __fsub_rn(loI[t], hiJ[t])));
-    lb = __fmaf_rn(g, g, lb);
-    if (lb > cutoff) return false;
+  int64_t lo = 0, hi = tiles - 1;  // largest J with units_before(J) <= u
+  while (lo < hi) {
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (units_before(mid) <= u) lo = mid;
+    else hi = mid - 1;
   }
-  return true;
+  J = lo;
+  blk = u - units_before(lo);
 }
 
-template <bool WRITE>
-__global__ void tile_prune_kernel(int64_t pairs, const float* __restrict__ lo, const float* __restrict__ hi,
-                                  int32_t d, float cutoff, int32_t* __restrict__ block_counts,
-                                  const int64_t* __restrict__ block_offsets, long long* __restrict__ work)
+// One warp per unit: the tiles I of the unit's block (I <= J) whose boxes may meet J's (I == J
+// always).  The bound's chain is checked every 4 dims, after loading those dims together (lb
+// only grows along the dims, so stopping later is as exact).  Writes the unit's keep mask
+// (bit q of word c: I = block start + 32 c + q) and its count.
+__global__ void tile_pairs_kernel(int64_t tiles, int64_t units, const float* __restrict__ lo,
+                                  const float* __restrict__ hi, int32_t d, float cutoff, int32_t* __restrict__ counts,
+                                  uint32_t* __restrict__ masks)
 {
-  __shared__ int32_t warp_tot[kPruneThreads / 32];
-  const int64_t b0 = static_cast<int64_t>(blockIdx.x) * kPruneBlock;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int64_t base = WRITE ? block_offsets[blockIdx.x] : 0;
+  const int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (u >= units) return;
+  int64_t J, blk;
+  unit_coords(u, tiles, J, blk);
   int32_t total = 0;
-  // items are taken in tile-pair order: round q covers [b0 + q*256, b0 + (q+1)*256)
-  for (int q = 0; q < kPruneItems; ++q) {
-    const long long c = b0 + static_cast<int64_t>(q) * kPruneThreads + threadIdx.x;
-    long long I = 0, J = 0;
-    if (c < pairs) prune_tri_coords(c, I, J);
-    const bool keep = c < pairs && tile_pair_survives(I, J, lo, hi, d, cutoff);
-    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
-    if (lane == 0) warp_tot[warp] = __popc(bal);
-    __syncthreads();
-    int32_t before = 0, round = 0;
-    for (int w2 = 0; w2 < kPruneThreads / 32; ++w2) {
-      if (w2 < warp) before += warp_tot[w2];
-      round += warp_tot[w2];
+  const int64_t i0 = blk * kUnitTiles;
+  const int64_t i1 = i0 + kUnitTiles - 1 < J ? i0 + kUnitTiles - 1 : J;
+#pragma unroll 1
+  for (int c = 0; c < static_cast<int>(kUnitTiles / 32); ++c) {
+    const int64_t I = i0 + 32 * c + lane;
+    bool keep = I <= i1;
+    if (keep && I != J) {
+      float lb = 0.0f;
+      for (int32_t t0 = 0; t0 < d; t0 += 4) {
+        float gq[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int32_t t = t0 + q;
+          gq[q] = 0.0f;
+          if (t < d) {
+            const int64_t ti = static_cast<int64_t>(t) * tiles;
+            gq[q] = fmaxf(0.0f, fmaxf(__fsub_rn(__ldg(lo + ti + J), __ldg(hi + ti + I)),
+                                      __fsub_rn(__ldg(lo + ti + I), __ldg(hi + ti + J))));
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) lb = __fmaf_rn(gq[q], gq[q], lb);
+        if (lb > cutoff) {
+          keep = false;
+          break;
+        }
+      }
     }
-    if (WRITE && keep) work[base + total + before + __popc(bal & ((1u << lane) - 1u))] = (J << 32) | I;
-    total += round;
-    __syncthreads();
+    const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+    if (lane == 0) masks[u * (kUnitTiles / 32) + c] = bal;
+    total += __popc(bal);
   }
-  if (!WRITE && threadIdx.x == 0) block_counts[blockIdx.x] = total;
+  if (lane == 0) counts[u] = total;
 }
 
-int64_t prune_blocks(int64_t pairs) { return ceil_div(pairs, kPruneBlock); }
+// One warp per unit: its kept tiles as packed worklist entries at off[u] ..., I ascending.
+__global__ void tile_pairs_write_kernel(int64_t tiles, int64_t units, const uint32_t* __restrict__ masks,
+                                        const int64_t* __restrict__ off, long long* __restrict__ work)
+{
+  const int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (u >= units) return;
+  int64_t J, blk;
+  unit_coords(u, tiles, J, blk);
+  int64_t at = off[u];
+#pragma unroll
+  for (int c = 0; c < static_cast<int>(kUnitTiles / 32); ++c) {
+    const uint32_t m = masks[u * (kUnitTiles / 32) + c];
+    if ((m >> lane) & 1u) work[at + __popc(m & ((1u << lane) - 1u))] = (J << 32) | (blk * kUnitTiles + 32 * c + lane);
+    at += __popc(m);
+  }
+}
+
+// ---- host side ----------------------------------------------------------------------------------
+
+int64_t prune_units(int64_t tiles) { return units_before(tiles); }
+
+size_t prune_scratch_bytes(int64_t tiles, int32_t d)
+{
+  (void)d;
+  const int64_t units = units_before(tiles);
+  return align_up(sizeof(int32_t) * units, 256) + align_up(sizeof(int64_t) * (units + 1), 256) +
+         align_up(sizeof(uint32_t) * units * (kUnitTiles / 32), 256);
+}
 
 Status launch_tile_boxes(const float* xt, int64_t n, int64_t npad, int32_t d, float* lo, float* hi, cudaStream_t s)
 {
@@ -121,27 +162,43 @@ Status launch_tile_boxes(const float* xt, int64_t n, int64_t npad, int32_t d, fl
   return Status::Ok();
 }
 
-// pass 1: per-block survivor counts and their exclusive scan (offsets[nb] = total)
-Status launch_prune_count(int64_t pairs, const float* lo, const float* hi, int32_t d, float cutoff,
-                          int32_t* counts, int64_t* offsets, void* scan_scratch, size_t scan_bytes,
+// per-J counts and their scan: afterwards the worklist length is at *count_out_dev
+Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
+                          size_t scratch_bytes, void* scan_scratch, size_t scan_bytes, const int64_t** count_out_dev,
                           cudaStream_t s)
 {
-  const int64_t nb = prune_blocks(pairs);
+  if (scratch_bytes < prune_scratch_bytes(tiles, d)) return Status::Err(DBM_ERR_INVALID, "prune scratch too small");
+  const int64_t units = units_before(tiles);
+  unsigned char* sp = static_cast<unsigned char*>(scratch);
+  int32_t* counts = reinterpret_cast<int32_t*>(sp);
+  int64_t* off = reinterpret_cast<int64_t*>(sp + align_up(sizeof(int32_t) * units, 256));
+  uint32_t* masks = reinterpret_cast<uint32_t*>(sp + align_up(sizeof(int32_t) * units, 256) +
+                                                align_up(sizeof(int64_t) * (units + 1), 256));
   count_launch();
-  tile_prune_kernel<false><<<static_cast<unsigned>(nb), kPruneThreads, 0, s>>>(pairs, lo, hi, d, cutoff, counts,
-                                                                                nullptr, nullptr);
+  tile_pairs_kernel<<<static_cast<unsigned>(ceil_div(units * 32, 256)), 256, 0, s>>>(tiles, units, lo, hi, d, cutoff,
+                                                                                   counts, masks);
   DBM_CUDA(cudaGetLastError());
-  return exclusive_scan_i32(counts, offsets, nb, scan_scratch, scan_bytes, s);
+  DBM_TRY(exclusive_scan_i32(counts, off, units, scan_scratch, scan_bytes, s));
+  *count_out_dev = off + units;
+  return Status::Ok();
 }
 
-// pass 2: surviving tile-pair indices, in tile-pair order
-Status launch_prune_write(int64_t pairs, const float* lo, const float* hi, int32_t d, float cutoff,
-                          const int64_t* offsets, long long* work, cudaStream_t s)
+// the packed worklist entries, J ascending then I ascending
+Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
+                          long long* work, cudaStream_t s)
 {
-  const int64_t nb = prune_blocks(pairs);
+  (void)lo;
+  (void)hi;
+  (void)d;
+  (void)cutoff;
+  const int64_t units = units_before(tiles);
+  const unsigned char* sp = static_cast<const unsigned char*>(scratch);
+  const int64_t* off = reinterpret_cast<const int64_t*>(sp + align_up(sizeof(int32_t) * units, 256));
+  const uint32_t* masks = reinterpret_cast<const uint32_t*>(sp + align_up(sizeof(int32_t) * units, 256) +
+                                                            align_up(sizeof(int64_t) * (units + 1), 256));
   count_launch();
-  tile_prune_kernel<true><<<static_cast<unsigned>(nb), kPruneThreads, 0, s>>>(pairs, lo, hi, d, cutoff, nullptr,
-                                                                              offsets, work);
+  tile_pairs_write_kernel<<<static_cast<unsigned>(ceil_div(units * 32, 256)), 256, 0, s>>>(tiles, units, masks, off,
+                                                                                         work);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
