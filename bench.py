@@ -278,6 +278,74 @@ def run_reference(args, cfg) -> None:
     print(json.dumps(out), flush=True)
 
 
+def screen_roofline(stats, screen_ms, d, n, ws, dms, sm_mhz, args) -> dict:
+    """Roofline of dist_screen_kernel: tcgen05 tf32 GEMM work of the screen (128 x 128 x KP per
+    screened tile pair, FMA = 2 flops) over the kernel's own event-timed duration, against the
+    tf32 dense peak taken as half the measured bf16 GEMM rate."""
+    kp = 8 * ((d + 4 + 7) // 8)
+    screened = int(stats.get("screened_tile_pairs", 0))
+    sms = float(np.mean(screen_ms)) if screen_ms else float("nan")
+    flops = float(screened) * 128 * 128 * kp * 2
+    achieved = flops / (sms * 1e-3) / 1e12
+    mp = measured_peaks()
+    bf16 = mp.get("bf16_tflops")
+    peak = bf16 / 2 if bf16 else 1590.0 / 2
+    cands = int(stats.get("screen_candidates", 0))
+    traffic = None
+    tp = ROOT / "profiles" / "dist_screen_kernel_traffic.json"
+    if tp.exists() and not args.n and ws == 1:
+        try:
+            traffic = json.loads(tp.read_text()).get(args.config)
+        except Exception:
+            traffic = None
+    pairs_bounded = float(screened) * 128 * 128
+    return {
+        "bound": "tensor", "kernel": "dist_screen_kernel", "achieved": achieved, "peak": peak,
+        "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
+        "peak_source": ("tf32 dense = 1/2 of the measured bf16 cuBLAS rate in MEASURED_PEAKS.json" if bf16
+                        else "tf32 dense = 1/2 of the fallback bf16 rate"),
+        "traffic": traffic, "flops_per_launch": flops, "ms_per_launch": sms,
+        "screened_tile_pairs": screened, "pairs_bounded_per_s": pairs_bounded / (sms * 1e-3),
+        "candidates": cands, "exact_chain_pairs": cands,
+        "exact_chain_flops": float(cands) * 3 * d,
+        "fallback_tile_pairs": int(stats.get("fallback_tile_pairs", 0)),
+        "tile_pairs_kept": stats.get("tile_pairs_kept"),
+        "distance_phase_ms": dms,
+        "accounting": ("unit = one screened 128x128 tile pair: 128*128*KP tf32 multiply-adds (KP = D + 4 "
+                       "rounded to 8: centred coordinates + the two split bound terms); the kernel also runs "
+                       "the exact fp32 chain (3D flops) for every candidate pair, reported separately. The "
+                       "tensor fraction is low by design: the kernel is bound by CUDA-core issue of the "
+                       "operand build and the screen epilogue, not by the MMA."),
+    }
+
+
+def exact_roofline(stats, unique_pairs, d, dms, sm_mhz, torch, dev, args, ws) -> dict:
+    """Roofline of dist_tri_kernel (the exact fp32 tile kernel, used when the screen does not
+    apply): flops actually evaluated over the distance phase."""
+    flops = unique_pairs * 3.0 * d  # D FSUB + D FFMA (FMA = 2 flops)
+    work_frac = float(stats.get("dist_work_fraction", 1.0) or 1.0)
+    flops_exec = flops * work_frac
+    achieved = flops_exec / (dms * 1e-3) / 1e12
+    peak = sgemm_fp32_peak(torch, dev)
+    nominal = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+    lane_frac = (unique_pairs * 2.0 * d * work_frac) / (dms * 1e-3) / (148 * 128 * sm_mhz * 1e6)
+    traffic = None
+    tp = ROOT / "profiles" / "dist_tri_kernel_traffic.json"
+    if tp.exists() and not args.n and ws == 1:
+        try:
+            traffic = json.loads(tp.read_text()).get(args.config)
+        except Exception:
+            traffic = None
+    return {"bound": "fp32", "kernel": "dist_tri_kernel", "achieved": achieved,
+            "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
+            "peak_source": "measured here: cuBLAS SGEMM 8192^3, TF32 off (no FP32 figure in MEASURED_PEAKS.json)",
+            "peak_nominal": nominal, "fp32_lane_utilisation": lane_frac,
+            "flops_per_launch": flops_exec, "ms_per_launch": dms, "executed_fraction": work_frac,
+            "full_grid_flops": flops, "attainable_frac": 0.75, "traffic": traffic,
+            "accounting": "flops evaluated: unique pairs N(N-1)/2 x 3D flops (D FSUB + D FFMA, FMA = 2) x "
+                          "executed_fraction; under this accounting the ceiling is 75% of the FMA-counted peak"}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -349,7 +417,11 @@ def main() -> None:
             r = parallel.sharded_fit_multi(stages, x, eps, ms, **kw)
             labels.copy_(r.labels)
             r.stats["ms_distance"] = dist_ms_box[-1]
-            r.stats["launches"] = r.stats.get("launches", 0)
+            sh = stages.last_shard_stats
+            for key in ("ms_screen", "screened_tile_pairs", "fallback_tile_pairs", "screen_candidates",
+                        "tile_pairs_kept", "dist_work_fraction"):
+                r.stats[key] = sh.get(key, 0)
+            r.stats["launches"] = r.stats.get("launches", 0) + sh.get("launches", 0)
             return r
     else:
         def one_fit():
@@ -362,7 +434,7 @@ def main() -> None:
 
     clocks = ClockSampler(local)
     clocks.start()
-    times, dist_ms, stats = [], [], None
+    times, dist_ms, screen_ms, stats = [], [], [], None
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
@@ -376,6 +448,7 @@ def main() -> None:
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
         dist_ms.append(r.stats["ms_distance"])
+        screen_ms.append(r.stats.get("ms_screen", 0.0))
         stats = r.stats
     torch.cuda.synchronize()
     if ws > 1:
@@ -400,24 +473,15 @@ def main() -> None:
     else:
         e2e_value, e2e_s = e2e_leg(h, pts, eps, ms, kw, labels, flush, args.steps, ws, dev, torch, dist,
                                    pairs)
-    # roofline of the dominant kernel (the distance pass): FP32 pipes (this rank's share)
+    # roofline of the dominant kernel (this rank's share)
     unique_pairs = n * (n - 1) / 2 / ws
-    flops = unique_pairs * 3.0 * d  # D FSUB + D FFMA (FMA = 2 flops)
     dms = float(np.mean(dist_ms)) if dist_ms else float("nan")
-    work_frac = float(stats.get("dist_work_fraction", 1.0) or 1.0)
-    flops_exec = flops * work_frac  # pair-dims actually evaluated (warps stop once beyond eps)
-    achieved = flops_exec / (dms * 1e-3) / 1e12
-    peak = sgemm_fp32_peak(torch, dev)
     sm_mhz = clk.get("sm_mhz") or 1965.0
-    nominal = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
-    lane_frac = (unique_pairs * 2.0 * d * work_frac) / (dms * 1e-3) / (148 * 128 * sm_mhz * 1e6)
-    traffic_path = ROOT / "profiles" / "dist_tri_kernel_traffic.json"
-    traffic = None
-    if traffic_path.exists() and not args.n and ws == 1:
-        try:
-            traffic = json.loads(traffic_path.read_text()).get(args.config)
-        except Exception:
-            traffic = None
+    screened = int(stats.get("screened_tile_pairs", 0) or 0)
+    if screened > 0:
+        roofline = screen_roofline(stats, screen_ms, d, n, ws, dms, sm_mhz, args)
+    else:
+        roofline = exact_roofline(stats, unique_pairs, d, dms, sm_mhz, torch, dev, args, ws)
 
     if rank == 0:
         cb = None
@@ -445,27 +509,16 @@ def main() -> None:
                        "l2": "flushed (256 MB write) between timed steps"},
             "gpu_launches": (int(stats.get("launches", 0)) + (2 if ws > 1 else 0)) * args.steps,
             "clocks": clk,
-            "roofline": {"bound": "fp32", "kernel": "dist_tri_kernel", "achieved": achieved,
-                         "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak if peak else None,
-                         "peak_source": "measured here: cuBLAS SGEMM 8192^3, TF32 off (no FP32 figure "
-                                        "in MEASURED_PEAKS.json)",
-                         "peak_nominal": nominal, "fp32_lane_utilisation": lane_frac,
-                         "flops_per_launch": flops_exec, "ms_per_launch": dms,
-                         "executed_fraction": work_frac,
-                         "full_grid_flops": flops,
-                         "attainable_frac": 0.75,
-                         "traffic": traffic,
-                         "accounting": "flops evaluated: unique pairs N(N-1)/2 x 3D flops (D FSUB + D FFMA, "
-                                       "FMA = 2) x executed_fraction (warps whose pairs all exceed the largest "
-                                       "eps skip their remaining dims); under this accounting the ceiling is "
-                                       "75% of the FMA-counted peak (each FSUB is one flop in a two-flop slot)"},
+            "roofline": roofline,
             "e2e": None if e2e_value is None else {
                 "value": e2e_value, "unit": "pairs/s",
                 "h2d_bytes_per_step": int(n * d * 4), "d2h_bytes_per_step": int(k * l * n * 4),
                 "ms_per_step": e2e_s / args.steps * 1e3},
             "graph": {"edges": stats["edges"], "total_nnz_max_eps": stats["total_nnz_max_eps"],
                       "distance_passes": stats["distance_passes"]},
-            "phase_ms": {"distance": dms},
+            "phase_ms": {"distance": dms, "screen_kernel": float(np.mean(screen_ms)) if screen_ms else None,
+                         "graph": stats.get("ms_graph"), "label": stats.get("ms_label"),
+                         "relabel": stats.get("ms_relabel")},
             "cpu_baseline": cb,
             "hbm_peak_gbs": measured_peaks().get("hbm_gbs"),
         }

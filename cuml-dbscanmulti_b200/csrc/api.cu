@@ -465,7 +465,10 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
                  as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards, perm,
                  work, work_count};
     if (screen) {
-      DBM_TRY(launch_screened_distance(a, as<float>(h->box_lo), as<float>(h->box_hi), as<long long>(h->fallback), s));
+      {
+        PhaseTimer ts(h, s, &st.ms_screen);
+        DBM_TRY(launch_screened_distance(a, as<float>(h->box_lo), as<float>(h->box_hi), as<long long>(h->fallback), s));
+      }
       DistLaunch f = a;
       f.shard = 0;
       f.nshards = 1;
@@ -885,7 +888,8 @@ int dbm_fit_multi_host(dbm_handle* h, const float* x_host, int64_t n, int64_t d,
 
 int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host,
                        int k, int shard, int nshards, int32_t* hist_dev, uint64_t* edges_dev,
-                       uint64_t edge_cap, uint64_t* edges_found, void* stream, char* err, size_t err_len)
+                       uint64_t edge_cap, uint64_t* edges_found, dbm_stats* stats, void* stream, char* err,
+                       size_t err_len)
 {
   if (!h) {
     dbm::set_err(err, err_len, "null handle");
@@ -902,9 +906,12 @@ int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, 
     dbm::square_eps(eps_host, k, eps2);
     dbm_stats st;
     std::memset(&st, 0, sizeof(st));
+    const int64_t launches0 = dbm::launches_so_far();
     uint64_t found = 0;
     r = dbm::distance_stage(h, x_dev, n, d, eps2, k, shard, nshards, hist_dev, edge_cap, &found, st, s);
     dbm::resolve_phase_timers(h);
+    st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
+    if (stats) *stats = st;
     if (r.ok()) {
       *edges_found = found;
       if (found <= edge_cap && found > 0) {

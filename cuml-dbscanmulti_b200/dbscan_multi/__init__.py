@@ -104,6 +104,7 @@ class Stats(ctypes.Structure):
         ("screened_tile_pairs", ctypes.c_int64),
         ("fallback_tile_pairs", ctypes.c_int64),
         ("screen_candidates", ctypes.c_int64),
+        ("ms_screen", ctypes.c_double),
     ]
 
     def as_dict(self) -> dict[str, Any]:
@@ -139,7 +140,8 @@ def load_library():
     lib.dbm_fit_multi.restype = i32
     lib.dbm_fit_multi_host.argtypes = fit_args + [cp, sz]
     lib.dbm_fit_multi_host.restype = i32
-    lib.dbm_distance_shard.argtypes = [p, p, i64, i64, p, i32, i32, i32, p, p, u64, ctypes.POINTER(u64), p, cp, sz]
+    lib.dbm_distance_shard.argtypes = [p, p, i64, i64, p, i32, i32, i32, p, p, u64, ctypes.POINTER(u64),
+                                       ctypes.POINTER(Stats), p, cp, sz]
     lib.dbm_distance_shard.restype = i32
     lib.dbm_fit_multi_from_graph.argtypes = [p, i64, i64, p, i32, p, i32, p, p, u64, i32, i32, p, p,
                                              ctypes.POINTER(Options), ctypes.POINTER(Stats), p, i32, p, cp, sz]

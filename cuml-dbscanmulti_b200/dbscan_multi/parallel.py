@@ -48,6 +48,7 @@ class DeviceStages:
     def __init__(self, handle: DbscanMulti):
         self.h = handle
         self.lib = handle._lib
+        self.last_shard_stats: dict[str, Any] = {}
 
     def default_budget(self) -> int:
         """80% of (free + this handle's reusable workspace), as the reference's fit_multi."""
@@ -76,12 +77,15 @@ class DeviceStages:
         for _ in range(2):
             edges = torch.empty(cap, dtype=torch.int64, device=x.device)
             found = ctypes.c_uint64(0)
+            st = Stats()
             rc = self.lib.dbm_distance_shard(self.h._h, ctypes.c_void_p(x.data_ptr()), n, d,
                                              eps.ctypes.data_as(ctypes.c_void_p), k, shard, nshards,
                                              ctypes.c_void_p(hist.data_ptr()), ctypes.c_void_p(edges.data_ptr()),
-                                             cap, ctypes.byref(found), ctypes.c_void_p(s), err, len(err))
+                                             cap, ctypes.byref(found), ctypes.byref(st), ctypes.c_void_p(s), err,
+                                             len(err))
             if rc != DBM_OK:
                 raise DbmError(rc, err.value.decode())
+            self.last_shard_stats = st.as_dict()
             if found.value <= cap:
                 return hist, edges[: found.value]
             cap = int(found.value)

@@ -108,6 +108,7 @@ typedef struct dbm_stats {
   int64_t screened_tile_pairs;  /* tile pairs bounded by the tensor-core screen */
   int64_t fallback_tile_pairs;  /* of those and the unscreenable ones, handed to the exact tile kernel */
   int64_t screen_candidates;    /* pairs the screen could not exclude (each re-evaluated exactly) */
+  double ms_screen;             /* device time of the screened-pass kernel alone, if timing enabled */
 } dbm_stats;
 
 typedef struct dbm_handle dbm_handle;
@@ -176,7 +177,9 @@ int dbm_fit_multi_host(dbm_handle* h, const float* x_host, int64_t n, int64_t d,
  * Replaces the reference's pass-1 search over a row batch (runner_multi.cuh:627-655). */
 int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host,
                        int k, int shard, int nshards, int32_t* hist_dev, uint64_t* edges_dev,
-                       uint64_t edge_cap, uint64_t* edges_found, void* stream, char* err, size_t err_len);
+                       uint64_t edge_cap, uint64_t* edges_found, dbm_stats* stats /* optional: the
+                       distance-pass fields (timers, screen and pruning counts) */, void* stream,
+                       char* err, size_t err_len);
 
 /* Everything after the distance pass, from the complete per-code histograms (summed over all
  * shards) and the complete list of neighbour pairs: degrees, core masks, CSR, batch plan and
