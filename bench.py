@@ -79,65 +79,81 @@ def make_points(cfg: dict, seed: int = 0) -> np.ndarray:
 
 # ---- clocks during the timed region: a separate nvidia-smi process (reads only) ----------------
 class ClockSampler:
-    """Samples SM clocks and throttle reasons every 50 ms in a child nvidia-smi process, so the
-    sampling never competes with this process for the interpreter lock."""
+    """Samples SM clocks and clock-event reasons every 20 ms in a child process (NVML through
+    nvidia_ml_py, else nvidia-smi -lms 20), each sample time-stamped; stop() keeps the samples
+    that fall inside the marked timed region, so sampling never competes with this process for
+    the interpreter lock and a short region still gets samples."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,utilization.gpu,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    CHILD = r"""
+import sys, time
+import pynvml as N
+N.nvmlInit()
+h = N.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
+mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+get = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or N.nvmlDeviceGetCurrentClocksThrottleReasons
+out = open(sys.argv[2], "w", buffering=1)
+while True:
+    out.write("%.6f,%d,%d,%d\n" % (time.time(), N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM), mx, get(h)))
+    time.sleep(0.02)
+"""
+    # NVML clock-event reason bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, device: int):
-        import shutil
         import tempfile
 
         self.device = device
         self.proc = None
-        self.path = None
-        self.smi = shutil.which("nvidia-smi")
+        self.t0 = self.t1 = None
         self.tmp = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
+        self.tmp.close()
 
     def start(self):
         import subprocess
+        import sys as _sys
 
-        if not self.smi:
-            return
-        self.proc = subprocess.Popen([self.smi, "-i", str(self.device), f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits", "-lms", "50"],
-                                     stdout=self.tmp, stderr=subprocess.DEVNULL)
+        try:
+            import pynvml  # noqa: F401
+            self.proc = subprocess.Popen([_sys.executable, "-c", self.CHILD, str(self.device), self.tmp.name],
+                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def stop(self) -> dict:
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi-unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml-unavailable"]}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        self.tmp.flush()
-        self.tmp.seek(0)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        clocks, reasons, max_mhz, rows = [], set(), None, 0
-        for line in self.tmp.read().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                mhz, mx, util = float(parts[0]), float(parts[1]), float(parts[2])
-            except ValueError:
-                continue
-            rows += 1
-            max_mhz = mx
-            if util > 50:
-                clocks.append(mhz)
-                for nm, flag in zip(names, parts[3:7]):
-                    if flag.lower() == "active":
-                        reasons.add(nm)
+        rows = []
+        with open(self.tmp.name) as f:
+            for line in f:
+                parts = line.strip().split(",")
+                if len(parts) == 4:
+                    try:
+                        rows.append((float(parts[0]), float(parts[1]), float(parts[2]), int(parts[3])))
+                    except ValueError:
+                        pass
         try:
             os.unlink(self.tmp.name)
         except OSError:
             pass
-        return {"sm_mhz": float(np.median(clocks)) if clocks else None, "sm_max_mhz": max_mhz,
-                "reasons": sorted(reasons), "samples_under_load": len(clocks), "samples": rows}
+        t0, t1 = self.t0 or 0.0, self.t1 or time.time()
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        reasons = sorted({nm for r in inside for nm, bit in self.BITS.items() if r[3] & bit})
+        clocks = [r[1] for r in inside]
+        return {"sm_mhz": float(np.median(clocks)) if clocks else None,
+                "sm_max_mhz": rows[-1][2] if rows else None, "reasons": reasons,
+                "samples_in_timed_region": len(inside), "samples": len(rows),
+                "timed_region_s": t1 - t0, "sampler": "NVML every 20 ms in a child process"}
 
 
 def measured_peaks() -> dict:
@@ -426,18 +442,19 @@ def main() -> None:
     else:
         def one_fit():
             return h.fit_multi(x, eps, ms, labels_out=labels, **kw)
+    clocks = ClockSampler(local)
+    clocks.start()
     for _ in range(args.warmup):
         one_fit()
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
 
-    clocks = ClockSampler(local)
-    clocks.start()
     times, dist_ms, screen_ms, stats = [], [], [], None
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
+    clocks.mark_start()
     for _ in range(args.steps):
         flush.zero_()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -451,6 +468,7 @@ def main() -> None:
         screen_ms.append(r.stats.get("ms_screen", 0.0))
         stats = r.stats
     torch.cuda.synchronize()
+    clocks.mark_end()
     if ws > 1:
         dist.barrier()
     clk = clocks.stop()
