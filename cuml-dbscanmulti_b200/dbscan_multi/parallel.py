@@ -11,7 +11,8 @@ path).  Here the work shards without changing a single label:
 3. every rank labels a contiguous range of the k*l configurations from the complete graph
    (``dbm_fit_multi_from_graph``), with a batch plan that is identical on all ranks because the
    budget and the CSR memory cap are agreed first (minimum over ranks);
-4. the label rows are all-gathered, so every rank ends with the full (k*l, N) result.
+4. the label rows are all-gathered (in place when the configs split evenly), so every rank ends
+   with the full (k*l, N) result.
 
 The collectives run on whatever backend the process group has (NCCL over NVLink on B200s,
 gloo for the CPU tests).  The kernel work sits behind a ``stages`` object so the tests can
@@ -121,11 +122,34 @@ def _all_gather_varlen(dist, t, group):
     dist.all_gather(counts, cnt, group=group)
     counts = [int(c.item()) for c in counts]
     mx = max(counts) if counts else 0
-    buf = torch.zeros(max(mx, 1), dtype=t.dtype, device=t.device)
+    buf = torch.empty(max(mx, 1), dtype=t.dtype, device=t.device)
     buf[: t.numel()] = t
     out = [torch.empty_like(buf) for _ in range(world)]
     dist.all_gather(out, buf, group=group)
     return [o[:c] for o, c in zip(out, counts)]
+
+
+def _gather_config_rows(dist, labels, C: int, n: int, group):
+    """Every rank holds the rows config_range(C, r, world) of a (C, n) label matrix; returns the
+    full matrix on every rank.  The row counts are known on every rank (no count exchange); with
+    equal shares the gather is in place into `labels` itself, else through a padded buffer."""
+    import torch
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    ranges = [config_range(C, r, world) for r in range(world)]
+    sizes = [b - a for a, b in ranges]
+    if min(sizes) == max(sizes):
+        flat = labels.reshape(-1)
+        per = sizes[0] * n
+        dist.all_gather_into_tensor(flat, flat[rank * per:(rank + 1) * per], group=group)
+        return labels
+    mx = max(sizes)
+    a, b = ranges[rank]
+    send = torch.zeros((mx, n), dtype=labels.dtype, device=labels.device)
+    send[: b - a] = labels[a:b]
+    out = torch.empty((world * mx, n), dtype=labels.dtype, device=labels.device)
+    dist.all_gather_into_tensor(out, send, group=group)
+    return torch.cat([out[r * mx: r * mx + sizes[r]] for r in range(world)])
 
 
 def sharded_fit_multi(stages, x, eps, min_samples, *, group=None, max_bytes_per_batch: int = 0,
@@ -161,9 +185,7 @@ def sharded_fit_multi(stages, x, eps, min_samples, *, group=None, max_bytes_per_
 
     c0, c1 = config_range(k * l, rank, world)
     labels, stats, routes = stages.fit_from_graph(n, d, e, m, hist, all_edges, c0, c1, opt)
-    mine = labels[c0:c1].reshape(-1)
-    rows = _all_gather_varlen(dist, mine, group)
-    full = torch.cat(rows).reshape(k * l, n)
+    full = _gather_config_rows(dist, labels, k * l, n, group)
     stats = dict(stats)
     stats["world_size"] = world
     stats["edges"] = int(all_edges.numel())

@@ -189,3 +189,26 @@ def test_a_failing_rank_is_detected_by_the_others(tmp_path):
     o1 = (tmp_path / "outcome_1.txt").read_text()
     assert "injected failure" in o1
     assert o0 != "ok"
+
+
+def _gather_worker(rank, world, port, C, n, result_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        a, b = parallel.config_range(C, rank, world)
+        labels = torch.full((C, n), -9, dtype=torch.int32)
+        labels[a:b] = torch.arange(a * n, b * n, dtype=torch.int32).reshape(b - a, n)
+        full = parallel._gather_config_rows(dist, labels, C, n, None)
+        np.save(os.path.join(result_dir, f"rows_{rank}.npy"), full.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("C,world", [(5, 2), (7, 3), (6, 3), (1, 2)])
+def test_label_rows_gather_even_and_uneven_splits(tmp_path, C, world):
+    n = 11
+    mp.spawn(_gather_worker, args=(world, _free_port(), C, n, str(tmp_path)), nprocs=world, join=True)
+    want = np.arange(C * n, dtype=np.int32).reshape(C, n)
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"rows_{r}.npy"), want)
