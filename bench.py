@@ -88,21 +88,23 @@ class ClockSampler:
 import sys, time
 import pynvml as N
 N.nvmlInit()
-h = N.nvmlDeviceGetHandleByIndex(int(sys.argv[1]))
-mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+hs = [N.nvmlDeviceGetHandleByIndex(int(i)) for i in sys.argv[1].split(",")]
+mx = [N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM) for h in hs]
 get = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or N.nvmlDeviceGetCurrentClocksThrottleReasons
 out = open(sys.argv[2], "w", buffering=1)
 while True:
-    out.write("%.6f,%d,%d,%d\n" % (time.time(), N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM), mx, get(h)))
+    t = time.time()
+    for h, m in zip(hs, mx):
+        out.write("%.6f,%d,%d,%d\n" % (t, N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM), m, get(h)))
     time.sleep(0.02)
 """
     # NVML clock-event reason bits
     BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, device: int):
+    def __init__(self, devices):
         import tempfile
 
-        self.device = device
+        self.devices = ",".join(str(int(x)) for x in devices)
         self.proc = None
         self.t0 = self.t1 = None
         self.tmp = tempfile.NamedTemporaryFile(mode="w+", suffix=".csv", delete=False)
@@ -114,7 +116,7 @@ while True:
 
         try:
             import pynvml  # noqa: F401
-            self.proc = subprocess.Popen([_sys.executable, "-c", self.CHILD, str(self.device), self.tmp.name],
+            self.proc = subprocess.Popen([_sys.executable, "-c", self.CHILD, self.devices, self.tmp.name],
                                          stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -373,6 +375,7 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling runs)")
     ap.add_argument("--n", type=int, default=0, help="override N (small cases for ncu captures)")
+    ap.add_argument("--no-clocks", action="store_true", help="diagnostics: time without the clock sampler")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.n:
@@ -442,8 +445,11 @@ def main() -> None:
     else:
         def one_fit():
             return h.fit_multi(x, eps, ms, labels_out=labels, **kw)
-    clocks = ClockSampler(local)
-    clocks.start()
+    # one sampler for all of this node's GPUs, on rank 0 only (a poller per rank measurably slows
+    # the host side of a sharded fit); --no-clocks is for diagnostics only
+    clocks = ClockSampler(range(ws) if ws > 1 else [local])
+    if rank == 0 and not args.no_clocks:
+        clocks.start()
     for _ in range(args.warmup):
         one_fit()
     torch.cuda.synchronize()
@@ -473,10 +479,14 @@ def main() -> None:
         dist.barrier()
     clk = clocks.stop()
     total_ms = float(np.sum(times))
+    rank_spread = None
     if ws > 1:
         t = torch.tensor([total_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t2 = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(t2, op=dist.ReduceOp.MIN)
         total_ms = float(t.item())
+        rank_spread = [float(t2.item()) / args.steps, total_ms / args.steps]
     ms_per_step = total_ms / args.steps
     pairs = float(n) * float(n)
     value = pairs * (1 if ws > 1 else ws) * args.steps / (total_ms * 1e-3)
@@ -534,6 +544,7 @@ def main() -> None:
                 "ms_per_step": e2e_s / args.steps * 1e3},
             "graph": {"edges": stats["edges"], "total_nnz_max_eps": stats["total_nnz_max_eps"],
                       "distance_passes": stats["distance_passes"]},
+            "rank_ms_per_step_min_max": rank_spread,
             "phase_ms": {"distance": dms, "screen_kernel": float(np.mean(screen_ms)) if screen_ms else None,
                          "graph": stats.get("ms_graph"), "label": stats.get("ms_label"),
                          "relabel": stats.get("ms_relabel")},
