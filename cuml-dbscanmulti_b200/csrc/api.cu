@@ -46,6 +46,9 @@ int32_t padded_dims(int32_t d);
 int64_t padded_points(int64_t n);
 size_t order_scratch_bytes(int64_t n);
 size_t prune_scratch_bytes(int64_t tiles, int32_t d);
+size_t core_indices_scratch_bytes(int64_t n);
+Status launch_core_indices(const uint8_t* core, int64_t n, int configs, int32_t* out, void* scratch,
+                           size_t scratch_bytes, cudaStream_t s);
 int64_t prune_units(int64_t tiles);
 Status launch_tile_boxes(const float* xt, int64_t n, int64_t npad, int32_t d, float* lo, float* hi, cudaStream_t s);
 Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
@@ -648,7 +651,9 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
       max_eps.col = reinterpret_cast<const int32_t*>(h->col.p) + base;
       max_eps.count = count;
       MultiSlab ms;
-      if (routes[b] == DBM_BATCH_DENSE || ne == 0) {
+      // smaller-eps slabs are only needed when this call owns a config of a smaller eps
+      const bool owns_small_eps = cfg_begin < ne * l;
+      if (routes[b] == DBM_BATCH_DENSE || ne == 0 || !owns_small_eps) {
         // direct: eps membership straight from each max-eps entry's code, no per-eps copies
         ms.direct = 1;
         ms.nslabs = 1;
@@ -785,6 +790,31 @@ uint64_t dbm_workspace_bytes(const dbm_handle* h) { return h ? h->workspace_byte
 void dbm_set_phase_timing(dbm_handle* h, int enabled)
 {
   if (h) h->timing = enabled != 0;
+}
+
+int dbm_core_sample_indices(dbm_handle* h, const uint8_t* core_dev, int64_t n, int configs, int32_t* out_dev,
+                            void* stream, char* err, size_t err_len)
+{
+  if (!h) {
+    dbm::set_err(err, err_len, "null handle");
+    return DBM_ERR_INVALID;
+  }
+  dbm::Status r;
+  if (!core_dev || !out_dev || n < 1 || configs < 1 || n >= (int64_t(1) << 31))
+    r = dbm::Status::Err(DBM_ERR_INVALID, "core mask and output are required, n in [1, 2^31), configs >= 1");
+  if (r.ok()) {
+    cudaSetDevice(h->device);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+    r = dbm::ensure(h->scan_scratch, dbm::core_indices_scratch_bytes(n));
+    if (r.ok())
+      r = dbm::launch_core_indices(core_dev, n, configs, out_dev, h->scan_scratch.p, h->scan_scratch.bytes, s);
+    if (r.ok()) {
+      const cudaError_t e = cudaStreamSynchronize(s);
+      if (e != cudaSuccess) r = dbm::Status::Err(DBM_ERR_CUDA, cudaGetErrorString(e));
+    }
+  }
+  dbm::set_err(err, err_len, r.msg);
+  return r.code;
 }
 
 int dbm_set_distance_mode(dbm_handle* h, int mode)

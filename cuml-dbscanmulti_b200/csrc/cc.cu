@@ -68,10 +68,15 @@ __device__ __forceinline__ void for_each_entry(const CcArgs& a, F&& f)
       const uint32_t w = static_cast<uint32_t>(s.col[q]);
       const int32_t j = static_cast<int32_t>(w & kColMask);
       const int32_t r = s.row[q];
-      for (int e = static_cast<int>(w >> kCodeShift); e < a.k; ++e) f(e, r, j);
+      const int e0 = max(static_cast<int>(w >> kCodeShift), a.cfg_begin / a.l);
+      const int e1 = min(a.k, (a.cfg_end + a.l - 1) / a.l);  // owned eps [e0, e1)
+      for (int e = e0; e < e1; ++e) f(e, r, j);
     }
   } else {
     for (int e = 0; e < a.ms.nslabs; ++e) {
+      int m_lo, m_hi;
+      cfg_range(a, e, m_lo, m_hi);
+      if (m_lo >= m_hi) continue;  // no config of this eps is owned by this call
       const SlabRef& s = a.ms.s[e];
       const int64_t b = s.begin_dev ? *s.begin_dev : 0;
       const int64_t lim = s.end_dev ? *s.end_dev : s.count;

@@ -17,6 +17,9 @@
 //   batch_nnz_kernel     per-batch nnz at the largest eps (runner_multi.cuh:898-904).
 #include "dbm_internal.cuh"
 
+#include <cub/device/device_select.cuh>
+#include <thrust/iterator/counting_iterator.h>
+
 #include <algorithm>
 
 namespace dbm {
@@ -311,6 +314,44 @@ Status launch_label_range(const int32_t* labels, int64_t total, int64_t n, unsig
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(total, 256), int64_t(sm_count) * 8));
   label_range_kernel<<<blocks > 0 ? blocks : 1, 256, 0, s>>>(labels, total, n, first_bad);
   DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// ---- core sample indices (sklearn convention) ---------------------------------------------------
+__global__ void fill_i32_kernel(int32_t* __restrict__ p, int64_t count, int32_t v)
+{
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = v;
+}
+
+size_t core_indices_scratch_bytes(int64_t n)
+{
+  size_t temp = 0;
+  thrust::counting_iterator<int32_t> it(0);
+  cub::DeviceSelect::Flagged(nullptr, temp, it, static_cast<const uint8_t*>(nullptr), static_cast<int32_t*>(nullptr),
+                             static_cast<int64_t*>(nullptr), static_cast<int>(n));
+  return align_up(temp, 256) + 256;
+}
+
+// out[c*n ...] = ascending indices i with core[c*n + i] != 0, then -1
+Status launch_core_indices(const uint8_t* core, int64_t n, int configs, int32_t* out, void* scratch,
+                           size_t scratch_bytes, cudaStream_t s)
+{
+  if (scratch_bytes < core_indices_scratch_bytes(n)) return Status::Err(DBM_ERR_INVALID, "core index scratch too small");
+  const int64_t total = n * configs;
+  count_launch();
+  fill_i32_kernel<<<static_cast<unsigned>(std::min<int64_t>(ceil_div(total, 256), 148 * 32)), 256, 0, s>>>(out, total, -1);
+  DBM_CUDA(cudaGetLastError());
+  int64_t* num = reinterpret_cast<int64_t*>(scratch);
+  void* temp = static_cast<unsigned char*>(scratch) + 256;
+  size_t temp_bytes = scratch_bytes - 256;
+  thrust::counting_iterator<int32_t> it(0);
+  for (int c = 0; c < configs; ++c) {
+    count_launch();
+    DBM_CUDA(cub::DeviceSelect::Flagged(temp, temp_bytes, it, core + static_cast<int64_t>(c) * n,
+                                        out + static_cast<int64_t>(c) * n, num, static_cast<int>(n), s));
+  }
   return Status::Ok();
 }
 

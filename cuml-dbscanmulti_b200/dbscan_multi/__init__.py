@@ -54,7 +54,7 @@ MAX_EPS = 16
 DISTANCE_MODES = {"auto": 0, "exact": 1, "screened": 2}
 
 EXPORTED = (
-    "dbm_create", "dbm_destroy", "dbm_workspace_bytes", "dbm_set_phase_timing", "dbm_set_distance_mode",
+    "dbm_create", "dbm_destroy", "dbm_workspace_bytes", "dbm_set_phase_timing", "dbm_set_distance_mode", "dbm_core_sample_indices",
     "dbm_fit_multi", "dbm_fit_multi_host", "dbm_neighbor_counts", "dbm_batch_size", "dbm_max_bytes_for_batch_size",
     "dbm_annotate_pays", "dbm_auto_index_bits", "dbm_build_info_json",
     "dbm_neighbor_counts_noalloc", "dbm_distance_shard", "dbm_fit_multi_from_graph",
@@ -134,6 +134,8 @@ def load_library():
     lib.dbm_set_phase_timing.restype = None
     lib.dbm_set_distance_mode.argtypes = [p, i32]
     lib.dbm_set_distance_mode.restype = i32
+    lib.dbm_core_sample_indices.argtypes = [p, p, i64, i32, p, p, cp, sz]
+    lib.dbm_core_sample_indices.restype = i32
     fit_args = [p, p, i64, i64, p, i32, p, i32, p, p, ctypes.POINTER(Options), ctypes.POINTER(Stats),
                 p, i32]
     lib.dbm_fit_multi.argtypes = fit_args + [p, cp, sz]
@@ -308,6 +310,28 @@ class DbscanMulti:
         if rc != DBM_OK:
             raise DbmError(rc, err.value.decode())
         return deg
+
+    def core_sample_indices(self, core, stream: int | None = None):
+        """sklearn's core_sample_indices_ for every labelling of a fit: row c holds the indices of
+        the core points of configuration c, ascending, then -1 (cuML's convention).  `core` is the
+        (configs, N) uint8 core mask of fit_multi(..., return_core=True): a CUDA tensor (result on
+        the device) or a numpy array (staged through the device)."""
+        import torch
+
+        on_host = not type(core).__module__.startswith("torch")
+        c = torch.from_numpy(np.ascontiguousarray(core, dtype=np.uint8)).to(f"cuda:{self.device}") if on_host \
+            else core.contiguous()
+        if c.dim() != 2 or c.dtype != torch.uint8:
+            raise DbmError(-1, "core must be a (configs, N) uint8 mask")
+        out = torch.empty(c.shape, dtype=torch.int32, device=c.device)
+        s = stream if stream is not None else torch.cuda.current_stream(c.device).cuda_stream
+        err = ctypes.create_string_buffer(1024)
+        rc = self._lib.dbm_core_sample_indices(self._h, ctypes.c_void_p(c.data_ptr()), int(c.shape[1]),
+                                               int(c.shape[0]), ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(s),
+                                               err, len(err))
+        if rc != DBM_OK:
+            raise DbmError(rc, err.value.decode())
+        return out.cpu().numpy() if on_host else out
 
     def fit_multi(self, x, eps, min_samples, *, max_bytes_per_batch: int = 0, backend: str = "cuvs",
                   index: str = "auto", route: str = "auto", neigh_per_row: int = 0,

@@ -10,7 +10,8 @@ path).  Here the work shards without changing a single label:
    neighbour pairs are all-gathered (variable counts, padded);
 3. every rank labels a contiguous range of the k*l configurations from the complete graph
    (``dbm_fit_multi_from_graph``), with a batch plan that is identical on all ranks because the
-   budget and the CSR memory cap are agreed first (minimum over ranks);
+   budget and the CSR memory cap are agreed first (minimum over ranks); the ranges balance the
+   neighbour entries of the configs' eps rather than the config count;
 4. the label rows are all-gathered (in place when the configs split evenly), so every rank ends
    with the full (k*l, N) result.
 
@@ -43,6 +44,31 @@ def config_range(c: int, rank: int, world: int) -> tuple[int, int]:
     return c * rank // world, c * (rank + 1) // world
 
 
+def balanced_config_ranges(cost: list[float], world: int) -> list[tuple[int, int]]:
+    """Contiguous ranges of the configs (in their eps-major order) with near-equal summed cost:
+    rank r ends its range at the first config where the prefix sum reaches (r + 1) / world of
+    the total, keeping every range non-empty while configs remain.  Deterministic, so every
+    rank computes the same split from the same (all-reduced) costs."""
+    c = len(cost)
+    if world <= 1 or c == 0:
+        return [(0, c)] + [(c, c)] * max(0, world - 1)
+    total = float(sum(cost)) or float(c)
+    w = [float(x) if sum(cost) else 1.0 for x in cost]
+    ranges, start, acc = [], 0, 0.0
+    for r in range(world):
+        if r == world - 1:
+            ranges.append((start, c))
+            break
+        target = total * (r + 1) / world
+        end = start
+        while end < c and (acc + w[end] <= target or end == start) and c - (end + 1) >= world - r - 1:
+            acc += w[end]
+            end += 1
+        ranges.append((start, end))
+        start = end
+    return ranges
+
+
 class DeviceStages:
     """The C-ABI stages on this rank's GPU."""
 
@@ -62,9 +88,14 @@ class DeviceStages:
         return 80 * available // 100
 
     def free_bytes(self) -> int:
+        """Free device memory for the CSR-fits check, queried once per handle (the query costs
+        a driver round trip per call); the workspace is reused across calls, so the figure only
+        matters for the first, sizing call."""
         import torch
 
-        return int(torch.cuda.mem_get_info(self.h.device)[0])
+        if getattr(self, "_free", None) is None:
+            self._free = int(torch.cuda.mem_get_info(self.h.device)[0])
+        return self._free
 
     def distance_shard(self, x, eps: np.ndarray, shard: int, nshards: int, cap_hint: int):
         import torch
@@ -129,14 +160,16 @@ def _all_gather_varlen(dist, t, group):
     return [o[:c] for o, c in zip(out, counts)]
 
 
-def _gather_config_rows(dist, labels, C: int, n: int, group):
-    """Every rank holds the rows config_range(C, r, world) of a (C, n) label matrix; returns the
-    full matrix on every rank.  The row counts are known on every rank (no count exchange); with
-    equal shares the gather is in place into `labels` itself, else through a padded buffer."""
+def _gather_config_rows(dist, labels, C: int, n: int, group, ranges=None):
+    """Every rank holds the rows ranges[r] (default config_range(C, r, world)) of a (C, n) label
+    matrix; returns the full matrix on every rank.  The row counts are known on every rank (no
+    count exchange); with equal shares the gather is in place into `labels` itself, else through
+    a padded buffer."""
     import torch
 
     world, rank = dist.get_world_size(group), dist.get_rank(group)
-    ranges = [config_range(C, r, world) for r in range(world)]
+    if ranges is None:
+        ranges = [config_range(C, r, world) for r in range(world)]
     sizes = [b - a for a, b in ranges]
     if min(sizes) == max(sizes):
         flat = labels.reshape(-1)
@@ -183,9 +216,18 @@ def sharded_fit_multi(stages, x, eps, min_samples, *, group=None, max_bytes_per_
     parts = _all_gather_varlen(dist, edges, group)
     all_edges = torch.cat(parts) if parts else edges
 
-    c0, c1 = config_range(k * l, rank, world)
-    labels, stats, routes = stages.fit_from_graph(n, d, e, m, hist, all_edges, c0, c1, opt)
-    full = _gather_config_rows(dist, labels, k * l, n, group)
+    # configs split by cost: the labelling walks the neighbour entries of each config's eps, so
+    # balance the per-eps entry counts (known identically on every rank from the summed
+    # histograms) instead of the number of configs
+    per_eps = hist.to(torch.int64).cumsum(0).sum(1).cpu().tolist()
+    cost = [float(per_eps[c // l]) + 1.0 for c in range(k * l)]
+    ranges = balanced_config_ranges(cost, world)
+    c0, c1 = ranges[rank]
+    if c1 > c0:
+        labels, stats, routes = stages.fit_from_graph(n, d, e, m, hist, all_edges, c0, c1, opt)
+    else:  # more ranks than configs: nothing to label here
+        labels, stats, routes = torch.empty((k * l, n), dtype=torch.int32, device=hist.device), {}, []
+    full = _gather_config_rows(dist, labels, k * l, n, group, ranges)
     stats = dict(stats)
     stats["world_size"] = world
     stats["edges"] = int(all_edges.numel())

@@ -192,6 +192,15 @@ int dbm_fit_multi_from_graph(dbm_handle* h, int64_t n, int64_t d, const float* e
                              dbm_stats* stats, uint8_t* batch_routes, int routes_len, void* stream,
                              char* err, size_t err_len);
 
+/* sklearn-style core sample indices of every labelling: out_dev[c*n + 0 ..] = the indices of
+ * the core points of configuration c in ascending order, then -1 up to n (int32, device).
+ * core_dev is the (configs x n) byte core mask of dbm_fit_multi.  This is the output cuML's
+ * DBSCAN computes after its final relabel (third_party/cuml/cpp/src/dbscan/runner.cuh:406-430:
+ * fill with -1, copy_if of the index range with the core mask as stencil), which the
+ * reference's fit_multi does not expose. */
+int dbm_core_sample_indices(dbm_handle* h, const uint8_t* core_dev, int64_t n, int configs, int32_t* out_dev,
+                            void* stream, char* err, size_t err_len);
+
 /* Per-eps neighbourhood sizes only (the point itself included): deg_dev[e*n + i] = #{j :
  * dist2(i, j) <= eps_e^2}, int32, device.  This is the degree vector the reference's
  * VertexDeg::run_multi produces per batch (src/multi/eps_neighborhood.cuh:440-479, vd[e]). */

@@ -387,3 +387,21 @@ def test_config_range_fit_from_graph_matches_full_fit(h, torch_mod):
     for c0, c1 in [(0, 2), (2, 5), (5, 6), (0, 6)]:
         lab, stats, _ = st.fit_from_graph(9000, 6, e, m, hist, edges, c0, c1, opt)
         assert np.array_equal(lab[c0:c1].cpu().numpy(), full[c0:c1])
+
+
+def test_core_sample_indices_follow_the_core_masks(h, torch_mod):
+    """sklearn/cuML core_sample_indices_ per labelling: ascending core indices, then -1
+    (third_party/cuml/cpp/src/dbscan/runner.cuh:406-430), from the fit's core masks."""
+    name = CASES[3]
+    pts, eps, ms, _ = load_case(name)
+    _, core, _ = gpu_fit(h, torch_mod, pts, eps, ms)
+    got = h.core_sample_indices(core.astype(np.uint8))
+    assert got.shape == core.shape and got.dtype == np.int32
+    for c in range(core.shape[0]):
+        idx = np.flatnonzero(core[c]).astype(np.int32)
+        assert np.array_equal(got[c, : len(idx)], idx)
+        assert (got[c, len(idx):] == -1).all()
+    x = torch_mod.from_numpy(np.ascontiguousarray(pts, dtype=np.float32)).cuda()
+    r = h.fit_multi(x, eps, ms, return_core=True)
+    dev = h.core_sample_indices(r.core)
+    assert dev.is_cuda and np.array_equal(dev.cpu().numpy(), got)
