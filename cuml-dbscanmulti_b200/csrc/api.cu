@@ -55,7 +55,7 @@ Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32
                           size_t scratch_bytes, void* scan_scratch, size_t scan_bytes, const int64_t** count_out_dev,
                           cudaStream_t s);
 Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
-                          long long* work, cudaStream_t s);
+                          long long* work, int64_t cap, cudaStream_t s);
 Status spatial_order(const float* x, int64_t n, int32_t d, int32_t* perm, void* scratch, size_t scratch_bytes,
                      cudaStream_t s);
 Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
@@ -206,6 +206,7 @@ struct dbm_handle {
   };
   std::vector<PendingTimer> pending_timers;  // phase events read after the call's final sync
   uint64_t edge_cap_hint = 0;
+  int64_t work_cap_hint = 0;  // worklist capacity learned from earlier calls (no count sync then)
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
   dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_scratch, work, fallback;
@@ -434,29 +435,34 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
   const int64_t T = ceil_div(n, 128);
   const int64_t pairs = T * (T + 1) / 2;
   const long long* work = nullptr;
-  int64_t work_count = 0;
+  int64_t work_count = 0, work_cap = 0;
+  const int64_t* count_dev = nullptr;
   if (perm) {
     DBM_TRY(ensure(h->box_lo, sizeof(float) * static_cast<size_t>(T) * di));
     DBM_TRY(ensure(h->box_hi, sizeof(float) * static_cast<size_t>(T) * di));
     DBM_TRY(ensure(h->prune_scratch, prune_scratch_bytes(T, di)));
     DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(prune_units(T) + 1)));
     DBM_TRY(launch_tile_boxes(as<float>(h->xt), n, padded_points(n), di, as<float>(h->box_lo), as<float>(h->box_hi), s));
-    const int64_t* count_dev = nullptr;
     DBM_TRY(launch_prune_count(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
                                h->prune_scratch.bytes, h->scan_scratch.p, h->scan_scratch.bytes, &count_dev, s));
-    h->pinned[0] = 0;
-    DBM_CUDA(cudaMemcpyAsync(h->pinned, count_dev, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
-    DBM_CUDA(cudaStreamSynchronize(s));
-    work_count = h->pinned[0];
-    DBM_TRY(ensure(h->work, sizeof(long long) * std::max<int64_t>(work_count, 1)));
+    if (screen && h->work_cap_hint > 0) {
+      // the screen reads the worklist length on the device; a capacity learned from earlier
+      // calls saves the host round trip (an overflow is seen at the pass's own sync below)
+      work_cap = h->work_cap_hint;
+    } else {
+      h->pinned[0] = 0;
+      DBM_CUDA(cudaMemcpyAsync(h->pinned, count_dev, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+      DBM_CUDA(cudaStreamSynchronize(s));
+      work_count = h->pinned[0];
+      work_cap = std::max<int64_t>(work_count, 1);
+    }
+    DBM_TRY(ensure(h->work, sizeof(long long) * work_cap));
+    work_cap = static_cast<int64_t>(h->work.bytes / sizeof(long long));
     DBM_TRY(launch_prune_write(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
-                               as<long long>(h->work), s));
+                               as<long long>(h->work), work_cap, s));
     work = as<long long>(h->work);
-    st.tile_pairs_kept = pairs > 0 ? static_cast<double>(work_count) / static_cast<double>(pairs) : 1.0;
-  } else {
-    st.tile_pairs_kept = 1.0;
   }
-  if (screen) DBM_TRY(ensure(h->fallback, sizeof(long long) * std::max<int64_t>(work_count, 1)));
+  if (screen) DBM_TRY(ensure(h->fallback, sizeof(long long) * std::max<int64_t>(work_cap, 1)));
   uint64_t cap = std::max<uint64_t>(h->edge_cap_hint, cap_hint);
   uint64_t found = 0;
   for (int pass = 0; pass < 2; ++pass) {
@@ -468,6 +474,8 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
                  as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards, perm,
                  work, work_count};
     if (screen) {
+      a.work_total_dev = count_dev;
+      a.work_cap = work_cap;
       {
         PhaseTimer ts(h, s, &st.ms_screen);
         DBM_TRY(launch_screened_distance(a, as<float>(h->box_lo), as<float>(h->box_hi), as<long long>(h->fallback), s));
@@ -483,10 +491,21 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
       DBM_TRY(launch_distance(a, s));
     }
     st.distance_passes = pass + 1;
-    for (int w = 0; w < 8; ++w) h->pinned[w] = 0;
+    for (int w = 0; w < 10; ++w) h->pinned[w] = 0;
     DBM_CUDA(cudaMemcpyAsync(h->pinned, h->counters.p, 8 * sizeof(unsigned long long), cudaMemcpyDeviceToHost, s));
     DBM_CUDA(cudaMemcpyAsync(h->pinned + 8, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    if (count_dev) DBM_CUDA(cudaMemcpyAsync(h->pinned + 9, count_dev, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     DBM_CUDA(cudaStreamSynchronize(s));
+    if (count_dev) {
+      work_count = h->pinned[9];
+      h->work_cap_hint = std::max<int64_t>(h->work_cap_hint, work_count + work_count / 8 + 1);
+      if (work_count > work_cap) {
+        // the worklist outgrew the learned capacity: redo the pass with the exact size (the
+        // hint is now large enough, so this recursion ends after one level)
+        return distance_stage(h, x, n, d, eps2, k, shard, nshards, hist, cap_hint, found_out, st, s);
+      }
+    }
+    st.tile_pairs_kept = !count_dev ? 1.0 : pairs > 0 ? static_cast<double>(work_count) / static_cast<double>(pairs) : 1.0;
     found = static_cast<uint64_t>(h->pinned[0]);
     {
       // exact-kernel work: 8 warps per 128 x 128 tile, each evaluating up to d dims for its

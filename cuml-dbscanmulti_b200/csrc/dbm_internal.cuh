@@ -178,6 +178,9 @@ struct DistLaunch {
   int64_t work_count = 0;
   const unsigned long long* work_count_dev = nullptr;  // count of `work` read on the device
                                                        // (the whole list, no sharding)
+  const int64_t* work_total_dev = nullptr;  // screened pass: the worklist length on the device
+  int64_t work_cap = 0;                     // (entries beyond work_cap were not written); each
+                                            // shard's slice is computed on the device
 };
 
 // Screened distance pass (dist_tc.cu): tensor-core bound + exact chain for the candidates;

@@ -72,6 +72,9 @@ struct ScreenParams {
   int32_t k;
   int64_t item_begin;
   int64_t item_count;
+  const int64_t* total_dev;      // when set: worklist length on the device (capped at cap),
+  int64_t cap;                   // and this shard's slice is computed here
+  int32_t shard, nshards;
   const long long* work;
   const float* xt;               // dp x npad, dim-major
   unsigned long long* counters;  // [0] edge cursor, [4] item cursor, [5] fallback count,
@@ -258,6 +261,12 @@ dist_screen_kernel(const ScreenParams p)
   const int64_t n = p.n;
   const float cutoff = p.eps2[p.k - 1];
   const float se = p.sqrt_e;
+  int64_t item_begin = p.item_begin, item_count = p.item_count;
+  if (p.total_dev) {
+    const int64_t total = *p.total_dev < p.cap ? *p.total_dev : p.cap;
+    item_begin = total * p.shard / p.nshards;
+    item_count = total * (p.shard + 1) / p.nshards - item_begin;
+  }
   if (tid < kMaxEps) s_eps2[tid] = p.eps2[tid];
   if (warp == 0) {
     tmem_alloc(&s_tmem, kTmemCols);
@@ -285,7 +294,7 @@ dist_screen_kernel(const ScreenParams p)
     return q < G ? cstart + q : s_chunk[(m + 1) & 1] + (q - G);
   };
   auto load_entry = [&](long long idx) -> long long {
-    return idx < p.item_count ? __ldg(p.work + p.item_begin + idx) : -1;
+    return idx < item_count ? __ldg(p.work + item_begin + idx) : -1;
   };
   long long e_cur = load_entry(item_index(0));
   long long e_nxt = e_cur >= 0 ? load_entry(item_index(1)) : -1;
@@ -549,8 +558,17 @@ Status launch_screened_distance(const DistLaunch& a, const float* box_lo, const 
   p.d = a.d;
   p.k = a.k;
   const int shards = a.nshards > 0 ? a.nshards : 1;
-  p.item_begin = a.work_count * a.shard / shards;
-  p.item_count = a.work_count * (a.shard + 1) / shards - p.item_begin;
+  p.shard = a.shard;
+  p.nshards = shards;
+  if (a.work_total_dev) {
+    p.total_dev = a.work_total_dev;
+    p.cap = a.work_cap;
+    p.item_begin = 0;
+    p.item_count = a.work_cap;  // an upper bound for the grid size
+  } else {
+    p.item_begin = a.work_count * a.shard / shards;
+    p.item_count = a.work_count * (a.shard + 1) / shards - p.item_begin;
+  }
   p.work = a.work;
   p.xt = a.xt;
   p.counters = a.counters;

@@ -124,7 +124,7 @@ __global__ void tile_pairs_kernel(int64_t tiles, int64_t units, const float* __r
 
 // One warp per unit: its kept tiles as packed worklist entries at off[u] ..., I ascending.
 __global__ void tile_pairs_write_kernel(int64_t tiles, int64_t units, const uint32_t* __restrict__ masks,
-                                        const int64_t* __restrict__ off, long long* __restrict__ work)
+                                        const int64_t* __restrict__ off, long long* __restrict__ work, int64_t cap)
 {
   const int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -135,7 +135,8 @@ __global__ void tile_pairs_write_kernel(int64_t tiles, int64_t units, const uint
 #pragma unroll
   for (int c = 0; c < static_cast<int>(kUnitTiles / 32); ++c) {
     const uint32_t m = masks[u * (kUnitTiles / 32) + c];
-    if ((m >> lane) & 1u) work[at + __popc(m & ((1u << lane) - 1u))] = (J << 32) | (blk * kUnitTiles + 32 * c + lane);
+    const int64_t idx = at + __popc(m & ((1u << lane) - 1u));
+    if (((m >> lane) & 1u) && idx < cap) work[idx] = (J << 32) | (blk * kUnitTiles + 32 * c + lane);
     at += __popc(m);
   }
 }
@@ -183,9 +184,9 @@ Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32
   return Status::Ok();
 }
 
-// the packed worklist entries, J ascending then I ascending
+// the packed worklist entries, J ascending then I ascending (the first `cap` of them)
 Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
-                          long long* work, cudaStream_t s)
+                          long long* work, int64_t cap, cudaStream_t s)
 {
   (void)lo;
   (void)hi;
@@ -198,7 +199,7 @@ Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32
                                                             align_up(sizeof(int64_t) * (units + 1), 256));
   count_launch();
   tile_pairs_write_kernel<<<static_cast<unsigned>(ceil_div(units * 32, 256)), 256, 0, s>>>(tiles, units, masks, off,
-                                                                                         work);
+                                                                                         work, cap);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
