@@ -98,8 +98,10 @@ __global__ void cc_touch_kernel(const CcArgs a, int32_t* __restrict__ L)
   });
 }
 
-// unite(P[cfg], r, j) for every core-core entry
-__global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t* __restrict__ err)
+// unite(P[cfg], r, j) for every core-core entry; with Q set, unite(Q[cfg], r, j) as well (the
+// batch-local and the global union-find of a batch share one walk of its entries)
+__global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t* __restrict__ Q,
+                                int32_t* __restrict__ err)
 {
   bool ok = true;
   for_each_entry(a, [&](int e, int32_t r, int32_t j) {
@@ -107,7 +109,11 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
     cfg_range(a, e, m_lo, m_hi);
     const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
     const int mm = min(min(cc[r], cc[j]), m_hi);
-    for (int m = m_lo; m < mm; ++m) ok &= uf_unite(P + static_cast<int64_t>(e * a.l + m) * a.n, r, j);
+    for (int m = m_lo; m < mm; ++m) {
+      const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
+      ok &= uf_unite(P + base, r, j);
+      if (Q) ok &= uf_unite(Q + base, r, j);
+    }
   });
   if (!ok) atomicOr(err, kErrUnionLimit);
 }
@@ -234,14 +240,15 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
   const unsigned nb = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sm_count) * 16)));
   if (single_batch) {
     count_launch(2);
-    cc_union_kernel<<<nb, 256, 0, s>>>(a, G, err);
+    cc_union_kernel<<<nb, 256, 0, s>>>(a, G, nullptr, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, G, best, tag);
   } else {
-    count_launch(4);
+    // the global union needs only to precede the border fold, so it rides along with the local
+    // one; the border candidates read the finished local union-find
+    count_launch(3);
     cc_touch_kernel<<<nb, 256, 0, s>>>(a, L);
-    cc_union_kernel<<<nb, 256, 0, s>>>(a, L, err);
+    cc_union_kernel<<<nb, 256, 0, s>>>(a, L, G, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, L, best, tag);
-    cc_union_kernel<<<nb, 256, 0, s>>>(a, G, err);
   }
   count_launch();
   cc_border_kernel<<<nb, 256, 0, s>>>(a, G, best, cur, tag);
