@@ -57,9 +57,38 @@ __device__ __forceinline__ void cfg_range(const CcArgs& a, int e, int& m_lo, int
   m_hi = max(0, min(a.l, a.cfg_end - e * a.l));
 }
 
-// One thread per (entry, minPts index m): the union-find chains of the l configs of an entry are
-// independent, so giving each its own thread keeps l times more memory requests in flight (the
-// kernels are bound by the latency of dependent L2 accesses, not by bandwidth).  f(e, m, r, j)
+template <class F>
+__device__ __forceinline__ void for_each_entry(const CcArgs& a, F&& f)
+{
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if (a.ms.direct) {
+    const SlabRef& s = a.ms.s[0];
+    for (int64_t q = t0; q < s.count; q += stride) {
+      const uint32_t w = static_cast<uint32_t>(s.col[q]);
+      const int32_t j = static_cast<int32_t>(w & kColMask);
+      const int32_t r = s.row[q];
+      const int e0 = max(static_cast<int>(w >> kCodeShift), a.cfg_begin / a.l);
+      const int e1 = min(a.k, (a.cfg_end + a.l - 1) / a.l);  // owned eps [e0, e1)
+      for (int e = e0; e < e1; ++e) f(e, r, j);
+    }
+  } else {
+    for (int e = 0; e < a.ms.nslabs; ++e) {
+      int m_lo, m_hi;
+      cfg_range(a, e, m_lo, m_hi);
+      if (m_lo >= m_hi) continue;  // no config of this eps is owned by this call
+      const SlabRef& s = a.ms.s[e];
+      const int64_t b = s.begin_dev ? *s.begin_dev : 0;
+      const int64_t lim = s.end_dev ? *s.end_dev : s.count;
+      for (int64_t q = b + t0; q < lim; q += stride) f(e, s.row[q], s.col[q] & static_cast<int32_t>(kColMask));
+    }
+  }
+}
+
+// One thread per (entry, minPts index m), for the union kernel: the union-find chains of the l
+// configs of an entry are independent, so giving each its own thread keeps l times more memory
+// requests in flight (the kernel is bound by the latency of dependent L2 accesses, not by
+// bandwidth).  The lighter kernels (one find or store per config) keep one thread per entry.  f(e, m, r, j)
 // runs for every eps e the entry belongs to and every m of e owned by this call.
 template <class F>
 __device__ __forceinline__ void for_each_entry_cfg(const CcArgs& a, F&& f)
@@ -106,11 +135,13 @@ __device__ __forceinline__ void for_each_entry_cfg(const CcArgs& a, F&& f)
 // L[cfg][v] = v for both endpoints of every entry (configs where v is core).
 __global__ void cc_touch_kernel(const CcArgs a, int32_t* __restrict__ L)
 {
-  for_each_entry_cfg(a, [&](int e, int m, int32_t r, int32_t j) {
+  for_each_entry(a, [&](int e, int32_t r, int32_t j) {
+    int m_lo, m_hi;
+    cfg_range(a, e, m_lo, m_hi);
     const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
-    int32_t* Lc = L + static_cast<int64_t>(e * a.l + m) * a.n;
-    if (m < cc[r]) Lc[r] = r;
-    if (m < cc[j]) Lc[j] = j;
+    const int cr = min(cc[r], m_hi), cj = min(cc[j], m_hi);
+    for (int m = m_lo; m < cr; ++m) L[static_cast<int64_t>(e * a.l + m) * a.n + r] = r;
+    for (int m = m_lo; m < cj; ++m) L[static_cast<int64_t>(e * a.l + m) * a.n + j] = j;
   });
 }
 
@@ -134,15 +165,20 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
 __global__ void cc_best_kernel(const CcArgs a, int32_t* __restrict__ P, unsigned long long* __restrict__ best,
                                uint32_t tag)
 {
-  for_each_entry_cfg(a, [&](int e, int m, int32_t r, int32_t j) {
+  for_each_entry(a, [&](int e, int32_t r, int32_t j) {
+    int m_lo, m_hi;
+    cfg_range(a, e, m_lo, m_hi);
     const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
-    const bool r_core = m < cc[r], j_core = m < cc[j];
-    if (r_core == j_core) return;
-    const int32_t c = r_core ? r : j;
-    const int32_t pt = r_core ? j : r;
-    const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
-    const int32_t root = uf_find(P + base, c);
-    atomicMin(best + base + pt, (static_cast<unsigned long long>(tag) << 32) | static_cast<uint32_t>(root));
+    const int cr = cc[r], cj = cc[j];
+    const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
+    for (int m = lo; m < hi; ++m) {
+      const bool r_core = m < cr;
+      const int32_t c = r_core ? r : j;
+      const int32_t pt = r_core ? j : r;
+      const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
+      const int32_t root = uf_find(P + base, c);
+      atomicMin(best + base + pt, (static_cast<unsigned long long>(tag) << 32) | static_cast<uint32_t>(root));
+    }
   });
 }
 
@@ -151,19 +187,23 @@ __global__ void cc_border_kernel(const CcArgs a, int32_t* __restrict__ G,
                                  const unsigned long long* __restrict__ best, int32_t* __restrict__ cur,
                                  uint32_t tag)
 {
-  for_each_entry_cfg(a, [&](int e, int m, int32_t r, int32_t j) {
+  for_each_entry(a, [&](int e, int32_t r, int32_t j) {
+    int m_lo, m_hi;
+    cfg_range(a, e, m_lo, m_hi);
     const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
-    const bool r_core = m < cc[r], j_core = m < cc[j];
-    if (r_core == j_core) return;
-    const int32_t pt = r_core ? j : r;
-    const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
-    const unsigned long long v = best[base + pt];
-    if (static_cast<uint32_t>(v >> 32) != tag) return;
-    const int32_t cand = uf_find(G + base, static_cast<int32_t>(v & 0xffffffffu));
-    volatile int32_t* cp = cur + base + pt;
-    const int32_t old = *cp;
-    const int32_t prev = (old == kNone) ? kNone : uf_find(G + base, old);
-    *cp = prev < cand ? prev : cand;
+    const int cr = cc[r], cj = cc[j];
+    const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
+    for (int m = lo; m < hi; ++m) {
+      const int32_t pt = (m < cr) ? j : r;
+      const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
+      const unsigned long long v = best[base + pt];
+      if (static_cast<uint32_t>(v >> 32) != tag) continue;
+      const int32_t cand = uf_find(G + base, static_cast<int32_t>(v & 0xffffffffu));
+      volatile int32_t* cp = cur + base + pt;
+      const int32_t old = *cp;
+      const int32_t prev = (old == kNone) ? kNone : uf_find(G + base, old);
+      *cp = prev < cand ? prev : cand;
+    }
   });
 }
 
@@ -239,18 +279,20 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
 {
   if (upper_entries <= 0 || cfg_begin >= cfg_end) return Status::Ok();
   const CcArgs a{ms, n, k, l, cfg_begin, cfg_end, cc};
-  const int64_t want = ceil_div(upper_entries * l, 256);
-  const unsigned nb = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sm_count) * 32)));
+  const unsigned nb = static_cast<unsigned>(
+    std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries, 256), static_cast<int64_t>(sm_count) * 16)));
+  const unsigned nbu = static_cast<unsigned>(
+    std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries * l, 256), static_cast<int64_t>(sm_count) * 32)));
   if (single_batch) {
     count_launch(2);
-    cc_union_kernel<<<nb, 256, 0, s>>>(a, G, nullptr, err);
+    cc_union_kernel<<<nbu, 256, 0, s>>>(a, G, nullptr, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, G, best, tag);
   } else {
     // the global union needs only to precede the border fold, so it rides along with the local
     // one; the border candidates read the finished local union-find
     count_launch(3);
     cc_touch_kernel<<<nb, 256, 0, s>>>(a, L);
-    cc_union_kernel<<<nb, 256, 0, s>>>(a, L, G, err);
+    cc_union_kernel<<<nbu, 256, 0, s>>>(a, L, G, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, L, best, tag);
   }
   count_launch();

@@ -63,14 +63,17 @@ __host__ __device__ __forceinline__ int64_t units_before(int64_t J)
 
 __device__ __forceinline__ void unit_coords(int64_t u, int64_t tiles, int64_t& J, int64_t& blk)
 {
-  int64_t lo = 0, hi = tiles - 1;  // largest J with units_before(J) <= u
-  while (lo < hi) {
-    const int64_t mid = (lo + hi + 1) >> 1;
-    if (units_before(mid) <= u) lo = mid;
-    else hi = mid - 1;
-  }
-  J = lo;
-  blk = u - units_before(lo);
+  // tile J = K q + r (K = kUnitTiles) owns q + 1 units, and the units before J = K q number
+  // K q (q + 1) / 2: q from the square root (corrected by +-1 for rounding), then r and blk by
+  // division
+  (void)tiles;
+  constexpr int64_t K = kUnitTiles;
+  int64_t q = static_cast<int64_t>((sqrt(1.0 + 8.0 * static_cast<double>(u) / K) - 1.0) * 0.5);
+  while (q > 0 && K * q * (q + 1) / 2 > u) --q;
+  while (K * (q + 1) * (q + 2) / 2 <= u) ++q;
+  const int64_t rem = u - K * q * (q + 1) / 2;
+  J = kUnitTiles * q + rem / (q + 1);
+  blk = rem % (q + 1);
 }
 
 // One warp per unit: the tiles I of the unit's block (I <= J) whose boxes may meet J's (I == J
