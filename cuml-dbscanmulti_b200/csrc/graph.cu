@@ -251,26 +251,27 @@ __global__ void filter_all_kernel(const int64_t* __restrict__ off, const uint32_
   if (warp >= rows) return;
   const int64_t r = s0 + warp;
   const int64_t beg = off[r], end = off[r + 1];
-  int64_t out[kMaxEps];
-  for (int e = 0; e < ne; ++e) out[e] = off_flat[static_cast<int64_t>(e) * rows + warp];
   const uint32_t below = (1u << lane) - 1u;
-  for (int64_t q0 = beg; q0 < end; q0 += 32) {
-    const int64_t q = q0 + lane;
-    uint32_t code = 0xffu, j = 0;
-    if (q < end) {
-      const uint32_t w = col[q];
-      code = w >> kCodeShift;
-      j = w & kColMask;
-    }
-    for (int e = 0; e < ne; ++e) {
+  // eps outermost with a scalar cursor (an array of cursors indexed by a runtime eps would live
+  // in local memory); the row's entries are re-read from L1 for each eps
+  for (int e = 0; e < ne; ++e) {
+    int64_t out = off_flat[static_cast<int64_t>(e) * rows + warp];
+    for (int64_t q0 = beg; q0 < end; q0 += 32) {
+      const int64_t q = q0 + lane;
+      uint32_t code = 0xffu, j = 0;
+      if (q < end) {
+        const uint32_t w = col[q];
+        code = w >> kCodeShift;
+        j = w & kColMask;
+      }
       const bool keep = code <= static_cast<uint32_t>(e);
       const uint32_t bal = __ballot_sync(0xffffffffu, keep);
       if (keep) {
-        const int64_t dst = out[e] + __popc(bal & below);
+        const int64_t dst = out + __popc(bal & below);
         col_flat[dst] = static_cast<int32_t>(j);
         row_flat[dst] = static_cast<int32_t>(r);
       }
-      out[e] += __popc(bal);
+      out += __popc(bal);
     }
   }
 }
