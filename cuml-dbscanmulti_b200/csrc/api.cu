@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <limits>
@@ -207,6 +208,10 @@ struct dbm_handle {
   std::vector<PendingTimer> pending_timers;  // phase events read after the call's final sync
   uint64_t edge_cap_hint = 0;
   int64_t work_cap_hint = 0;  // worklist capacity learned from earlier calls (no count sync then)
+  // free device memory as of the last query (a cudaMemGetInfo costs ~1 ms of host time)
+  size_t free_cached = 0, total_cached = 0;
+  uint64_t free_cached_ws = 0;  // the handle's workspace bytes at that query
+  std::chrono::steady_clock::time_point free_cached_at{};
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
   dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_scratch, work, fallback;
@@ -377,6 +382,25 @@ static void square_eps(const float* eps, int k, float* eps2)
   }
 }
 
+// Free device memory, as cudaMemGetInfo reports it.  The query is cached on the handle for up to
+// one second and corrected by the handle's own workspace growth since then (the only
+// allocations this library makes); another process allocating in that second is the one case a
+// fresh query would see differently.
+static Status free_memory(dbm_handle* h, size_t* free_b, size_t* total_b)
+{
+  const auto now = std::chrono::steady_clock::now();
+  const uint64_t ws = h->workspace_bytes();
+  if (h->total_cached == 0 || now - h->free_cached_at > std::chrono::seconds(1) || ws < h->free_cached_ws) {
+    DBM_CUDA(cudaMemGetInfo(&h->free_cached, &h->total_cached));
+    h->free_cached_at = now;
+    h->free_cached_ws = ws;
+  }
+  const uint64_t grown = ws - h->free_cached_ws;
+  *free_b = h->free_cached > grown ? h->free_cached - grown : 0;
+  *total_b = h->total_cached;
+  return Status::Ok();
+}
+
 // Budget, index width and the first batch-size check (runner_multi.cuh:1315-1337, 458-499).
 static Status plan_budget(dbm_handle* h, int64_t n, int k, int l, const dbm_options& opt, dbm_stats& st,
                           Plan& plan)
@@ -387,7 +411,7 @@ static Status plan_budget(dbm_handle* h, int64_t n, int k, int l, const dbm_opti
                     : (static_cast<long double>(n) * n >= static_cast<long double>(INT32_MAX) ? 64 : 32);
   if (opt.max_bytes_per_batch == 0) {
     size_t free_b = 0, total_b = 0;
-    DBM_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    DBM_TRY(free_memory(h, &free_b, &total_b));
     const uint64_t reusable = h->workspace_bytes();
     const uint64_t used = total_b - std::min<uint64_t>(total_b, free_b);
     const uint64_t available = reusable > used ? total_b : std::min<uint64_t>(total_b, free_b + reusable);
@@ -589,7 +613,7 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
     uint64_t available = opt.csr_cap_bytes;
     if (available == 0) {
       size_t fr = 0, to = 0;
-      DBM_CUDA(cudaMemGetInfo(&fr, &to));
+      DBM_TRY(free_memory(h, &fr, &to));
       available = fr;
     }
     int64_t measured = 0;

@@ -77,25 +77,30 @@ class DeviceStages:
         self.lib = handle._lib
         self.last_shard_stats: dict[str, Any] = {}
 
-    def default_budget(self) -> int:
-        """80% of (free + this handle's reusable workspace), as the reference's fit_multi."""
+    def _mem_info(self) -> tuple[int, int]:
+        """(free, total) device memory, queried at most once a second (the query costs
+        milliseconds of host time)."""
+        import time
+
         import torch
 
-        free, total = torch.cuda.mem_get_info(self.h.device)
+        now = time.monotonic()
+        if getattr(self, "_mem_at", None) is None or now - self._mem_at > 1.0:
+            self._mem = tuple(int(v) for v in torch.cuda.mem_get_info(self.h.device))
+            self._mem_at = now
+        return self._mem
+
+    def default_budget(self) -> int:
+        """80% of (free + this handle's reusable workspace), as the reference's fit_multi."""
+        free, total = self._mem_info()
         reusable = self.h.workspace_bytes
         used = total - min(total, free)
         available = total if reusable > used else min(total, free + reusable)
         return 80 * available // 100
 
     def free_bytes(self) -> int:
-        """Free device memory for the CSR-fits check, queried once per handle (the query costs
-        a driver round trip per call); the workspace is reused across calls, so the figure only
-        matters for the first, sizing call."""
-        import torch
-
-        if getattr(self, "_free", None) is None:
-            self._free = int(torch.cuda.mem_get_info(self.h.device)[0])
-        return self._free
+        """Free device memory for the CSR-fits check (the workspace is reused across calls)."""
+        return self._mem_info()[0]
 
     def distance_shard(self, x, eps: np.ndarray, shard: int, nshards: int, cap_hint: int):
         import torch
