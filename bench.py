@@ -199,10 +199,15 @@ def cpu_baseline(pts: np.ndarray, eps, target_s: float = 12.0) -> dict:
 
     threads = oracle.default_threads()
     n = len(pts)
-    rows = 32
-    t0 = time.perf_counter()
-    oracle.codes_degrees(pts, eps, row0=0, rows=rows, want_codes=False, threads=threads)
-    dt = time.perf_counter() - t0
+    # calibrate on a probe long enough (>= 0.5 s) that thread start-up does not skew the rate
+    rows, dt = 32, 0.0
+    while True:
+        t0 = time.perf_counter()
+        oracle.codes_degrees(pts, eps, row0=0, rows=rows, want_codes=False, threads=threads)
+        dt = time.perf_counter() - t0
+        if dt >= 0.5 or rows >= n:
+            break
+        rows = min(n, rows * 4)
     rows2 = int(min(n, max(rows, rows * target_s / max(dt, 1e-6))))
     t0 = time.perf_counter()
     oracle.codes_degrees(pts, eps, row0=0, rows=rows2, want_codes=False, threads=threads)
