@@ -5,7 +5,7 @@
 // fma(q[t]-p[t], q[t]-p[t], acc) in dim order, code = smallest e with acc <= eps2[e]) costs
 // 2*D CUDA-core operations per pair.  In the sparse regime almost every pair of a surviving
 // tile pair is far beyond the largest eps, so this kernel first bounds all 128 x 128 pairs with
-// one bf16 tcgen05 GEMM and evaluates the exact chain only for the pairs the bound cannot
+// one tf32 tcgen05 GEMM and evaluates the exact chain only for the pairs the bound cannot
 // exclude.  Nothing about the results changes: a pair is a neighbour iff its exact chain says
 // so, and the bound provably never drops a neighbour (argument below).
 //
@@ -35,13 +35,14 @@
 //   rows:   thread r loads its row of tile I from XT into registers, one item ahead;
 //   build:  centred tf32 operands in the canonical K-major no-swizzle layout (8-row x 16-byte
 //           core matrices; LBO = 2048 B between the two K halves of an MMA, SBO = 128 B
-//           between 8-row groups) plus the h / g columns; tile J (operand and fp32 copy in
-//           shared memory) only when J changes;
+//           between 8-row groups) plus the h / g columns; tile J (operand, and for D <= 36 an
+//           fp32 copy in shared memory) only when J changes;
 //   MMA:    KS x tcgen05.mma.cta_group::1.kind::tf32 (M = N = 128, K = 8) into 128 TMEM
 //           columns, committed to an mbarrier;
 //   screen: tcgen05.ld 32x32b.x32 -> per-thread candidate masks;
 //   exact:  thread r runs the fp32 chain for each of its candidates from its registers and the
-//           fp32 tile J, then code, COO word and per-code histogram (dist_tri_kernel's outputs).
+//           fp32 tile J (shared memory, or XT for D > 36), then code, COO word and per-code
+//           histogram (dist_tri_kernel's outputs).
 // A tile pair whose bound admits more than kScreenCap candidates (dense regime), or whose
 // coordinates are too large for the bound, is appended to a fallback list for dist_tri_kernel.
 #include "dbm_internal.cuh"
@@ -233,19 +234,44 @@ __device__ __forceinline__ float col_slack(float m, float se)
   return __fsub_rd(g, __fmul_ru(0.0001220703125f, m));
 }
 
+// build_row for a row read straight from XT four dims at a time; an invalid row is centred to 0
+template <int KP>
+__device__ __forceinline__ float build_row_xt(const float* __restrict__ xt, int64_t npad, int64_t col, bool valid,
+                                              const float* __restrict__ cs, int r, unsigned char* op)
+{
+  float nq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const float* q = xt + col;
+#pragma unroll
+  for (int ch = 0; ch < KP / 4; ++ch) {
+    float w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const int t = ch * 4 + h;
+      const float x = valid ? __ldg(q + t * npad) : cs[t];
+      w[h] = tf32_rn(__fsub_rn(x, cs[t]));
+      nq[h] = __fmaf_rn(w[h], w[h], nq[h]);
+    }
+    *reinterpret_cast<float4*>(op + ch * kKHalfBytes + r * 16) = make_float4(w[0], w[1], w[2], w[3]);
+  }
+  return __fadd_rn(__fadd_rn(nq[0], nq[1]), __fadd_rn(nq[2], nq[3]));
+}
+
 template <int KS>
-__global__ void __launch_bounds__(kScreenThreads, (KS <= 5 ? 3 : 1))
+__global__ void __launch_bounds__(kScreenThreads, (KS <= 5 ? 3 : 2))
 dist_screen_kernel(const ScreenParams p)
 {
   constexpr int KP = 8 * KS;
   constexpr bool kPrefetch = KS <= 5;
+  // Up to D = 36 tile J's fp32 rows stay in shared memory for the exact chain; above that they
+  // are read from XT (L2) instead, which halves the CTA's shared memory and fits two CTAs per SM.
+  constexpr bool kSmemJ = KS <= 5;
   constexpr int G = kScreenGrab;
   extern __shared__ unsigned char dyn_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* opA = base;
   unsigned char* opB = opA + KS * kKStepBytes;
   float* xJ = reinterpret_cast<float*>(opB + KS * kKStepBytes);  // [KP][128] fp32 of tile J
-  uint32_t* hitq = reinterpret_cast<uint32_t*>(xJ + KP * kScreenTile);
+  uint32_t* hitq = reinterpret_cast<uint32_t*>(xJ + (kSmemJ ? KP * kScreenTile : 0));
 
   __shared__ __align__(8) uint64_t bar_mma;
   __shared__ uint32_t s_tmem;
@@ -328,16 +354,22 @@ dist_screen_kernel(const ScreenParams p)
       __syncthreads();  // the previous item's readers of xJ / s_c are done
       if (tid < KP) s_c[tid] = tid < d ? 0.5f * (p.box_lo[tid * p.tiles + J] + p.box_hi[tid * p.tiles + J]) : 0.0f;
       const bool valid = tid < cols_j;
-      float xj[KP];
-      load_row<KP>(p.xt, p.npad, J * kScreenTile + tid, valid, xj);
+      float mj;
+      if constexpr (kSmemJ) {
+        float xj[KP];
+        load_row<KP>(p.xt, p.npad, J * kScreenTile + tid, valid, xj);
 #pragma unroll
-      for (int t = 0; t < KP; ++t) xJ[t * kScreenTile + tid] = xj[t];
-      __syncthreads();  // s_c
-      if (!valid) {
+        for (int t = 0; t < KP; ++t) xJ[t * kScreenTile + tid] = xj[t];
+        __syncthreads();  // s_c
+        if (!valid) {
 #pragma unroll
-        for (int t = 0; t < KP; ++t) xj[t] = s_c[t];  // centred to zero
+          for (int t = 0; t < KP; ++t) xj[t] = s_c[t];  // centred to zero
+        }
+        mj = build_row<KP>(xj, s_c, tid, opB);
+      } else {
+        __syncthreads();  // s_c
+        mj = build_row_xt<KP>(p.xt, p.npad, J * kScreenTile + tid, valid, s_c, tid, opB);
       }
-      const float mj = build_row<KP>(xj, s_c, tid, opB);
       const bool bad = valid && !(mj < 1e30f);
       const int any_bad = __syncthreads_or(bad);
       put_ext(opB, tid, d, false, valid && !any_bad ? col_slack(mj, se) : 1e30f);
@@ -429,9 +461,11 @@ dist_screen_kernel(const ScreenParams p)
             // rows t >= d are 0 on both sides: fma(0, 0, w) == w, so the chain over KP rows
             // is bit-identical to the chain over d
             float w = 0.0f;
+            const float* qj = p.xt + J * kScreenTile + j;
 #pragma unroll
             for (int t = 0; t < KP; ++t) {
-              const float diff = __fsub_rn(xr[t], xJ[t * kScreenTile + j]);
+              const float xjt = kSmemJ ? xJ[t * kScreenTile + j] : __ldg(qj + t * p.npad);
+              const float diff = __fsub_rn(xr[t], xjt);
               w = __fmaf_rn(diff, diff, w);
             }
             if (w <= cutoff) {
@@ -509,8 +543,8 @@ int32_t screen_rows(int32_t d) { return (d + 4 + 7) / 8 * 8; }
 static size_t screen_smem_bytes(int ks, int32_t d)
 {
   (void)d;
-  const size_t need = 1024 + static_cast<size_t>(2 * ks) * kKStepBytes +
-                      static_cast<size_t>(8 * ks) * kScreenTile * sizeof(float) + kScreenCap * sizeof(uint32_t);
+  const size_t xj = ks <= 5 ? static_cast<size_t>(8 * ks) * kScreenTile * sizeof(float) : 0;  // kSmemJ
+  const size_t need = 1024 + static_cast<size_t>(2 * ks) * kKStepBytes + xj + kScreenCap * sizeof(uint32_t);
   return need < kScreenMinSmem ? kScreenMinSmem : need;
 }
 
