@@ -189,6 +189,9 @@ struct DistLaunch {
 // [5] fallback count, [6] candidates, [7] screened tile pairs.
 bool screen_supported(int32_t d, float eps2_max);
 int32_t screen_rows(int32_t d);  // XT rows the screened pass reads (zero beyond d)
+// Tensor map over the first `rows` rows of XT (dim-major, npad floats per row): boxes of
+// {128 points, rows} (rows <= 256), zero-filled past n.
+Status make_tile_map(const float* xt, int64_t n, int32_t rows, CUtensorMap* map);
 Status launch_screened_distance(const DistLaunch& a, const float* box_lo, const float* box_hi, long long* fallback,
                                 cudaStream_t s);
 

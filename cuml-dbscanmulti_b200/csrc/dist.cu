@@ -394,6 +394,24 @@ Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* e
 
 
 // Tensor map over XT (dp x npad fp32, dim-major): boxes of {128 points, dbox dims}.
+Status make_tile_map(const float* xt, int64_t n, int32_t rows, CUtensorMap* map)
+{
+  auto encode = get_encode_fn();
+  if (!encode) return Status::Err(DBM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (rows < 1 || rows > 256) return Status::Err(DBM_ERR_INVALID, "tile map rows out of range");
+  const int64_t npad = padded_points(n);
+  const cuuint64_t gdim[2] = {static_cast<cuuint64_t>(n), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t gstride[1] = {static_cast<cuuint64_t>(npad) * sizeof(float)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTile), static_cast<cuuint32_t>(rows)};
+  const cuuint32_t estride[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(xt), gdim, gstride, box,
+                      estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return Status::Err(DBM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return Status::Ok();
+}
+
 Status make_xt_map(const float* xt, int64_t n, int32_t d, CUtensorMap* map, int32_t* dbox_out)
 {
   auto encode = get_encode_fn();

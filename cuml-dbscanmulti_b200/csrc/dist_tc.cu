@@ -32,14 +32,16 @@
 //
 // Per CTA (128 threads; thread r owns row r of tile I and column r of tile J), persistent over
 // the worklist:
-//   rows:   thread r loads its row of tile I from XT into registers, one item ahead;
+//   rows:   one TMA load stages tile I's fp32 rows ({128 points, KP dims} of XT) in the
+//           operand-A buffer, issued as soon as the previous MMA has read that buffer; thread r
+//           copies its row to registers, and after a barrier the operand is built in place;
 //   build:  centred tf32 operands in the canonical K-major no-swizzle layout (8-row x 16-byte
 //           core matrices; LBO = 2048 B between the two K halves of an MMA, SBO = 128 B
 //           between 8-row groups) plus the h / g columns; tile J (operand, and for D <= 36 an
 //           fp32 copy in shared memory) only when J changes;
 //   MMA:    KS x tcgen05.mma.cta_group::1.kind::tf32 (M = N = 128, K = 8) into 128 TMEM
 //           columns, committed to an mbarrier;
-//   screen: tcgen05.ld 32x32b.x32 -> per-thread candidate masks;
+//   screen: tcgen05.ld 32x32b.x64 (x32 for D <= 20) -> per-thread candidate masks;
 //   exact:  thread r runs the fp32 chain for each of its candidates from its registers and the
 //           fp32 tile J (shared memory, or XT for D > 36), then code, COO word and per-code
 //           histogram (dist_tri_kernel's outputs).
@@ -55,7 +57,8 @@ namespace dbm {
 constexpr int kScreenTile = 128;
 constexpr int kScreenThreads = 128;
 constexpr int kScreenCap = 1024;        // candidates per tile pair before the fallback
-constexpr int kScreenGrab = 16;         // worklist entries per chunk (one atomic each)
+constexpr int kScreenGrab = 16;         // worklist entries per chunk (one atomic each), at least
+constexpr int kScreenGrabMax = 64;      // ... and at most: larger chunks change tile J less often
 constexpr uint32_t kScreenPolls = 1u << 24;
 constexpr uint32_t kTmemCols = 128;
 constexpr uint32_t kKHalfBytes = 2048;  // one 4-column (16-byte) K slice of a 128-row operand
@@ -132,18 +135,23 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar)
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
-// 32 consecutive fp32 columns of this thread's TMEM lane; the wait is part of the same asm so
-// no use of the registers can be scheduled before the data has landed.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32])
+// 32 consecutive fp32 columns of this thread's TMEM lane, waited for in the same asm
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[32])
 {
   asm volatile(
-    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-    "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
     "tcgen05.wait::ld.sync.aligned;"
-    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-      "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-      "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+    : "r"(taddr)
+    : "memory");
+}
+// 64 consecutive fp32 columns of this thread's TMEM lane, waited for in the same asm
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&v)[64])
+{
+  asm volatile(
+    "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+    "tcgen05.wait::ld.sync.aligned;"
+    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]), "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]), "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]), "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]), "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
     : "r"(taddr)
     : "memory");
 }
@@ -258,24 +266,30 @@ __device__ __forceinline__ float build_row_xt(const float* __restrict__ xt, int6
 
 template <int KS>
 __global__ void __launch_bounds__(kScreenThreads, (KS <= 5 ? 3 : 2))
-dist_screen_kernel(const ScreenParams p)
+dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParams p)
 {
   constexpr int KP = 8 * KS;
-  constexpr bool kPrefetch = KS <= 5;
   // Up to D = 36 tile J's fp32 rows stay in shared memory for the exact chain; above that they
   // are read from XT (L2) instead, which halves the CTA's shared memory and fits two CTAs per SM.
   constexpr bool kSmemJ = KS <= 5;
-  constexpr int G = kScreenGrab;
+  // wider TMEM loads wait less often; the narrow ones keep small-D instances at 4 CTAs per SM
+  constexpr int kLdCols = KS <= 3 ? 32 : 64;
+  constexpr uint32_t kStageBytes = KP * kScreenTile * sizeof(float);  // == KS * kKStepBytes
   extern __shared__ unsigned char dyn_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
+  // Tile I arrives by TMA as fp32 [KP][128] in the operand-A buffer; every thread copies its row
+  // to registers and, after a barrier, writes the operand over it in place.
   unsigned char* opA = base;
+  const float* stage = reinterpret_cast<const float*>(opA);
   unsigned char* opB = opA + KS * kKStepBytes;
   float* xJ = reinterpret_cast<float*>(opB + KS * kKStepBytes);  // [KP][128] fp32 of tile J
   uint32_t* hitq = reinterpret_cast<uint32_t*>(xJ + (kSmemJ ? KP * kScreenTile : 0));
 
   __shared__ __align__(8) uint64_t bar_mma;
+  __shared__ __align__(8) uint64_t bar_tma;
   __shared__ uint32_t s_tmem;
   __shared__ long long s_chunk[2];  // worklist start of the current / next chunk of this CTA
+  __shared__ int s_clen[2];         // ... and its length
   __shared__ int s_cnt[2], s_hits[2];
   __shared__ int s_badJ;
   __shared__ unsigned long long s_base;
@@ -300,12 +314,27 @@ dist_screen_kernel(const ScreenParams p)
   }
   if (tid == 0) {
     mbar_init(&bar_mma, 1);
+    mbar_init(&bar_tma, 1);
     mbar_fence_init();
-    s_chunk[0] = static_cast<long long>(atomicAdd(p.counters + 4, static_cast<unsigned long long>(G)));
-    s_chunk[1] = static_cast<long long>(atomicAdd(p.counters + 4, static_cast<unsigned long long>(G)));
     s_cnt[0] = s_cnt[1] = 0;
     s_hits[0] = s_hits[1] = 0;
     s_badJ = 0;
+  }
+  // Chunks shrink with the work left (an eighth of it spread over the grid, clamped to
+  // [kScreenGrab, kScreenGrabMax]): long runs of one tile J while there is plenty of work, a short
+  // tail.  Thread 0 grabs; `seen` is the cursor as it last saw it.
+  long long seen = 0;
+  auto grab = [&](int slot) {
+    long long g = (item_count - seen) / (8LL * gridDim.x);
+    g = g < kScreenGrab ? kScreenGrab : (g > kScreenGrabMax ? kScreenGrabMax : g);
+    const long long c = static_cast<long long>(atomicAdd(p.counters + 4, static_cast<unsigned long long>(g)));
+    s_chunk[slot] = c;
+    s_clen[slot] = static_cast<int>(g);
+    seen = c + g;
+  };
+  if (tid == 0) {
+    grab(0);
+    grab(1);
   }
   tc_fence_before();
   __syncthreads();
@@ -313,11 +342,12 @@ dist_screen_kernel(const ScreenParams p)
   const uint32_t tmem = s_tmem;
   const uint32_t trow = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 
-  // The CTA's items: chunks of G consecutive worklist entries, each chunk grabbed one ahead.
+  // The CTA's items: chunks of consecutive worklist entries, each chunk grabbed one ahead.
   long long cstart = s_chunk[0];
+  int clen = s_clen[0];
   int pos = 0, m = 0;
-  auto item_index = [&](int q) -> long long {  // q-th item from the current chunk's start (q < 2G)
-    return q < G ? cstart + q : s_chunk[(m + 1) & 1] + (q - G);
+  auto item_index = [&](int q) -> long long {  // q-th item from the current chunk's start (q <= clen + 1)
+    return q < clen ? cstart + q : s_chunk[(m + 1) & 1] + (q - clen);
   };
   auto load_entry = [&](long long idx) -> long long {
     return idx < item_count ? __ldg(p.work + item_begin + idx) : -1;
@@ -325,15 +355,13 @@ dist_screen_kernel(const ScreenParams p)
   long long e_cur = load_entry(item_index(0));
   long long e_nxt = e_cur >= 0 ? load_entry(item_index(1)) : -1;
 
-  float xr[KP];  // this thread's row of the current item's tile I
-  float xn[KP];  // ... of the next item (prefetched)
-  if (e_cur >= 0) {
-    long long I0, J0;
-    screen_coords(e_cur, I0, J0);
-    load_row<KP>(p.xt, p.npad, I0 * kScreenTile + tid, I0 * kScreenTile + tid < n, xn);
+  uint32_t ph_mma = 0, ph_tma = 0;
+  bool tma_pending = false;  // a stage load is in flight (tracked by thread 0)
+  if (tid == 0 && e_cur >= 0) {
+    mbar_arrive_expect_tx(&bar_tma, kStageBytes);
+    tma_load_2d(opA, &xt_map, static_cast<int32_t>((e_cur & 0xffffffffLL) * kScreenTile), 0, &bar_tma);
+    tma_pending = true;
   }
-
-  uint32_t ph_mma = 0;
   long long curJ = -1;
   unsigned long long my_candidates = 0, my_screened = 0;
   bool failed = false;
@@ -346,12 +374,23 @@ dist_screen_kernel(const ScreenParams p)
     const bool diag = (I == J);
     const int rows_i = static_cast<int>(n - I * kScreenTile < kScreenTile ? n - I * kScreenTile : kScreenTile);
     const int cols_j = static_cast<int>(n - J * kScreenTile < kScreenTile ? n - J * kScreenTile : kScreenTile);
+
+    // ---- tile I: staged fp32 rows -> registers ----
+    const bool staged = mbar_wait_bounded(&bar_tma, ph_tma, kScreenPolls);
+    float xr[KP];  // this thread's row of tile I
 #pragma unroll
-    for (int t = 0; t < KP; ++t) xr[t] = xn[t];
+    for (int t = 0; t < KP; ++t) xr[t] = stage[t * kScreenTile + tid];
+    // every thread has read the stage (the operand overwrites it), and the previous item's
+    // readers of xJ / s_c are done
+    if (__syncthreads_or(!staged)) {
+      failed = true;
+      break;
+    }
+    ph_tma ^= 1u;
+    if (tid == 0) tma_pending = false;
 
     // ---- tile J (operand B, fp32 copy, centre) when it changes ----
     if (J != curJ) {
-      __syncthreads();  // the previous item's readers of xJ / s_c are done
       if (tid < KP) s_c[tid] = tid < d ? 0.5f * (p.box_lo[tid * p.tiles + J] + p.box_hi[tid * p.tiles + J]) : 0.0f;
       const bool valid = tid < cols_j;
       float mj;
@@ -377,7 +416,7 @@ dist_screen_kernel(const ScreenParams p)
       curJ = J;
     }
 
-    // ---- operand A from the registers ----
+    // ---- operand A, in place of the stage ----
     const bool valid_i = tid < rows_i;
     if (!valid_i) {
 #pragma unroll
@@ -389,12 +428,22 @@ dist_screen_kernel(const ScreenParams p)
     fence_proxy_async_smem();
     tc_fence_before();
     const bool skip = __syncthreads_or(bad_i) || s_badJ;
+    // the next item's tile I goes into the operand-A buffer once nothing reads it any more:
+    // right away when this item issues no MMA, else when the MMA has completed
+    auto stage_next = [&]() {
+      if (e_nxt >= 0) {
+        mbar_arrive_expect_tx(&bar_tma, kStageBytes);
+        tma_load_2d(opA, &xt_map, static_cast<int32_t>((e_nxt & 0xffffffffLL) * kScreenTile), 0, &bar_tma);
+        tma_pending = true;
+      }
+    };
     if (tid == 0) {
       s_cnt[par ^ 1] = 0;  // the previous item's counters: every thread has read them
       s_hits[par ^ 1] = 0;
       if (skip) {
         // coordinates too large for the bound's arithmetic: exact tile kernel
         p.fallback[atomicAdd(p.counters + 5, 1ULL)] = e_cur;
+        stage_next();
       } else {
         tc_fence_after();
         const uint32_t a0 = smem_u32(opA), b0 = smem_u32(opB);
@@ -404,14 +453,9 @@ dist_screen_kernel(const ScreenParams p)
         umma_commit(&bar_mma);
       }
     }
-    // prefetch the next item's rows while the MMA runs
-    if (kPrefetch && e_nxt >= 0) {
-      long long In, Jn;
-      screen_coords(e_nxt, In, Jn);
-      load_row<KP>(p.xt, p.npad, In * kScreenTile + tid, In * kScreenTile + tid < n, xn);
-    }
     if (!skip) {
       const bool ok = mbar_wait_bounded(&bar_mma, ph_mma, kScreenPolls);
+      if (tid == 0 && ok) stage_next();
       if (__syncthreads_or(!ok)) {
         failed = true;
         break;
@@ -419,26 +463,30 @@ dist_screen_kernel(const ScreenParams p)
       ph_mma ^= 1u;
       tc_fence_after();
 
-      // ---- screen: row tid of V, 32 columns per load ----
+      // ---- screen: row tid of V, kLdCols columns per TMEM load ----
       uint32_t mask[4];
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(trow + cc * 32, v);
-        uint32_t all = 0xffffffffu;
+      for (int hh = 0; hh < 128 / kLdCols; ++hh) {
+        uint32_t v[kLdCols];
+        tmem_ld(trow + hh * kLdCols, v);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) all &= v[j];
-        uint32_t hits = 0;
-        if (!(all >> 31)) {
+        for (int c2 = 0; c2 < kLdCols / 32; ++c2) {
+          const int cc = hh * (kLdCols / 32) + c2;
+          uint32_t all = 0xffffffffu;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) hits |= ((~v[j]) >> 31) << j;
-          if (diag) {
-            // strict upper triangle of the diagonal tile: columns > tid
-            const int lo = tid - cc * 32;  // keep columns cc*32 + j with j > lo
-            hits &= lo >= 31 ? 0u : (lo < 0 ? 0xffffffffu : (0xffffffffu << (lo + 1)));
+          for (int j = 0; j < 32; ++j) all &= v[c2 * 32 + j];
+          uint32_t hits = 0;
+          if (!(all >> 31)) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) hits |= ((~v[c2 * 32 + j]) >> 31) << j;
+            if (diag) {
+              // strict upper triangle of the diagonal tile: columns > tid
+              const int lo = tid - cc * 32;  // keep columns cc*32 + j with j > lo
+              hits &= lo >= 31 ? 0u : (lo < 0 ? 0xffffffffu : (0xffffffffu << (lo + 1)));
+            }
           }
+          mask[cc] = hits;
         }
-        mask[cc] = hits;
       }
       tc_fence_before();
       const int cnt = __popc(mask[0]) + __popc(mask[1]) + __popc(mask[2]) + __popc(mask[3]);
@@ -500,19 +548,15 @@ dist_screen_kernel(const ScreenParams p)
         }
       }
     }
-    if (!kPrefetch && e_nxt >= 0) {
-      long long In, Jn;
-      screen_coords(e_nxt, In, Jn);
-      load_row<KP>(p.xt, p.npad, In * kScreenTile + tid, In * kScreenTile + tid < n, xn);
-    }
     // ---- advance the item stream ----
     e_cur = e_nxt;
     e_nxt = e_nn;
     par ^= 1;
-    if (++pos == G) {
-      if (tid == 0) s_chunk[m & 1] = static_cast<long long>(atomicAdd(p.counters + 4, static_cast<unsigned long long>(G)));
+    if (++pos == clen) {
+      if (tid == 0) grab(m & 1);
       ++m;
       cstart = s_chunk[m & 1];
+      clen = s_clen[m & 1];
       pos = 0;
     }
   }
@@ -521,6 +565,7 @@ dist_screen_kernel(const ScreenParams p)
     if (tid == 0) atomicOr(p.err, kErrTmaTimeout);
     mbar_wait_bounded(&bar_mma, ph_mma, kScreenPolls);  // a bounded chance for the MMA to land
   }
+  if (tid == 0 && tma_pending) mbar_wait_bounded(&bar_tma, ph_tma, kScreenPolls);  // and the stage load
   if (tid == 0) {
     if (my_candidates) atomicAdd(p.counters + 6, my_candidates);
     if (my_screened) atomicAdd(p.counters + 7, my_screened);
@@ -551,6 +596,8 @@ static size_t screen_smem_bytes(int ks, int32_t d)
 template <int KS>
 static Status launch_screen_ks(const ScreenParams& p, int sm_count, cudaStream_t s)
 {
+  CUtensorMap map;
+  DBM_TRY(make_tile_map(p.xt, p.n, 8 * KS, &map));
   const size_t smem = screen_smem_bytes(KS, p.d);
   DBM_CUDA(cudaFuncSetAttribute(dist_screen_kernel<KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(smem)));
@@ -576,7 +623,7 @@ static Status launch_screen_ks(const ScreenParams& p, int sm_count, cudaStream_t
   if (grid > chunks) grid = chunks;
   if (grid < 1) return Status::Ok();
   count_launch();
-  dist_screen_kernel<KS><<<static_cast<unsigned>(grid), kScreenThreads, smem, s>>>(p);
+  dist_screen_kernel<KS><<<static_cast<unsigned>(grid), kScreenThreads, smem, s>>>(map, p);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
