@@ -265,7 +265,7 @@ __device__ __forceinline__ float build_row_xt(const float* __restrict__ xt, int6
 }
 
 template <int KS>
-__global__ void __launch_bounds__(kScreenThreads, (KS <= 5 ? 3 : 2))
+__global__ void __launch_bounds__(kScreenThreads, (KS <= 3 ? 4 : (KS <= 5 ? 3 : 2)))
 dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParams p)
 {
   constexpr int KP = 8 * KS;
@@ -283,7 +283,7 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
   const float* stage = reinterpret_cast<const float*>(opA);
   unsigned char* opB = opA + KS * kKStepBytes;
   float* xJ = reinterpret_cast<float*>(opB + KS * kKStepBytes);  // [KP][128] fp32 of tile J
-  uint32_t* hitq = reinterpret_cast<uint32_t*>(xJ + (kSmemJ ? KP * kScreenTile : 0));
+  uint32_t* hitq = reinterpret_cast<uint32_t*>(xJ + (kSmemJ ? KP * kScreenTile : 0));  // [2][kScreenCap]
 
   __shared__ __align__(8) uint64_t bar_mma;
   __shared__ __align__(8) uint64_t bar_tma;
@@ -292,11 +292,10 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
   __shared__ int s_clen[2];         // ... and its length
   __shared__ int s_cnt[2], s_hits[2];
   __shared__ int s_badJ;
-  __shared__ unsigned long long s_base;
   __shared__ float s_c[72];
   __shared__ float s_eps2[kMaxEps];
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int d = p.d;
   const int64_t n = p.n;
   const float cutoff = p.eps2[p.k - 1];
@@ -323,18 +322,30 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
   // Chunks shrink with the work left (an eighth of it spread over the grid, clamped to
   // [kScreenGrab, kScreenGrabMax]): long runs of one tile J while there is plenty of work, a short
   // tail.  Thread 0 grabs; `seen` is the cursor as it last saw it.
-  long long seen = 0;
+  // A chunk grabbed at a chunk boundary is needed only near the end of the following chunk, so
+  // its cursor value is stored one item later and the atomic's latency stays off the item path.
+  long long seen = 0, pend_c = 0;
+  int pend_slot = -1, pend_g = 0;
   auto grab = [&](int slot) {
     long long g = (item_count - seen) / (8LL * gridDim.x);
     g = g < kScreenGrab ? kScreenGrab : (g > kScreenGrabMax ? kScreenGrabMax : g);
-    const long long c = static_cast<long long>(atomicAdd(p.counters + 4, static_cast<unsigned long long>(g)));
-    s_chunk[slot] = c;
-    s_clen[slot] = static_cast<int>(g);
-    seen = c + g;
+    pend_c = static_cast<long long>(atomicAdd(p.counters + 4, static_cast<unsigned long long>(g)));
+    pend_g = static_cast<int>(g);
+    pend_slot = slot;
+  };
+  auto publish = [&]() {
+    if (pend_slot >= 0) {
+      s_chunk[pend_slot] = pend_c;
+      s_clen[pend_slot] = pend_g;
+      seen = pend_c + pend_g;
+      pend_slot = -1;
+    }
   };
   if (tid == 0) {
     grab(0);
+    publish();
     grab(1);
+    publish();
   }
   tc_fence_before();
   __syncthreads();
@@ -366,6 +377,31 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
   unsigned long long my_candidates = 0, my_screened = 0;
   bool failed = false;
   int par = 0;
+  // Neighbour pairs of an item are queued in shared memory (hitq[par]) and written out during the
+  // next item's MMA: each warp takes a contiguous quarter of the queue and one edge-cursor atomic.
+  int32_t prev_row0 = 0, prev_col0 = 0;
+  auto flush = [&](int slot) {
+    const int nh = s_hits[slot];
+    const int q0 = nh * warp / (kScreenThreads / 32), q1 = nh * (warp + 1) / (kScreenThreads / 32);
+    if (q1 <= q0) return;
+    unsigned long long b0 = 0;
+    if (lane == 0) b0 = atomicAdd(p.counters, static_cast<unsigned long long>(q1 - q0));
+    b0 = __shfl_sync(0xffffffffu, b0, 0);
+    for (int q = q0 + lane; q < q1; q += 32) {
+      const uint32_t e = hitq[slot * kScreenCap + q];
+      const int code = static_cast<int>(e >> 28);
+      const int32_t oi = p.perm[prev_row0 + static_cast<int>((e >> 8) & 0xffu)];
+      const int32_t oj = p.perm[prev_col0 + static_cast<int>(e & 0xffu)];
+      const int32_t lo = min(oi, oj), hi = max(oi, oj);
+      const unsigned long long idx = b0 + static_cast<unsigned long long>(q - q0);
+      if (idx < p.edge_cap)
+        p.edges[idx] = (static_cast<uint64_t>(lo) << 32) | (static_cast<uint64_t>(code) << kCodeShift) |
+                       static_cast<uint64_t>(hi);
+      int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
+      atomicAdd(hrow + oi, 1);
+      atomicAdd(hrow + oj, 1);
+    }
+  };
 
   while (e_cur >= 0) {
     const long long e_nn = e_nxt >= 0 ? load_entry(item_index(pos + 2)) : -1;  // two items ahead
@@ -438,8 +474,9 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
       }
     };
     if (tid == 0) {
-      s_cnt[par ^ 1] = 0;  // the previous item's counters: every thread has read them
-      s_hits[par ^ 1] = 0;
+      publish();
+      s_cnt[par ^ 1] = 0;  // the previous item's count: every thread has read it
+      s_hits[par] = 0;     // this item's queue: flushed during the previous item
       if (skip) {
         // coordinates too large for the bound's arithmetic: exact tile kernel
         p.fallback[atomicAdd(p.counters + 5, 1ULL)] = e_cur;
@@ -453,6 +490,7 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
         umma_commit(&bar_mma);
       }
     }
+    flush(par ^ 1);  // the previous item's pairs, while the MMA runs
     if (!skip) {
       const bool ok = mbar_wait_bounded(&bar_mma, ph_mma, kScreenPolls);
       if (tid == 0 && ok) stage_next();
@@ -520,35 +558,15 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
               int code = 0;
               while (w > s_eps2[code]) ++code;
               const int q = atomicAdd(&s_hits[par], 1);
-              hitq[q] = (static_cast<uint32_t>(code) << 28) | (static_cast<uint32_t>(tid) << 8) | static_cast<uint32_t>(j);
+              hitq[par * kScreenCap + q] = (static_cast<uint32_t>(code) << 28) | (static_cast<uint32_t>(tid) << 8) | static_cast<uint32_t>(j);
             }
-          }
-        }
-        __syncthreads();
-        const int nh = s_hits[par];
-        if (nh > 0) {
-          if (tid == 0) s_base = atomicAdd(p.counters, static_cast<unsigned long long>(nh));
-          __syncthreads();
-          const unsigned long long b0 = s_base;
-          const int32_t row0 = static_cast<int32_t>(I) * kScreenTile, col0 = static_cast<int32_t>(J) * kScreenTile;
-          for (int q = tid; q < nh; q += kScreenThreads) {
-            const uint32_t e = hitq[q];
-            const int code = static_cast<int>(e >> 28);
-            const int32_t oi = p.perm[row0 + static_cast<int>((e >> 8) & 0xffu)];
-            const int32_t oj = p.perm[col0 + static_cast<int>(e & 0xffu)];
-            const int32_t lo = min(oi, oj), hi = max(oi, oj);
-            const unsigned long long idx = b0 + static_cast<unsigned long long>(q);
-            if (idx < p.edge_cap)
-              p.edges[idx] = (static_cast<uint64_t>(lo) << 32) | (static_cast<uint64_t>(code) << kCodeShift) |
-                             static_cast<uint64_t>(hi);
-            int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
-            atomicAdd(hrow + oi, 1);
-            atomicAdd(hrow + oj, 1);
           }
         }
       }
     }
     // ---- advance the item stream ----
+    prev_row0 = static_cast<int32_t>(I) * kScreenTile;
+    prev_col0 = static_cast<int32_t>(J) * kScreenTile;
     e_cur = e_nxt;
     e_nxt = e_nn;
     par ^= 1;
@@ -561,6 +579,10 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
     }
   }
 
+  if (!failed) {
+    __syncthreads();  // the last item's queue is complete
+    flush(par ^ 1);
+  }
   if (failed) {
     if (tid == 0) atomicOr(p.err, kErrTmaTimeout);
     mbar_wait_bounded(&bar_mma, ph_mma, kScreenPolls);  // a bounded chance for the MMA to land
@@ -589,7 +611,7 @@ static size_t screen_smem_bytes(int ks, int32_t d)
 {
   (void)d;
   const size_t xj = ks <= 5 ? static_cast<size_t>(8 * ks) * kScreenTile * sizeof(float) : 0;  // kSmemJ
-  const size_t need = 1024 + static_cast<size_t>(2 * ks) * kKStepBytes + xj + kScreenCap * sizeof(uint32_t);
+  const size_t need = 1024 + static_cast<size_t>(2 * ks) * kKStepBytes + xj + 2 * kScreenCap * sizeof(uint32_t);
   return need < kScreenMinSmem ? kScreenMinSmem : need;
 }
 
