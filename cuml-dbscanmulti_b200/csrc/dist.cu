@@ -361,6 +361,40 @@ __global__ void transpose_pad_kernel(const float* __restrict__ x, float* __restr
   }
 }
 
+// The same for d <= kTransposeMaxD: 64 points per block and every row of them at once, so each
+// point's row is gathered once (one contiguous 4d-byte read) and every XT row is written as
+// 256-byte runs.  Shared pitch d or d + 1, whichever is odd (conflict-free column reads).
+constexpr int kTransposePts = 64;
+constexpr int kTransposeMaxD = 128;
+__global__ void transpose_rows_kernel(const float* __restrict__ x, float* __restrict__ xt, int64_t n, int32_t d,
+                                      int32_t dp, int64_t npad, int32_t* __restrict__ err,
+                                      const int32_t* __restrict__ perm)
+{
+  extern __shared__ float tile[];  // [kTransposePts][pitch]
+  __shared__ int32_t src[kTransposePts];
+  const int pitch = d | 1;
+  const int64_t i0 = static_cast<int64_t>(blockIdx.x) * kTransposePts;
+  if (threadIdx.x < kTransposePts) {
+    const int64_t i = i0 + threadIdx.x;
+    src[threadIdx.x] = i < n ? (perm ? perm[i] : static_cast<int32_t>(i)) : -1;
+  }
+  __syncthreads();
+  bool bad = false;
+  for (int idx = threadIdx.x; idx < kTransposePts * d; idx += blockDim.x) {
+    const int r = idx / d, t = idx - r * d;
+    const int32_t sr = src[r];
+    const float v = sr >= 0 ? x[static_cast<int64_t>(sr) * d + t] : 0.0f;
+    bad |= !isfinite(v);
+    tile[r * pitch + t] = v;
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(err, kErrNonFinite);
+  for (int idx = threadIdx.x; idx < dp * kTransposePts; idx += blockDim.x) {
+    const int t = idx / kTransposePts, r = idx - t * kTransposePts;
+    const int64_t i = i0 + r;
+    if (i < npad) xt[static_cast<int64_t>(t) * npad + i] = t < d ? tile[r * pitch + t] : 0.0f;
+  }
+}
+
 // ---- host side ------------------------------------------------------------------------------
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn()
@@ -385,9 +419,15 @@ Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* e
 {
   const int32_t dp = rows > padded_dims(d) ? rows : padded_dims(d);
   const int64_t npad = padded_points(n);
-  dim3 grid(static_cast<unsigned>(ceil_div(npad, 32)), static_cast<unsigned>(ceil_div(dp, 32)));
   count_launch();
-  transpose_pad_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xt, n, d, dp, npad, err, perm);
+  if (d <= kTransposeMaxD) {
+    const size_t smem = sizeof(float) * kTransposePts * static_cast<size_t>(d | 1);
+    transpose_rows_kernel<<<static_cast<unsigned>(ceil_div(npad, kTransposePts)), 256, smem, s>>>(x, xt, n, d, dp, npad,
+                                                                                                  err, perm);
+  } else {
+    dim3 grid(static_cast<unsigned>(ceil_div(npad, 32)), static_cast<unsigned>(ceil_div(dp, 32)));
+    transpose_pad_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xt, n, d, dp, npad, err, perm);
+  }
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
