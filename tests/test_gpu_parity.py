@@ -405,3 +405,30 @@ def test_core_sample_indices_follow_the_core_masks(h, torch_mod):
     r = h.fit_multi(x, eps, ms, return_core=True)
     dev = h.core_sample_indices(r.core)
     assert dev.is_cuda and np.array_equal(dev.cpu().numpy(), got)
+
+
+@pytest.mark.parametrize("route,rows", [("auto", None), ("dense", 700), ("annotated", 2000)])
+def test_dense_stress_calibrated_grid_matches_oracle(h, torch_mod, route, rows):
+    """The dense-route stress shape (D = 64, 10 blobs of std 2 in [-5,5]^64, no noise, minPts
+    {10, 50, 200}) with eps at the 5/10/20% quantiles of sampled pair distances, as the bench's
+    calibrated workload sets them: the largest eps links ~20% of all pairs, most tile pairs
+    overflow the screen's candidate queue and go to the exact kernel, and the core graph has
+    giant components."""
+    import bench
+
+    cfg = dict(bench.CONFIGS["c5q"], n=5000)  # >= 4096: the screened pass runs
+    pts = bench.make_points(cfg, 3)
+    eps = bench.workload_eps(cfg, pts)
+    ms = cfg["min_samples"]
+    kw = dict(index="int32")
+    if route != "auto":
+        kw["route"] = route
+    if rows:
+        kw["max_bytes_per_batch"] = dm.max_bytes_for_batch_size(len(pts), len(eps), len(ms), rows, "cuvs", 0,
+                                                                "int32")
+    labels, core, r = gpu_fit(h, torch_mod, pts, eps, ms, **kw)
+    assert r.stats["screened_tile_pairs"] > 0 and r.stats["fallback_tile_pairs"] > 0
+    ol, oc, odeg = oracle.fit_multi(pts, eps, ms, r.stats["batch_size"])
+    assert np.array_equal(core, oc)
+    assert np.array_equal(labels, ol)
+    assert (odeg[-1] - 1).sum() > 0.15 * len(pts) * (len(pts) - 1)  # really dense
