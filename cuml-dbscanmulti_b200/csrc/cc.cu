@@ -49,6 +49,8 @@ struct CcArgs {
   int64_t n;
   int k, l, cfg_begin, cfg_end;
   const int32_t* cc;  // k x n: core iff m < cc[e*n + i]
+  int sample_shift = 0;  // union over every 2^s-th entry only (0: all entries)
+  bool quick = false;    // union: skip entries whose endpoints already share a parent
 };
 
 __device__ __forceinline__ void cfg_range(const CcArgs& a, int e, int& m_lo, int& m_hi)
@@ -96,12 +98,14 @@ __device__ __forceinline__ void for_each_entry_cfg(const CcArgs& a, F&& f)
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t L = a.l;
+  const int sh = a.sample_shift;
   if (a.ms.direct) {
     const SlabRef& s = a.ms.s[0];
-    const int64_t total = s.count * L;
+    const int64_t total = ((s.count + (int64_t(1) << sh) - 1) >> sh) * L;
     for (int64_t x = t0; x < total; x += stride) {
-      const int64_t q = x / L;
-      const int m = static_cast<int>(x - q * L);
+      const int64_t qs = x / L;
+      const int m = static_cast<int>(x - qs * L);
+      const int64_t q = qs << sh;
       const uint32_t w = static_cast<uint32_t>(s.col[q]);
       const int32_t j = static_cast<int32_t>(w & kColMask);
       const int32_t r = s.row[q];
@@ -122,9 +126,9 @@ __device__ __forceinline__ void for_each_entry_cfg(const CcArgs& a, F&& f)
       const int64_t b = s.begin_dev ? *s.begin_dev : 0;
       const int64_t lim = s.end_dev ? *s.end_dev : s.count;
       const int64_t span = m_hi - m_lo;
-      const int64_t total = (lim - b) * span;
+      const int64_t total = ((lim - b + (int64_t(1) << sh) - 1) >> sh) * span;
       for (int64_t x = t0; x < total; x += stride) {
-        const int64_t q = b + x / span;
+        const int64_t q = b + ((x / span) << sh);
         const int m = m_lo + static_cast<int>(x % span);
         f(e, m, s.row[q], s.col[q] & static_cast<int32_t>(kColMask));
       }
@@ -152,13 +156,29 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
 {
   bool ok = true;
   for_each_entry_cfg(a, [&](int e, int m, int32_t r, int32_t j) {
+    const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
+    // after a compression, endpoints of one component mostly point at the same root: equal
+    // parents mean the union is a no-op (exact whatever the state of the forest)
+    if (a.quick && P[base + r] == P[base + j] && (!Q || Q[base + r] == Q[base + j])) return;
     const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
     if (m >= cc[r] || m >= cc[j]) return;
-    const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
     ok &= uf_unite(P + base, r, j);
     if (Q) ok &= uf_unite(Q + base, r, j);
   });
   if (!ok) atomicOr(err, kErrUnionLimit);
+}
+
+// P[x] = root of x for every x of the configs [c0, c1) (full path compression)
+__global__ void cc_compress_kernel(int64_t n, int c0, int c1, int32_t* __restrict__ P)
+{
+  const int64_t total = static_cast<int64_t>(c1 - c0) * n;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total; x += stride) {
+    const int64_t cfg = c0 + x / n, i = x % n;
+    int32_t* g = P + cfg * n;
+    const int32_t root = uf_find(g, static_cast<int32_t>(i));
+    if (g[i] != root) g[i] = root;
+  }
 }
 
 // For every entry with exactly one core endpoint c: best[p] = min(tag << 32 | find(P, c)).
@@ -255,6 +275,8 @@ __global__ void cc_labels_kernel(int64_t n, int k, int l, int64_t x0, int64_t x1
 }
 
 // ---- launchers ----------------------------------------------------------------------------
+// neighbour entries per point from which a one-batch labelling takes the sampled union path
+constexpr int64_t kDenseEntriesPerRow = 64;
 static inline unsigned blocks_for(int64_t work, int threads)
 {
   return static_cast<unsigned>(ceil_div(work > 0 ? work : 1, threads));
@@ -283,7 +305,23 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
     std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries, 256), static_cast<int64_t>(sm_count) * 16)));
   const unsigned nbu = static_cast<unsigned>(
     std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries * l, 256), static_cast<int64_t>(sm_count) * 32)));
-  if (single_batch) {
+  if (single_batch && upper_entries >= kDenseEntriesPerRow * n) {
+    // dense graph (afforest-style sampling, Sutton et al. 2018): unite a 1/8 sample of the
+    // entries, compress, then the full pass finds most endpoint pairs already under one root and
+    // skips them after two loads; the forest's roots are the same as a plain pass would leave
+    CcArgs sa = a;
+    sa.sample_shift = 3;
+    CcArgs qa = a;
+    qa.quick = true;
+    const unsigned nbs = static_cast<unsigned>(std::max<int64_t>(1, nbu / 8));
+    const unsigned nbc = static_cast<unsigned>(std::max<int64_t>(
+      1, std::min<int64_t>(ceil_div(static_cast<int64_t>(cfg_end - cfg_begin) * n, 256), static_cast<int64_t>(sm_count) * 16)));
+    count_launch(4);
+    cc_union_kernel<<<nbs, 256, 0, s>>>(sa, G, nullptr, err);
+    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, G);
+    cc_union_kernel<<<nbu, 256, 0, s>>>(qa, G, nullptr, err);
+    cc_best_kernel<<<nb, 256, 0, s>>>(a, G, best, tag);
+  } else if (single_batch) {
     count_launch(2);
     cc_union_kernel<<<nbu, 256, 0, s>>>(a, G, nullptr, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, G, best, tag);
