@@ -45,7 +45,8 @@
 //   exact:  thread r runs the fp32 chain for each of its candidates from its registers and the
 //           fp32 tile J (shared memory, or XT for D > 36), then code, COO word and per-code
 //           histogram (dist_tri_kernel's outputs).
-// A tile pair whose bound admits more than kScreenCap candidates (dense regime), or whose
+// A tile pair whose bound admits more than kScreenCap candidates (kScreenCapXT above D = 36;
+// dense regime), or whose
 // coordinates are too large for the bound, is appended to a fallback list for dist_tri_kernel.
 #include "dbm_internal.cuh"
 
@@ -57,6 +58,9 @@ namespace dbm {
 constexpr int kScreenTile = 128;
 constexpr int kScreenThreads = 128;
 constexpr int kScreenCap = 1024;        // candidates per tile pair before the fallback
+// ... above D = 36, where each candidate's exact chain reads tile J's row from L2: a tile pair
+// with that many candidates is cheaper in the exact tile kernel
+constexpr int kScreenCapXT = 256;
 constexpr int kScreenGrab = 16;         // worklist entries per chunk (one atomic each), at least
 constexpr int kScreenGrabMax = 64;      // ... and at most: larger chunks change tile J less often
 constexpr uint32_t kScreenPolls = 1u << 24;
@@ -533,7 +537,7 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
       const int total = s_cnt[par];
       my_screened += 1;
       my_candidates += static_cast<unsigned long long>(total);
-      if (total > kScreenCap) {
+      if (total > (kSmemJ ? kScreenCap : kScreenCapXT)) {
         if (tid == 0) p.fallback[atomicAdd(p.counters + 5, 1ULL)] = e_cur;
       } else if (total > 0) {
         // ---- exact chain for each candidate of this row ----
