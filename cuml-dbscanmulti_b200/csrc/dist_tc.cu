@@ -46,8 +46,8 @@
 //           fp32 tile J (shared memory, or XT for D > 36), then code, COO word and per-code
 //           histogram (dist_tri_kernel's outputs).
 // A tile pair whose bound admits more than kScreenCap candidates (kScreenCapXT above D = 36;
-// dense regime), or whose
-// coordinates are too large for the bound, is appended to a fallback list for dist_tri_kernel.
+// dense regime), or whose coordinates are too large for the bound, is appended to a fallback
+// list for dist_tri_kernel.
 #include "dbm_internal.cuh"
 
 #include <algorithm>
