@@ -69,6 +69,68 @@ def balanced_config_ranges(cost: list[float], world: int) -> list[tuple[int, int
     return ranges
 
 
+# Relative per-element costs of the labelling kernels, fitted to one-GPU C4 timings (0.92 ms of
+# slab walks over 4.25e6 entries, 1.27 ms of unions over 1.63e7 (entry, config) pairs, 0.35 ms
+# of relabel over 1.6e7 (point, config) pairs): the per-eps slab walks (compaction, touch,
+# border candidates, border fold) per entry of an eps the rank owns any config of, the union
+# per (entry, owned config), the relabel per (point, owned config).
+LABEL_COST_WALK = 22.0
+LABEL_COST_UNION = 7.8
+LABEL_COST_RELABEL = 2.2
+
+
+def labelling_cost(per_eps: list[float], l: int, n: int, a: int, b: int) -> float:
+    """Model cost of labelling the configs [a, b) (eps-major, l per eps)."""
+    if b <= a:
+        return 0.0
+    e0, e1 = a // l, (b - 1) // l
+    walk = sum(per_eps[e0:e1 + 1])
+    union = sum(per_eps[c // l] for c in range(a, b))
+    return LABEL_COST_WALK * walk + LABEL_COST_UNION * union + LABEL_COST_RELABEL * n * (b - a)
+
+
+def labelling_ranges(per_eps: list[float], l: int, n: int, world: int) -> list[tuple[int, int]]:
+    """Contiguous config ranges, one per rank, minimising the largest modelled labelling cost
+    (bisection on the bound with a greedy feasibility sweep; the cost of a range only grows as
+    it widens).  A rank's cost counts each eps it touches once for the slab walks, so the split
+    prefers to keep an eps's configs together.  Deterministic: every rank computes the same
+    split from the same (all-reduced) entry counts."""
+    c = len(per_eps) * l
+    if world <= 1 or c == 0:
+        return [(0, c)] + [(c, c)] * max(0, world - 1)
+
+    def cost(a, b):
+        return labelling_cost(per_eps, l, n, a, b)
+
+    def sweep(bound):
+        out, a = [], 0
+        while a < c:
+            b = a + 1
+            while b < c and cost(a, b + 1) <= bound:
+                b += 1
+            out.append((a, b))
+            a = b
+        return out
+
+    lo = max(cost(i, i + 1) for i in range(c))
+    hi = cost(0, c)
+    for _ in range(60):
+        mid = 0.5 * (lo + hi)
+        if len(sweep(mid)) <= world:
+            hi = mid
+        else:
+            lo = mid
+    ranges = sweep(hi)
+    # every rank gets work while configs remain: split the costliest multi-config range in two
+    while len(ranges) < min(world, c):
+        i = max((j for j in range(len(ranges)) if ranges[j][1] - ranges[j][0] > 1),
+                key=lambda j: (cost(*ranges[j]), -j))
+        a, b = ranges[i]
+        best = min(range(a + 1, b), key=lambda s: (max(cost(a, s), cost(s, b)), s))
+        ranges[i:i + 1] = [(a, best), (best, b)]
+    return ranges + [(c, c)] * (world - len(ranges))
+
+
 class DeviceStages:
     """The C-ABI stages on this rank's GPU."""
 
@@ -221,12 +283,11 @@ def sharded_fit_multi(stages, x, eps, min_samples, *, group=None, max_bytes_per_
     parts = _all_gather_varlen(dist, edges, group)
     all_edges = torch.cat(parts) if parts else edges
 
-    # configs split by cost: the labelling walks the neighbour entries of each config's eps, so
-    # balance the per-eps entry counts (known identically on every rank from the summed
-    # histograms) instead of the number of configs
-    per_eps = hist.to(torch.int64).cumsum(0).sum(1).cpu().tolist()
-    cost = [float(per_eps[c // l]) + 1.0 for c in range(k * l)]
-    ranges = balanced_config_ranges(cost, world)
+    # configs split by modelled labelling cost: the slab walks of each eps a rank touches, the
+    # union per owned config and the relabel, from the per-eps entry counts (known identically
+    # on every rank from the summed histograms)
+    per_eps = [float(v) for v in hist.to(torch.int64).cumsum(0).sum(1).cpu().tolist()]
+    ranges = labelling_ranges(per_eps, l, n, world)
     c0, c1 = ranges[rank]
     if c1 > c0:
         labels, stats, routes = stages.fit_from_graph(n, d, e, m, hist, all_edges, c0, c1, opt)

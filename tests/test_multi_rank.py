@@ -228,3 +228,34 @@ def test_balanced_config_ranges_partition_and_balance():
     rs = parallel.balanced_config_ranges([1] * 12 + [100] * 4, 4)
     assert rs[-1][1] - rs[-1][0] <= 2
     assert parallel.balanced_config_ranges([1.0] * 16, 4) == [(0, 4), (4, 8), (8, 12), (12, 16)]
+
+
+def _brute_force_best(per_eps, l, n, world):
+    import itertools
+
+    c = len(per_eps) * l
+    best = None
+    for cuts in itertools.combinations(range(1, c), min(world, c) - 1):
+        bounds = (0,) + cuts + (c,)
+        worst = max(parallel.labelling_cost(per_eps, l, n, a, b) for a, b in zip(bounds, bounds[1:]))
+        best = worst if best is None else min(best, worst)
+    return best
+
+
+def test_labelling_ranges_partition_and_match_the_brute_force_optimum():
+    rng = np.random.default_rng(8)
+    for k, l in ((1, 5), (3, 2), (4, 4), (5, 1)):
+        for world in (1, 2, 3, 4, 8):
+            per_eps = sorted(float(v) for v in rng.uniform(0, 1e6, k))  # nested eps: counts grow
+            n = 100_000
+            rs = parallel.labelling_ranges(per_eps, l, n, world)
+            c = k * l
+            assert len(rs) == world and rs[0][0] == 0 and rs[-1][1] == c
+            assert all(a[1] == b[0] and a[0] <= a[1] for a, b in zip(rs, rs[1:]))
+            if c >= world:
+                assert all(b > a for a, b in rs)
+            got = max(parallel.labelling_cost(per_eps, l, n, a, b) for a, b in rs)
+            assert got <= _brute_force_best(per_eps, l, n, world) * (1 + 1e-9)
+    # identical on every rank: a pure function of its inputs
+    pe = [250.0, 19000.0, 371500.0, 3862750.0]
+    assert parallel.labelling_ranges(pe, 4, 10**6, 8) == parallel.labelling_ranges(list(pe), 4, 10**6, 8)
