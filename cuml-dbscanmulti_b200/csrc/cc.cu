@@ -50,7 +50,7 @@ struct CcArgs {
   int k, l, cfg_begin, cfg_end;
   const int32_t* cc;  // k x n: core iff m < cc[e*n + i]
   int sample_shift = 0;  // union over every 2^s-th entry only (0: all entries)
-  bool quick = false;    // union: skip entries whose endpoints already share a parent
+  bool quick = false;    // union: skip a union-find whose two endpoints already share a parent
 };
 
 __device__ __forceinline__ void cfg_range(const CcArgs& a, int e, int& m_lo, int& m_hi)
@@ -157,13 +157,16 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
   bool ok = true;
   for_each_entry_cfg(a, [&](int e, int m, int32_t r, int32_t j) {
     const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
-    // after a compression, endpoints of one component mostly point at the same root: equal
-    // parents mean the union is a no-op (exact whatever the state of the forest)
-    if (a.quick && P[base + r] == P[base + j] && (!Q || Q[base + r] == Q[base + j])) return;
+    // equal parents mean the union is a no-op, exact whatever the state of the forest (a stale
+    // batch-local parent of a non-core endpoint can only skip a union the core test below would
+    // skip too); after a compression most endpoint pairs of one component take this exit
+    const bool skip_p = a.quick && P[base + r] == P[base + j];
+    const bool skip_q = !Q || (a.quick && Q[base + r] == Q[base + j]);
+    if (skip_p && skip_q) return;
     const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
     if (m >= cc[r] || m >= cc[j]) return;
-    ok &= uf_unite(P + base, r, j);
-    if (Q) ok &= uf_unite(Q + base, r, j);
+    if (!skip_p) ok &= uf_unite(P + base, r, j);
+    if (!skip_q) ok &= uf_unite(Q + base, r, j);
   });
   if (!ok) atomicOr(err, kErrUnionLimit);
 }
@@ -300,7 +303,8 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
                        cudaStream_t s)
 {
   if (upper_entries <= 0 || cfg_begin >= cfg_end) return Status::Ok();
-  const CcArgs a{ms, n, k, l, cfg_begin, cfg_end, cc};
+  CcArgs a{ms, n, k, l, cfg_begin, cfg_end, cc};
+  a.quick = true;
   const unsigned nb = static_cast<unsigned>(
     std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries, 256), static_cast<int64_t>(sm_count) * 16)));
   const unsigned nbu = static_cast<unsigned>(
@@ -311,15 +315,13 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
     // skips them after two loads; the forest's roots are the same as a plain pass would leave
     CcArgs sa = a;
     sa.sample_shift = 3;
-    CcArgs qa = a;
-    qa.quick = true;
     const unsigned nbs = static_cast<unsigned>(std::max<int64_t>(1, nbu / 8));
     const unsigned nbc = static_cast<unsigned>(std::max<int64_t>(
       1, std::min<int64_t>(ceil_div(static_cast<int64_t>(cfg_end - cfg_begin) * n, 256), static_cast<int64_t>(sm_count) * 16)));
     count_launch(4);
     cc_union_kernel<<<nbs, 256, 0, s>>>(sa, G, nullptr, err);
     cc_compress_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, G);
-    cc_union_kernel<<<nbu, 256, 0, s>>>(qa, G, nullptr, err);
+    cc_union_kernel<<<nbu, 256, 0, s>>>(a, G, nullptr, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, G, best, tag);
   } else if (single_batch) {
     count_launch(2);
