@@ -210,21 +210,27 @@ class DeviceStages:
         return labels, st.as_dict(), [ROUTE_NAMES[int(routes[i])] for i in range(int(st.batches))]
 
 
-def _all_gather_varlen(dist, t, group):
-    """All-gather 1-D tensors of different lengths (pads to the longest); returns the parts."""
+def _all_gather_varlen(dist, t, group, extra=None):
+    """All-gather 1-D tensors of different lengths: one exchange of the counts, then one flat
+    all_gather of buffers padded to the longest; returns the parts.  `extra`, a tensor already
+    queued on the stream, is copied to the host in the same synchronisation as the counts and
+    returned with the parts (or None)."""
     import torch
 
     world = dist.get_world_size(group)
     cnt = torch.tensor([t.numel()], dtype=torch.int64, device=t.device)
-    counts = [torch.zeros_like(cnt) for _ in range(world)]
-    dist.all_gather(counts, cnt, group=group)
-    counts = [int(c.item()) for c in counts]
-    mx = max(counts) if counts else 0
-    buf = torch.empty(max(mx, 1), dtype=t.dtype, device=t.device)
+    counts_t = torch.zeros(world, dtype=torch.int64, device=t.device)
+    dist.all_gather_into_tensor(counts_t, cnt, group=group)
+    host = counts_t.cpu()
+    extra_host = extra.cpu() if extra is not None else None
+    counts = [int(c) for c in host.tolist()]
+    mx = max(max(counts), 1)
+    buf = torch.empty(mx, dtype=t.dtype, device=t.device)
     buf[: t.numel()] = t
-    out = [torch.empty_like(buf) for _ in range(world)]
-    dist.all_gather(out, buf, group=group)
-    return [o[:c] for o, c in zip(out, counts)]
+    out = torch.empty(world * mx, dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, buf, group=group)
+    parts = [out[r * mx: r * mx + c] for r, c in enumerate(counts)]
+    return (parts, extra_host) if extra is not None else parts
 
 
 def _gather_config_rows(dist, labels, C: int, n: int, group, ranges=None):
@@ -280,13 +286,15 @@ def sharded_fit_multi(stages, x, eps, min_samples, *, group=None, max_bytes_per_
     hint = n * (neigh_per_row if neigh_per_row > 0 else 16) // (2 * world) + 1024
     hist, edges = stages.distance_shard(x, e, rank, world, hint)
     dist.all_reduce(hist, op=dist.ReduceOp.SUM, group=group)
-    parts = _all_gather_varlen(dist, edges, group)
+    # per-eps entry counts ride along with the pair counts' host synchronisation
+    per_eps_dev = hist.to(torch.int64).cumsum(0).sum(1)
+    parts, per_eps_host = _all_gather_varlen(dist, edges, group, extra=per_eps_dev)
     all_edges = torch.cat(parts) if parts else edges
 
     # configs split by modelled labelling cost: the slab walks of each eps a rank touches, the
     # union per owned config and the relabel, from the per-eps entry counts (known identically
     # on every rank from the summed histograms)
-    per_eps = [float(v) for v in hist.to(torch.int64).cumsum(0).sum(1).cpu().tolist()]
+    per_eps = [float(v) for v in per_eps_host.tolist()]
     ranges = labelling_ranges(per_eps, l, n, world)
     c0, c1 = ranges[rank]
     if c1 > c0:
