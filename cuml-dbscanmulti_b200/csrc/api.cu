@@ -891,9 +891,9 @@ int dbm_fit_multi(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const
   }
   dbm::resolve_phase_timers(h);
   if (stats) *stats = st;
-  if (batch_routes && routes_len > 0) {
-    for (int i = 0; i < routes_len; ++i)
-      batch_routes[i] = i < static_cast<int>(routes.size()) ? routes[i] : DBM_BATCH_NOT_APPLICABLE;
+  if (batch_routes && routes_len > 0) {  // the batches only: the tail is left untouched
+    const int nr = std::min(routes_len, static_cast<int>(routes.size()));
+    for (int i = 0; i < nr; ++i) batch_routes[i] = routes[i];
   }
   if (!r.ok()) {
     dbm::set_err(err, err_len, r.msg);
@@ -1035,9 +1035,10 @@ int dbm_fit_multi_from_graph(dbm_handle* h, int64_t n, int64_t d, const float* e
   dbm::resolve_phase_timers(h);
   st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
   if (stats) *stats = st;
-  if (batch_routes && routes_len > 0)
-    for (int i = 0; i < routes_len; ++i)
-      batch_routes[i] = i < static_cast<int>(routes.size()) ? routes[i] : DBM_BATCH_NOT_APPLICABLE;
+  if (batch_routes && routes_len > 0) {  // the batches only: the tail is left untouched
+    const int nr = std::min(routes_len, static_cast<int>(routes.size()));
+    for (int i = 0; i < nr; ++i) batch_routes[i] = routes[i];
+  }
   dbm::set_err(err, err_len, r.msg);
   return r.code;
 }

@@ -333,6 +333,14 @@ class DbscanMulti:
             raise DbmError(rc, err.value.decode())
         return out.cpu().numpy() if on_host else out
 
+    def _routes_buffer(self, size: int):
+        """A per-handle route buffer of at least `size` bytes (the library writes only the
+        batches' entries, so it is reused without clearing)."""
+        buf = getattr(self, "_routes", None)
+        if buf is None or len(buf) < size:
+            buf = self._routes = (ctypes.c_uint8 * size)()
+        return buf
+
     def fit_multi(self, x, eps, min_samples, *, max_bytes_per_batch: int = 0, backend: str = "cuvs",
                   index: str = "auto", route: str = "auto", neigh_per_row: int = 0,
                   csr_cap_bytes: int = 0, return_core: bool = False, labels_out=None,
@@ -352,7 +360,7 @@ class DbscanMulti:
             x = x.contiguous()
             n, d = int(x.shape[0]), int(x.shape[1])
             maxb = n + 1
-            routes = (ctypes.c_uint8 * maxb)()
+            routes = self._routes_buffer(maxb)
             labels = labels_out if labels_out is not None else torch.empty((k * l, n), dtype=torch.int32, device=x.device)
             core = torch.empty((k * l, n), dtype=torch.uint8, device=x.device) if return_core else None
             s = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
@@ -368,7 +376,7 @@ class DbscanMulti:
             # NaN/Inf are detected on the device (DBM_ERR_NONFINITE)
             n, d = xh.shape
             maxb = n + 1
-            routes = (ctypes.c_uint8 * maxb)()
+            routes = self._routes_buffer(maxb)
             if labels_out is not None:
                 labels = labels_out
                 if (labels.dtype != np.int32 or labels.shape != (k * l, n)

@@ -196,7 +196,7 @@ class DeviceStages:
         k, l = len(eps), len(ms)
         labels = torch.empty((k * l, n), dtype=torch.int32, device=hist.device)
         st = Stats()
-        routes = (ctypes.c_uint8 * (n + 1))()
+        routes = self.h._routes_buffer(n + 1)
         s = torch.cuda.current_stream(hist.device).cuda_stream
         err = ctypes.create_string_buffer(1024)
         edges = edges.contiguous()

@@ -145,7 +145,8 @@ int dbm_set_distance_mode(dbm_handle* h, int mode);
  * opt:          NULL = defaults (cuvs backend, auto index, auto route, worst-case
  *               neighbours, automatic budget)
  * stats:        optional out
- * batch_routes: optional out, DBM_BATCH_* per batch (ascending), routes_len entries
+ * batch_routes: optional out, DBM_BATCH_* per batch (ascending), at most routes_len entries;
+ *               only the first stats->batches entries are written
  * Synchronises `stream` before returning (like the reference, which reads per-batch
  * sizes back to the host).
  */
