@@ -312,7 +312,7 @@ def run_reference(args, cfg) -> None:
     out = {
         "impl": "reference", "metric": "pair_distances_per_s", "value": value, "unit": "pairs/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": n * n / value * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": n * n / value * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.config, "desc": cfg["desc"], "n": n, "d": cfg["d"],
                    "eps": cfg["eps"], "min_samples": cfg["min_samples"]},
