@@ -78,10 +78,11 @@ Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0,
                               cudaStream_t s);
 Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int ne,
                          const int64_t* off_flat, int32_t* col_flat, int32_t* row_flat, cudaStream_t s);
-Status launch_cc_roots(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
-                       int32_t* flags, cudaStream_t s);
-Status launch_cc_labels(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
-                        const int32_t* cur, const int64_t* rank, int32_t* labels, cudaStream_t s);
+Status launch_cc_root_bits(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc, int32_t* G,
+                           uint32_t* words, int32_t* cnt, int sm_count, cudaStream_t s);
+Status launch_cc_labels(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc, int32_t* G,
+                        const int32_t* cur, const uint32_t* words, const int64_t* wrank, int32_t* labels,
+                        cudaStream_t s);
 
 // ---- batch-size rules (runner_multi.cuh:79-119, 214-268, 437-499) --------------------------
 struct Plan {
@@ -729,14 +730,20 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
   // ---- final relabel of the configs [cfg_begin, cfg_end) ----
   {
     PhaseTimer t(h, s, &st.ms_relabel);
-    const int64_t x0 = static_cast<int64_t>(cfg_begin) * n, x1 = static_cast<int64_t>(cfg_end) * n;
-    DBM_TRY(ensure(h->flags, sizeof(int32_t) * kln));
-    DBM_TRY(ensure(h->rank, sizeof(int64_t) * (kln + 1)));
-    DBM_TRY(launch_cc_roots(n, k, l, x0, x1, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->flags), s));
-    DBM_TRY(exclusive_scan_i32(as<int32_t>(h->flags) + x0, as<int64_t>(h->rank), x1 - x0, h->scan_scratch.p,
-                               h->scan_scratch.bytes, s));
-    DBM_TRY(launch_cc_labels(n, k, l, x0, x1, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->cur),
-                             as<int64_t>(h->rank), labels, s));
+    // roots as a bitmap (one 32-bit word per 32 points and config): the rank of a root is the
+    // scan of the words' popcounts plus the bits below it, so the scan runs over n/32 words per
+    // config instead of n flags
+    const int64_t W = ceil_div(n, 32);
+    const int64_t words_all = static_cast<int64_t>(k) * l * W, owned = static_cast<int64_t>(cfg_end - cfg_begin) * W;
+    DBM_TRY(ensure(h->flags, sizeof(uint32_t) * static_cast<size_t>(words_all + owned)));
+    DBM_TRY(ensure(h->rank, sizeof(int64_t) * static_cast<size_t>(owned + 1)));
+    uint32_t* words = as<uint32_t>(h->flags);
+    int32_t* cnt = as<int32_t>(h->flags) + words_all;
+    DBM_TRY(launch_cc_root_bits(n, l, cfg_begin, cfg_end, W, as<int32_t>(h->cc), as<int32_t>(h->G), words, cnt,
+                                h->sm_count, s));
+    DBM_TRY(exclusive_scan_i32(cnt, as<int64_t>(h->rank), owned, h->scan_scratch.p, h->scan_scratch.bytes, s));
+    DBM_TRY(launch_cc_labels(n, l, cfg_begin, cfg_end, W, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->cur),
+                             words, as<int64_t>(h->rank), labels, s));
   }
   DBM_TRY(read_err_flag(h, s));
   return Status::Ok();

@@ -230,51 +230,58 @@ __global__ void cc_border_kernel(const CcArgs a, int32_t* __restrict__ G,
   });
 }
 
-// flags[cfg][i] = 1 for the root of every core component (compressing G on the way); only the
-// configs [x0 / n, x1 / n) are touched.
-__global__ void cc_roots_kernel(int64_t n, int k, int l, int64_t x0, int64_t x1,
-                                const int32_t* __restrict__ cc, int32_t* __restrict__ G,
-                                int32_t* __restrict__ flags)
+// Roots of the configs [c0, c1) as a bitmap: config cfg owns W = ceil(n / 32) words, bit i of its
+// word i / 32 is set iff i is the root (minimum index) of a core component; cnt[w - c0 * W] is the
+// popcount of word w.  One thread per (config, padded point), so every warp covers one whole word.
+__global__ void cc_root_bits_kernel(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* __restrict__ cc,
+                                    int32_t* __restrict__ G, uint32_t* __restrict__ words, int32_t* __restrict__ cnt)
 {
-  const int64_t x = x0 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (x >= x1) return;
-  const int64_t cfg = x / n, i = x - cfg * n;
-  const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
-  int32_t f = 0;
-  if (m < cc[static_cast<int64_t>(e) * n + i]) {
-    const int32_t root = uf_find(G + cfg * n, static_cast<int32_t>(i));
-    f = (root == static_cast<int32_t>(i));
+  const int64_t per = W * 32;
+  const int64_t total = static_cast<int64_t>(c1 - c0) * per;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;  // a multiple of 32
+  for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total; x += stride) {
+    const int64_t cl = x / per, i = x - cl * per, cfg = c0 + cl;
+    const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
+    bool root = false;
+    if (i < n && m < cc[static_cast<int64_t>(e) * n + i])
+      root = uf_find(G + cfg * n, static_cast<int32_t>(i)) == static_cast<int32_t>(i);
+    const uint32_t bits = __ballot_sync(0xffffffffu, root);
+    if ((threadIdx.x & 31) == 0) {
+      const int64_t w = cl * W + i / 32;
+      words[c0 * W + w] = bits;
+      cnt[w] = __popc(bits);
+    }
   }
-  flags[x] = f;
 }
 
-// cluster id = rank of the component root among the config's roots; -1 noise
-__global__ void cc_labels_kernel(int64_t n, int k, int l, int64_t x0, int64_t x1,
-                                 const int32_t* __restrict__ cc, int32_t* __restrict__ G,
-                                 const int32_t* __restrict__ cur, const int64_t* __restrict__ rank,
+// cluster id = rank of the component root among the config's roots (word prefix from the scan of
+// the popcounts, plus the set bits below the root in its word); -1 noise
+__global__ void cc_labels_kernel(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* __restrict__ cc,
+                                 int32_t* __restrict__ G, const int32_t* __restrict__ cur,
+                                 const uint32_t* __restrict__ words, const int64_t* __restrict__ wrank,
                                  int32_t* __restrict__ labels)
 {
+  const int64_t x0 = static_cast<int64_t>(c0) * n;
   const int64_t x = x0 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (x >= x1) return;
+  if (x >= static_cast<int64_t>(c1) * n) return;
   const int64_t cfg = x / n, i = x - cfg * n;
   const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
   int32_t* g = G + cfg * n;
-  const int64_t rb = cfg * n - x0;  // rank holds the scan of flags[x0, x1)
-  const int64_t r0 = rank[rb];
-  int32_t out;
+  int32_t v;
   if (m < cc[static_cast<int64_t>(e) * n + i]) {
-    const int32_t root = uf_find(g, static_cast<int32_t>(i));
-    out = static_cast<int32_t>(rank[rb + root] - r0);
+    v = static_cast<int32_t>(i);
   } else {
-    const int32_t v = cur[x];
+    v = cur[x];
     if (v == kNone) {
-      out = -1;
-    } else {
-      const int32_t root = uf_find(g, v);
-      out = static_cast<int32_t>(rank[rb + root] - r0);
+      labels[x] = -1;
+      return;
     }
   }
-  labels[x] = out;
+  const int32_t root = uf_find(g, v);
+  const int64_t wl = (cfg - c0) * W;  // this config's first word in the scanned range
+  const int64_t w = wl + root / 32;
+  const uint32_t below = words[cfg * W + root / 32] & ((1u << (root & 31)) - 1u);
+  labels[x] = static_cast<int32_t>(wrank[w] - wrank[wl]) + __popc(below);
 }
 
 // ---- launchers ----------------------------------------------------------------------------
@@ -341,20 +348,27 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
   return Status::Ok();
 }
 
-Status launch_cc_roots(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
-                       int32_t* flags, cudaStream_t s)
+Status launch_cc_root_bits(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc, int32_t* G,
+                           uint32_t* words, int32_t* cnt, int sm_count, cudaStream_t s)
 {
+  const int64_t total = static_cast<int64_t>(c1 - c0) * W * 32;
+  if (total <= 0) return Status::Ok();
+  const unsigned grid = static_cast<unsigned>(std::max<int64_t>(
+    1, std::min<int64_t>(ceil_div(total, 256), static_cast<int64_t>(sm_count) * 32)));
   count_launch();
-  cc_roots_kernel<<<blocks_for(x1 - x0, 256), 256, 0, s>>>(n, k, l, x0, x1, cc, G, flags);
+  cc_root_bits_kernel<<<grid, 256, 0, s>>>(n, l, c0, c1, W, cc, G, words, cnt);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
 
-Status launch_cc_labels(int64_t n, int k, int l, int64_t x0, int64_t x1, const int32_t* cc, int32_t* G,
-                        const int32_t* cur, const int64_t* rank, int32_t* labels, cudaStream_t s)
+Status launch_cc_labels(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc, int32_t* G,
+                        const int32_t* cur, const uint32_t* words, const int64_t* wrank, int32_t* labels,
+                        cudaStream_t s)
 {
+  const int64_t total = static_cast<int64_t>(c1 - c0) * n;
+  if (total <= 0) return Status::Ok();
   count_launch();
-  cc_labels_kernel<<<blocks_for(x1 - x0, 256), 256, 0, s>>>(n, k, l, x0, x1, cc, G, cur, rank, labels);
+  cc_labels_kernel<<<blocks_for(total, 256), 256, 0, s>>>(n, l, c0, c1, W, cc, G, cur, words, wrank, labels);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
