@@ -44,31 +44,6 @@ def config_range(c: int, rank: int, world: int) -> tuple[int, int]:
     return c * rank // world, c * (rank + 1) // world
 
 
-def balanced_config_ranges(cost: list[float], world: int) -> list[tuple[int, int]]:
-    """Contiguous ranges of the configs (in their eps-major order) with near-equal summed cost:
-    rank r ends its range at the first config where the prefix sum reaches (r + 1) / world of
-    the total, keeping every range non-empty while configs remain.  Deterministic, so every
-    rank computes the same split from the same (all-reduced) costs."""
-    c = len(cost)
-    if world <= 1 or c == 0:
-        return [(0, c)] + [(c, c)] * max(0, world - 1)
-    total = float(sum(cost)) or float(c)
-    w = [float(x) if sum(cost) else 1.0 for x in cost]
-    ranges, start, acc = [], 0, 0.0
-    for r in range(world):
-        if r == world - 1:
-            ranges.append((start, c))
-            break
-        target = total * (r + 1) / world
-        end = start
-        while end < c and (acc + w[end] <= target or end == start) and c - (end + 1) >= world - r - 1:
-            acc += w[end]
-            end += 1
-        ranges.append((start, end))
-        start = end
-    return ranges
-
-
 # Relative per-element costs of the labelling kernels, fitted to one-GPU C4 timings (0.92 ms of
 # slab walks over 4.25e6 entries, 1.27 ms of unions over 1.63e7 (entry, config) pairs, 0.35 ms
 # of relabel over 1.6e7 (point, config) pairs): the per-eps slab walks (compaction, touch,

@@ -214,22 +214,6 @@ def test_label_rows_gather_even_and_uneven_splits(tmp_path, C, world):
         assert np.array_equal(np.load(tmp_path / f"rows_{r}.npy"), want)
 
 
-def test_balanced_config_ranges_partition_and_balance():
-    rng = np.random.default_rng(3)
-    for C in (1, 2, 5, 16, 33):
-        for world in (1, 2, 3, 4, 8):
-            cost = list(rng.uniform(0, 10, C))
-            rs = parallel.balanced_config_ranges(cost, world)
-            assert len(rs) == world and rs[0][0] == 0 and rs[-1][1] == C
-            assert all(a[1] == b[0] and a[0] <= a[1] for a, b in zip(rs, rs[1:]))
-            if C >= world:
-                assert all(b > a for a, b in rs)  # nobody idle when there is enough work
-    # heavy configs at the end get ranges of their own
-    rs = parallel.balanced_config_ranges([1] * 12 + [100] * 4, 4)
-    assert rs[-1][1] - rs[-1][0] <= 2
-    assert parallel.balanced_config_ranges([1.0] * 16, 4) == [(0, 4), (4, 8), (8, 12), (12, 16)]
-
-
 def _brute_force_best(per_eps, l, n, world):
     import itertools
 
