@@ -149,3 +149,100 @@ def write_dataset(base: str | Path, points: np.ndarray, eps: Sequence[float], mi
     meta_path = base.with_name(base.name + ".json")
     meta_path.write_text(json.dumps(meta, indent=2, ensure_ascii=False), encoding="utf-8")
     return meta_path
+
+
+# ---- grid heuristics: which (eps, minPts) grid to run on a dataset ------------------------------
+# The reference's generator proposes a grid per dataset (tools/gerar_datasets.py:493-605); these
+# functions restate its rules so a grid can be chosen without it: minPts from an intrinsic
+# dimension estimate and log2(N), eps from quantiles of a sampled k-distance curve (the automated
+# form of the classic k-distance plot).  Same samples, same neighbour searches, same arithmetic,
+# so the same grid (pinned against outputs of the reference generator in tests/test_datasets.py).
+
+GRID_SEED = 42  # the generator's default seed: samples drawn with it select the same rows
+
+
+@dataclass
+class GridSuggestion:
+    eps: list[float]
+    min_samples: list[int]
+    min_samples_reference: int   # the minPts whose k-distance curve gave the eps values
+    intrinsic_dimension: float
+    sample_rank: int             # neighbour rank used in the sample (corrected for its size)
+
+
+def _sample_rows(n: int, max_points: int, seed: int) -> np.ndarray:
+    """Indices of a uniform sample without replacement (all rows when n <= max_points)."""
+    if n <= int(max_points):
+        return np.arange(n)
+    return np.random.default_rng(seed).choice(n, size=int(max_points), replace=False)
+
+
+def _neighbour_distances(x: np.ndarray, k: int) -> np.ndarray:
+    from sklearn.neighbors import NearestNeighbors
+
+    return NearestNeighbors(n_neighbors=int(k), algorithm="auto").fit(x).kneighbors(x)[0]
+
+
+def intrinsic_dimension(x, k: int = 20, sample_size: int = 5000, seed: int = GRID_SEED) -> float:
+    """Levina-Bickel maximum-likelihood estimate of the intrinsic dimension (median over a
+    sample of the per-point estimates from the k nearest neighbours), clipped to [1, 2D].
+    A curve or a ring in many dimensions comes out near 1, which is what minPts should follow."""
+    x = np.asarray(x, dtype=np.float32)
+    xs = np.ascontiguousarray(x[_sample_rows(x.shape[0], sample_size, seed)], dtype=np.float32)
+    kk = int(min(max(4, k), xs.shape[0] - 1))
+    if kk < 3:
+        return float(x.shape[1])
+    dist = _neighbour_distances(xs, kk + 1)[:, 1:]  # drop each point itself (distance 0)
+    tiny = 1e-12
+    inv = np.mean(np.log((dist[:, -1:] + tiny) / (dist[:, :-1] + tiny)), axis=1)
+    local = 1.0 / np.maximum(inv, tiny)
+    return float(np.clip(float(np.nanmedian(local)), 1.0, max(1.0, 2.0 * x.shape[1])))
+
+
+def suggest_min_samples(x, sample_size: int = 5000, max_min_samples: int = 256,
+                        seed: int = GRID_SEED) -> tuple[list[int], float]:
+    """minPts candidates {b/2, b, 2b, 4b} clipped to [4, max], with b = max(4, ceil(2 dim),
+    ceil(log2 N)); returns them ascending with the dimension estimate."""
+    x = np.asarray(x, dtype=np.float32)
+    dim = intrinsic_dimension(x, sample_size=sample_size, seed=seed)
+    base = max(4, int(np.ceil(2.0 * dim)), int(np.ceil(np.log2(max(x.shape[0], 2)))))
+    cands = sorted({int(np.clip(c, 4, max_min_samples)) for c in (base // 2, base, 2 * base, 4 * base)})
+    return cands, dim
+
+
+def suggest_eps(x, min_samples: int, quantiles=(0.50, 0.70, 0.85), max_points: int = 60000,
+                seed: int = GRID_SEED, labels=None) -> tuple[list[float], int]:
+    """eps candidates at `quantiles` of the k-distance curve of a sample of at most max_points
+    rows (k = min_samples, the point itself included).  A sample of s of N rows uses the rank
+    1 + round((min_samples - 1)(s - 1)/(N - 1)), the rank whose distance in the sample estimates
+    the full data's min_samples-th neighbour.  With true labels given, noise rows (label < 0)
+    stay in the neighbour index but their own k-distances are left out of the quantiles when
+    enough rows remain (the uniform noise tail would otherwise pull the largest eps far beyond
+    the clusters).  Returns the distinct float32 values ascending and the rank used."""
+    x = np.asarray(x, dtype=np.float32)
+    idx = _sample_rows(x.shape[0], max_points, seed)
+    xs = x[idx]
+    if x.shape[0] <= 1 or xs.shape[0] <= 1:
+        k = 1
+    else:
+        frac = (xs.shape[0] - 1) / (x.shape[0] - 1)
+        k = int(np.clip(1 + int(round(max(0, int(min_samples) - 1) * frac)), 2, xs.shape[0]))
+    kth = _neighbour_distances(xs, k)[:, -1]
+    if labels is not None:
+        structured = np.asarray(labels)[idx] >= 0
+        if structured.sum() >= max(50, 0.1 * kth.size):
+            kth = kth[structured]
+    kth = np.sort(kth)
+    eps = np.asarray([np.quantile(kth, q) for q in quantiles], dtype=np.float32)
+    eps = np.unique(np.maximum(eps, np.float32(1e-6))).astype(np.float32)
+    return [float(v) for v in eps], int(k)
+
+
+def suggest_grid(x, quantiles=(0.50, 0.70, 0.85), seed: int = GRID_SEED, labels=None) -> GridSuggestion:
+    """The full grid: the minPts candidates, and eps from the k-distance curve of the middle
+    candidate (3 x 4 = 12 configurations with the default quantiles)."""
+    ms, dim = suggest_min_samples(x, seed=seed)
+    ref = ms[len(ms) // 2]
+    eps, k = suggest_eps(x, ref, quantiles=quantiles, seed=seed, labels=labels)
+    return GridSuggestion(eps=eps, min_samples=ms, min_samples_reference=ref, intrinsic_dimension=dim,
+                          sample_rank=k)

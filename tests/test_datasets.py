@@ -86,3 +86,36 @@ def test_metadata_expectations(tmp_path):
                     ({"eps_quantiles": (0.5, 0.85)}, "quantiles")):
         with pytest.raises(datasets.DatasetError, match=msg):
             datasets.load_dataset(meta, **kw)
+
+
+def _grid_cases():
+    import importlib.util
+    import json
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parent / "golden"
+    spec = importlib.util.spec_from_file_location("grid_fixtures", here / "make_grid_fixtures.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    data = json.loads((here / "grid_heuristics.json").read_text())
+    return mod.grid_case_points, data
+
+
+def test_grid_heuristics_match_the_reference_generator():
+    """Each case's points are regenerated from its seed; minPts candidates, the intrinsic
+    dimension, the sampled neighbour rank and the eps values (with and without the true labels)
+    must equal what the reference generator's heuristics returned for them."""
+    from dbscan_multi import datasets as ds
+
+    make, data = _grid_cases()
+    assert data["seed"] == ds.GRID_SEED
+    for case in data["cases"]:
+        x, y = make(case["n"], case["d"], case["centres"], case["std"], case["noise"], case["seed"])
+        g = ds.suggest_grid(x, labels=y)
+        assert g.min_samples == case["min_samples"], case["name"]
+        assert g.min_samples_reference == case["min_samples_reference"]
+        assert g.intrinsic_dimension == case["intrinsic_dimension"]
+        assert g.sample_rank == case["sample_rank"]
+        assert g.eps == case["eps"], case["name"]
+        eps_plain, _ = ds.suggest_eps(x, case["min_samples_reference"])
+        assert eps_plain == case["eps_without_labels"], case["name"]
