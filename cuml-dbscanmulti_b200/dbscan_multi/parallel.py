@@ -44,14 +44,17 @@ def config_range(c: int, rank: int, world: int) -> tuple[int, int]:
     return c * rank // world, c * (rank + 1) // world
 
 
-# Relative per-element costs of the labelling kernels, fitted to one-GPU C4 timings (0.92 ms of
-# slab walks over 4.25e6 entries, 1.27 ms of unions over 1.63e7 (entry, config) pairs, 0.35 ms
-# of relabel over 1.6e7 (point, config) pairs): the per-eps slab walks (compaction, touch,
-# border candidates, border fold) per entry of an eps the rank owns any config of, the union
-# per (entry, owned config), the relabel per (point, owned config).
+# Relative per-element costs of the labelling kernels, fitted to C4 timings on one and two GPUs
+# (per rank: one walk of the eps = 4.5 slab ~0.83 ms for 3.86e6 entries, each further config's
+# union ~0.19 ms, the per-batch compaction of the smaller-eps slabs ~0.7 ms, relabel ~0.014 ms per
+# config and 1e6 points): the slab walks per entry of an eps the rank owns any config of; the
+# compaction per max-eps entry, paid once by a rank that owns any config of a smaller eps (it
+# reads every max-eps entry of every batch); the union per (entry, owned config); the relabel per
+# (point, owned config).
 LABEL_COST_WALK = 22.0
-LABEL_COST_UNION = 7.8
-LABEL_COST_RELABEL = 2.2
+LABEL_COST_COMPACT = 18.0
+LABEL_COST_UNION = 4.9
+LABEL_COST_RELABEL = 1.4
 
 
 def labelling_cost(per_eps: list[float], l: int, n: int, a: int, b: int) -> float:
@@ -60,15 +63,18 @@ def labelling_cost(per_eps: list[float], l: int, n: int, a: int, b: int) -> floa
         return 0.0
     e0, e1 = a // l, (b - 1) // l
     walk = sum(per_eps[e0:e1 + 1])
+    compact = per_eps[-1] if e0 < len(per_eps) - 1 else 0.0
     union = sum(per_eps[c // l] for c in range(a, b))
-    return LABEL_COST_WALK * walk + LABEL_COST_UNION * union + LABEL_COST_RELABEL * n * (b - a)
+    return (LABEL_COST_WALK * walk + LABEL_COST_COMPACT * compact + LABEL_COST_UNION * union
+            + LABEL_COST_RELABEL * n * (b - a))
 
 
 def labelling_ranges(per_eps: list[float], l: int, n: int, world: int) -> list[tuple[int, int]]:
     """Contiguous config ranges, one per rank, minimising the largest modelled labelling cost
     (bisection on the bound with a greedy feasibility sweep; the cost of a range only grows as
-    it widens).  A rank's cost counts each eps it touches once for the slab walks, so the split
-    prefers to keep an eps's configs together.  Deterministic: every rank computes the same
+    it widens).  A rank's cost counts each eps it touches once for the slab walks and the
+    compaction once if it owns any smaller-eps config, so the split prefers to keep an eps's
+    configs together and the largest eps's configs apart from the rest.  Deterministic: every rank computes the same
     split from the same (all-reduced) entry counts."""
     c = len(per_eps) * l
     if world <= 1 or c == 0:
