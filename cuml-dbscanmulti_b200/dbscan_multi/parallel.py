@@ -57,16 +57,30 @@ LABEL_COST_UNION = 4.9
 LABEL_COST_RELABEL = 1.4
 
 
+class _LabelCost:
+    """The labelling cost model with prefix sums, so the cost of any config range is O(1)."""
+
+    def __init__(self, per_eps: list[float], l: int, n: int):
+        self.l, self.n, self.k = int(l), int(n), len(per_eps)
+        self.last = float(per_eps[-1]) if per_eps else 0.0
+        self.eps_pre = np.concatenate([[0.0], np.cumsum(np.asarray(per_eps, dtype=np.float64))])
+        per_cfg = np.repeat(np.asarray(per_eps, dtype=np.float64), self.l)
+        self.cfg_pre = np.concatenate([[0.0], np.cumsum(per_cfg)])
+
+    def __call__(self, a: int, b: int) -> float:
+        if b <= a:
+            return 0.0
+        e0, e1 = a // self.l, (b - 1) // self.l
+        walk = self.eps_pre[e1 + 1] - self.eps_pre[e0]
+        compact = self.last if e0 < self.k - 1 else 0.0
+        union = self.cfg_pre[b] - self.cfg_pre[a]
+        return float(LABEL_COST_WALK * walk + LABEL_COST_COMPACT * compact + LABEL_COST_UNION * union
+                     + LABEL_COST_RELABEL * self.n * (b - a))
+
+
 def labelling_cost(per_eps: list[float], l: int, n: int, a: int, b: int) -> float:
     """Model cost of labelling the configs [a, b) (eps-major, l per eps)."""
-    if b <= a:
-        return 0.0
-    e0, e1 = a // l, (b - 1) // l
-    walk = sum(per_eps[e0:e1 + 1])
-    compact = per_eps[-1] if e0 < len(per_eps) - 1 else 0.0
-    union = sum(per_eps[c // l] for c in range(a, b))
-    return (LABEL_COST_WALK * walk + LABEL_COST_COMPACT * compact + LABEL_COST_UNION * union
-            + LABEL_COST_RELABEL * n * (b - a))
+    return _LabelCost(per_eps, l, n)(a, b)
 
 
 def labelling_ranges(per_eps: list[float], l: int, n: int, world: int) -> list[tuple[int, int]]:
@@ -74,14 +88,12 @@ def labelling_ranges(per_eps: list[float], l: int, n: int, world: int) -> list[t
     (bisection on the bound with a greedy feasibility sweep; the cost of a range only grows as
     it widens).  A rank's cost counts each eps it touches once for the slab walks and the
     compaction once if it owns any smaller-eps config, so the split prefers to keep an eps's
-    configs together and the largest eps's configs apart from the rest.  Deterministic: every rank computes the same
-    split from the same (all-reduced) entry counts."""
+    configs together and the largest eps's configs apart from the rest.  Deterministic: every
+    rank computes the same split from the same (all-reduced) entry counts."""
     c = len(per_eps) * l
     if world <= 1 or c == 0:
         return [(0, c)] + [(c, c)] * max(0, world - 1)
-
-    def cost(a, b):
-        return labelling_cost(per_eps, l, n, a, b)
+    cost = _LabelCost(per_eps, l, n)
 
     def sweep(bound):
         out, a = [], 0
@@ -91,13 +103,16 @@ def labelling_ranges(per_eps: list[float], l: int, n: int, world: int) -> list[t
                 b += 1
             out.append((a, b))
             a = b
+            if len(out) > world:  # infeasible already
+                break
         return out
 
     lo = max(cost(i, i + 1) for i in range(c))
     hi = cost(0, c)
     for _ in range(60):
         mid = 0.5 * (lo + hi)
-        if len(sweep(mid)) <= world:
+        r = sweep(mid)
+        if len(r) <= world and r[-1][1] == c:
             hi = mid
         else:
             lo = mid
