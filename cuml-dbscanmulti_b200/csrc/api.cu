@@ -73,7 +73,7 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int k, int l, int cfg_begin,
                        int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
                        unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
-                       cudaStream_t s);
+                       int union_limit, cudaStream_t s);
 Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0, int64_t rows, int32_t* counts,
                               cudaStream_t s);
 Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int ne,
@@ -217,6 +217,7 @@ struct dbm_handle {
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
   dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_scratch, work, fallback;
   int distance_mode = DBM_DISTANCE_AUTO;
+  int union_limit = dbm::kUnionRetryLimit;  // test knob (dbm_set_union_retry_limit)
   dbm::Buffer xdev, labels_dev, core_dev;  // host-buffer entry point only
   int64_t* pinned = nullptr;               // small D2H staging
   size_t pinned_count = 0;
@@ -722,7 +723,7 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
       }
       DBM_TRY(launch_cc_batch(ms, count, n, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc), nb == 1,
                               as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
-                              as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, s));
+                              as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, h->union_limit, s));
       base += count;
     }
   }
@@ -865,6 +866,13 @@ int dbm_core_sample_indices(dbm_handle* h, const uint8_t* core_dev, int64_t n, i
   }
   dbm::set_err(err, err_len, r.msg);
   return r.code;
+}
+
+int dbm_set_union_retry_limit(dbm_handle* h, int limit)
+{
+  if (!h || limit < 0) return DBM_ERR_INVALID;
+  h->union_limit = limit == 0 ? 0 : std::min(limit, dbm::kUnionRetryLimit);
+  return DBM_OK;
 }
 
 int dbm_set_distance_mode(dbm_handle* h, int mode)

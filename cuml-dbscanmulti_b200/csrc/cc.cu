@@ -51,6 +51,7 @@ struct CcArgs {
   const int32_t* cc;  // k x n: core iff m < cc[e*n + i]
   int sample_shift = 0;  // union over every 2^s-th entry only (0: all entries)
   bool quick = false;    // union: skip a union-find whose two endpoints already share a parent
+  int union_limit = kUnionRetryLimit;  // retry bound of each uf_unite (lowered only by a test knob)
 };
 
 __device__ __forceinline__ void cfg_range(const CcArgs& a, int e, int& m_lo, int& m_hi)
@@ -165,8 +166,8 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
     if (skip_p && skip_q) return;
     const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
     if (m >= cc[r] || m >= cc[j]) return;
-    if (!skip_p) ok &= uf_unite(P + base, r, j);
-    if (!skip_q) ok &= uf_unite(Q + base, r, j);
+    if (!skip_p) ok &= uf_unite(P + base, r, j, a.union_limit);
+    if (!skip_q) ok &= uf_unite(Q + base, r, j, a.union_limit);
   });
   if (!ok) atomicOr(err, kErrUnionLimit);
 }
@@ -307,11 +308,12 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int k, int l, int cfg_begin,
                        int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
                        unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
-                       cudaStream_t s)
+                       int union_limit, cudaStream_t s)
 {
   if (upper_entries <= 0 || cfg_begin >= cfg_end) return Status::Ok();
   CcArgs a{ms, n, k, l, cfg_begin, cfg_end, cc};
   a.quick = true;
+  a.union_limit = union_limit;
   const unsigned nb = static_cast<unsigned>(
     std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries, 256), static_cast<int64_t>(sm_count) * 16)));
   const unsigned nbu = static_cast<unsigned>(

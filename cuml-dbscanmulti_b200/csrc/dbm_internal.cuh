@@ -120,10 +120,14 @@ __device__ __forceinline__ int32_t uf_find(int32_t* parent, int32_t x)
   return x;
 }
 
+// Retry bound of uf_unite: a hook can lose its CAS to a concurrent hook at most once per root
+// change, so the bound is never reached in practice; it exists so that no loop can spin forever.
+constexpr int kUnionRetryLimit = 1 << 20;
+
 // Returns false if the retry bound ran out (never expected; reported as an error flag).
-__device__ __forceinline__ bool uf_unite(int32_t* parent, int32_t a, int32_t b)
+__device__ __forceinline__ bool uf_unite(int32_t* parent, int32_t a, int32_t b, int limit = kUnionRetryLimit)
 {
-  for (int it = 0; it < (1 << 20); ++it) {
+  for (int it = 0; it < limit; ++it) {
     a = uf_find(parent, a);
     b = uf_find(parent, b);
     if (a == b) return true;

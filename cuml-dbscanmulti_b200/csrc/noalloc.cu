@@ -1,19 +1,24 @@
 // noalloc.cu -- per-eps neighbour counts without any device allocation.
 //
-// Some callers cannot call cudaMalloc: code that runs while a stream is being captured into
-// a CUDA graph, code living under an allocator that owns all of the device's memory (a
-// framework's caching allocator, a hard memory budget), and latency-critical callers that
-// cannot afford the implicit device-wide synchronisation of cudaMalloc/cudaFree.  For them,
-// dbm_neighbor_counts_noalloc computes the same per-eps degrees as dbm_neighbor_counts but
-// takes every byte of scratch from one file-scope device array of fixed size, so the call
-// allocates nothing.  The caller still passes the points and the output buffer.
+// Some callers cannot call cudaMalloc: code living under an allocator that owns all of the
+// device's memory (a framework's caching allocator, a hard memory budget), and latency-critical
+// callers that cannot afford the implicit device-wide synchronisation of cudaMalloc/cudaFree.
+// For them, dbm_neighbor_counts_noalloc computes the same per-eps degrees as
+// dbm_neighbor_counts but takes every byte of scratch from one file-scope device array of fixed
+// size, so the call allocates nothing.  The caller still passes the points and the output
+// buffer.
 //
 // The array (kNoAllocScratchBytes, 32 MiB) is part of the library image: every GPU on which
 // the library is used keeps it until the process exits.  Its device address is looked up
-// once per device, on the first call made with that device current; make that first call
-// before starting any stream capture.  All calls share the array and it keeps the previous
-// call's contents, so the parts that must start at zero are cleared on every call, and two
-// calls that overlap on the GPU (different streams or threads) race on it.
+// once per device, on the first call made with that device current.  All calls share the
+// array and it keeps the previous call's contents, so the parts that must start at zero are
+// cleared on every call, and two calls that overlap on the GPU (different streams or threads)
+// race on it.  The call ends by reading its status word back to the host and synchronising the
+// stream.
+//
+// Cost: the exact tile kernel over every tile pair (O(N^2 D)); the spatial order, tile-pair
+// pruning and tensor-core screen of dbm_neighbor_counts need buffers sized by N and by the
+// surviving tile pairs, which this entry point does not have.
 #include "dbm_internal.cuh"
 
 #include <algorithm>

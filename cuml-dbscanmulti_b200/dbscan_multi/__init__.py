@@ -58,6 +58,7 @@ EXPORTED = (
     "dbm_fit_multi", "dbm_fit_multi_host", "dbm_neighbor_counts", "dbm_batch_size", "dbm_max_bytes_for_batch_size",
     "dbm_annotate_pays", "dbm_auto_index_bits", "dbm_build_info_json",
     "dbm_neighbor_counts_noalloc", "dbm_distance_shard", "dbm_fit_multi_from_graph",
+    "dbm_set_union_retry_limit",
 )
 
 
@@ -134,6 +135,8 @@ def load_library():
     lib.dbm_set_phase_timing.restype = None
     lib.dbm_set_distance_mode.argtypes = [p, i32]
     lib.dbm_set_distance_mode.restype = i32
+    lib.dbm_set_union_retry_limit.argtypes = [p, i32]
+    lib.dbm_set_union_retry_limit.restype = i32
     lib.dbm_core_sample_indices.argtypes = [p, p, i64, i32, p, p, cp, sz]
     lib.dbm_core_sample_indices.restype = i32
     fit_args = [p, p, i64, i64, p, i32, p, i32, p, p, ctypes.POINTER(Options), ctypes.POINTER(Stats),
@@ -277,6 +280,13 @@ class DbscanMulti:
         rc = self._lib.dbm_set_distance_mode(self._h, DISTANCE_MODES[mode])
         if rc != DBM_OK:
             raise DbmError(rc, f"bad distance mode {mode!r}")
+
+    def set_union_retry_limit(self, limit: int) -> None:
+        """Test knob: the retry bound of every union-find hook (default 2**20; 0 makes the
+        labelling give up with DBM_ERR_NOT_CONVERGED).  The handle stays usable."""
+        rc = self._lib.dbm_set_union_retry_limit(self._h, int(limit))
+        if rc != DBM_OK:
+            raise DbmError(rc, f"bad union retry limit {limit!r}")
 
     def _options(self, backend, index, route, neigh_per_row, max_bytes_per_batch, csr_cap_bytes):
         if backend not in BACKENDS:

@@ -135,6 +135,13 @@ void dbm_set_phase_timing(dbm_handle* h, int enabled);
 #define DBM_DISTANCE_SCREENED 2
 int dbm_set_distance_mode(dbm_handle* h, int mode);
 
+/* Test knob (fault injection without a GPU fault, like the reference's thread-local test knobs
+ * csr_teto_de_teste / rota_forcada, runner_multi.cuh:145-160, 426-430): the retry bound of every
+ * union-find hook in the labelling kernels (default 2^20, the largest accepted).  0 makes every
+ * hook that is not already a no-op give up at once, so the fit returns DBM_ERR_NOT_CONVERGED
+ * ("union-find retry bound ran out") and the handle stays usable.  DBM_ERR_INVALID for limit < 0. */
+int dbm_set_union_retry_limit(dbm_handle* h, int limit);
+
 /* ---- the fit ------------------------------------------------------------------------ */
 /*
  * x_dev:        n x d float32, row-major, device
@@ -210,17 +217,21 @@ int dbm_neighbor_counts(dbm_handle* h, const float* x_dev, int64_t n, int64_t d,
                         size_t err_len);
 
 /* Allocation-free per-eps neighbourhood sizes.  No counterpart in the reference: it exists for
- * callers that cannot call cudaMalloc -- code running while a stream is captured into a CUDA
- * graph, code under an allocator that owns all device memory, latency-critical code that
- * cannot take cudaMalloc's device-wide synchronisation.  Same output as dbm_neighbor_counts
- * (deg_dev[e*n + i], int32, device), but every byte of scratch comes from one file-scope device
- * array of 32 MiB (the padded dim-major copy of the points, 4*Dp*Npad bytes with Dp = d rounded
- * up to 4 and Npad = n rounded up to 4, plus 4*k*n bytes of counts and 768 bytes of counters);
- * larger inputs are rejected with DBM_ERR_TOO_LARGE.  The array is resident on every GPU that
- * uses the library until the process exits.  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress) with that device current: make it before any stream
- * capture.  Calls share the array, so calls that overlap on the GPU race; each call clears the
- * parts that must start at zero.  No handle is needed; stream NULL = the legacy default stream. */
+ * callers that cannot call cudaMalloc -- code under an allocator that owns all of the device's
+ * memory (a framework's caching allocator, a hard per-process budget), or latency-critical code
+ * that cannot take the device-wide synchronisation cudaMalloc/cudaFree imply.  Same output as
+ * dbm_neighbor_counts (deg_dev[e*n + i], int32, device), but every byte of scratch comes from
+ * one file-scope device array of 32 MiB (the padded dim-major copy of the points, 4*Dp*Npad
+ * bytes with Dp = d rounded up to 4 and Npad = n rounded up to 4, plus 4*k*n bytes of counts and
+ * 768 bytes of counters); larger inputs are rejected with DBM_ERR_TOO_LARGE.  The array is
+ * resident on every GPU that uses the library until the process exits.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with that device current.
+ * Calls share the array, so calls that overlap on the GPU race; each call clears the parts that
+ * must start at zero.  Cost: the exact tile kernel over every 128 x 128 tile pair, O(N^2 D),
+ * without the spatial order, pruning or tensor-core screen of dbm_neighbor_counts (which needs
+ * allocated buffers for them), so it can be orders of magnitude slower on large sparse inputs.
+ * The call synchronises `stream` and reads a status word back to the host before it returns.
+ * No handle is needed; stream NULL = the legacy default stream. */
 int dbm_neighbor_counts_noalloc(const float* x_dev, int64_t n, int64_t d, const float* eps_host,
                                 int k, int32_t* deg_dev, void* stream, char* err, size_t err_len);
 

@@ -5,6 +5,7 @@
 from __future__ import annotations
 
 import json
+import os
 import re
 import subprocess
 import sys
@@ -16,7 +17,13 @@ import pytest
 ROOT = Path(__file__).resolve().parents[1]
 CLI = ROOT / "cuml-dbscanmulti_b200" / "bin" / "dbscan_multi"
 GOLDEN = ROOT / "tests" / "golden"
-REFERENCE_TOOLS = Path("/root/reference/tools")
+# The reference checkout, when mounted (its tools/ hold the JSON contract validator); the
+# checks that need it skip when DBM_REFERENCE_ROOT is unset.
+REFERENCE_ROOT = os.environ.get("DBM_REFERENCE_ROOT", "")
+REFERENCE_TOOLS = Path(REFERENCE_ROOT) / "tools" if REFERENCE_ROOT else None
+# Optional directory where the GPU tests also leave their recorded CLI outputs (JSON lines and
+# label files) for tests/golden/ fixtures; unset = tmp_path only.
+RECORD_DIR = os.environ.get("DBM_RECORD_DIR", "")
 
 
 def run(*args, check=False):
@@ -96,7 +103,7 @@ def validate_contract(meta, backend, n, d, eps, min_samples, index, route):
 
 def validate_with_reference_tool(meta, **kw):
     """When the reference's tools are mounted, also run its own validator on the JSON."""
-    if not (REFERENCE_TOOLS / "bench_vs_cuml.py").exists():
+    if REFERENCE_TOOLS is None or not (REFERENCE_TOOLS / "bench_vs_cuml.py").exists():
         return
     sys.path.insert(0, str(REFERENCE_TOOLS))
     try:
@@ -149,6 +156,7 @@ def test_cli_golden_bundles_every_mode(tmp_path, name):
     pts_path = tmp_path / "p.f32"
     pts.tofile(pts_path)
     runs = []
+    recorded = {}
     modes = MODES if name in FULL_MODE_CASES else [MODES[0], MODES[7]]
     for mode in modes:
         out = tmp_path / "l.i32"
@@ -167,13 +175,27 @@ def test_cli_golden_bundles_every_mode(tmp_path, name):
         validate_contract(meta, mode["backend"], pts.shape[0], pts.shape[1], eps, ms, mode["index"], mode["route"])
         labels = np.fromfile(out, np.int32).reshape(len(eps) * len(ms), pts.shape[0])
         assert np.array_equal(labels, z["labels"]), mode
+        recorded[mode_name(mode)] = labels
         runs.append({"request": dict(backend=mode["backend"], n=int(pts.shape[0]), d=int(pts.shape[1]),
                                      eps=eps, min_samples=ms, index=mode["index"], route=mode["route"]),
                      "json": meta})
+    # the label files each mode wrote, kept for the reference's own validation gate
+    # (tests/test_validation_gate.py) and, for one case, the JSON lines for its contract validator
+    np.savez_compressed(tmp_path / f"{name}.cli_labels.npz", **recorded)
     if name == "010_random_seed_000":
-        rec_dir = ROOT / "gpurun_out"
-        rec_dir.mkdir(exist_ok=True)
-        (rec_dir / "cli_run.json").write_text(json.dumps({"runs": runs}, indent=1))
+        (tmp_path / "cli_run.json").write_text(json.dumps({"runs": runs}, indent=1))
+    if RECORD_DIR:
+        dst = Path(RECORD_DIR)
+        dst.mkdir(parents=True, exist_ok=True)
+        for f in tmp_path.glob("*.json*"):
+            (dst / f.name).write_bytes(f.read_bytes())
+        (dst / f"{name}.cli_labels.npz").write_bytes((tmp_path / f"{name}.cli_labels.npz").read_bytes())
+
+
+def mode_name(mode):
+    """Name of a CLI mode, as the reference's validation matrix spells its sources."""
+    base = f"{mode['backend']}_{mode['route']}_{mode['index']}"
+    return base + ("_batched" if mode.get("max_mbytes") else "")
 
 
 @pytest.mark.gpu

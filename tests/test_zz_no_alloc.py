@@ -1,8 +1,8 @@
 """The allocation-free entry point, dbm_neighbor_counts_noalloc, against dbm_neighbor_counts.
 
-Callers that cannot call cudaMalloc (inside a stream capture, under an allocator that owns
-the device, or on a latency-critical path) use dbm_neighbor_counts_noalloc, whose scratch is a
-fixed 32 MiB device array inside the library.  This file is collected last on purpose.  It
+Callers that cannot call cudaMalloc (under an allocator that owns all of the device's memory,
+or on a path that cannot take cudaMalloc's device-wide synchronisation) use
+dbm_neighbor_counts_noalloc, whose scratch is a fixed 32 MiB device array inside the library.  This file is collected last on purpose.  It
 calls the new entry point through the C ABI twice in a row on the same inputs and requires
 both outputs to equal the allocating entry point's degrees exactly (integer counts, so the
 tolerance is zero), then checks that an input too large for the static scratch is refused.
