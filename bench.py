@@ -12,10 +12,15 @@ eps {3.0,3.5,4.0,4.5} x minPts {5,10,20,40}, a 128 GB budget with neigh_per_row=
 (8 batches of 127,8xx rows).  Seeded synthetic data with the shapes of the published
 configuration.
 
-Metric: pair-distances per second = N^2 ordered pairs per grid / grid wall time (the
-reference's unit; each distance evaluated here covers two ordered pairs).  `value` times
-device-resident input with CUDA events; `e2e` times the host-buffer C-ABI entry point with
-the point copy in and the label copy out inside the timed region.
+Metric: the k x l grid wall time (`grid_wall_s`, seconds per grid), and as `value` the
+effective pair-distances per second = N^2 ordered pairs per grid / grid wall time (the
+reference's unit; pairs ruled out by the exact tile bound or the tensor-core screen are resolved
+without an fp32 distance evaluation, so this is a rate of pairs resolved, not of distances
+computed).  `value` times device-resident input with CUDA events; `e2e` times the host-buffer
+C-ABI entry point with the point copy in and the label copy out inside the timed region.
+Before timing, the labels are checked against the oracle's digests of the workload and, on
+several GPUs, against a one-GPU fit (`labels_match_oracle`, `labels_match_1gpu`; a mismatch
+fails the run).
 
 Multi-GPU (torchrun, one process per GPU): the same grid, sharded -- each rank evaluates an
 equal share of the distance tile pairs, histograms are all-reduced and neighbour pairs
@@ -42,13 +47,13 @@ for _p in (ROOT / "cuml-dbscanmulti_b200", ROOT / "oracle"):
 
 CONFIGS = {
     "c1": dict(n=10_000, d=2, centers=8, box=10.0, std=(0.5, 0.5), noise=0.05, zero_cols=0,
-               eps=[0.2, 0.3, 0.5], min_samples=[5, 10, 20], budget=None, npr=0,
+               eps=[0.2, 0.3, 0.5], min_samples=[5, 10, 20], budget=128 * 10**9, npr=0,
                desc="Gaussian blobs N=10,000 D=2, 8 centres U[-10,10]^2, std 0.5, 5% noise; 3x3 grid"),
     "c2": dict(n=100_000, d=8, centers=20, box=10.0, std=(0.5, 1.0), noise=0.05, zero_cols=0,
-               eps=[0.4, 0.6, 0.8, 1.0, 1.2], min_samples=[10], budget=None, npr=0,
+               eps=[0.4, 0.6, 0.8, 1.0, 1.2], min_samples=[10], budget=128 * 10**9, npr=0,
                desc="Multi-EPS N=100,000 D=8, 20 centres U[-10,10]^8, std U[0.5,1.0], 5% noise; k=5, l=1"),
     "c3": dict(n=500_000, d=32, centers=50, box=20.0, std=(1.0, 1.0), noise=0.10, zero_cols=0,
-               eps=[4.0], min_samples=[5, 10, 20, 40, 80], budget=None, npr=0,
+               eps=[4.0], min_samples=[5, 10, 20, 40, 80], budget=128 * 10**9, npr=0,
                desc="Multi-minPts N=500,000 D=32, 50 centres U[-20,20]^32, std 1.0, 10% noise; k=1, l=5"),
     "c4": dict(n=1_000_000, d=33, centers=100, box=20.0, std=(0.8, 1.5), noise=0.05, zero_cols=1,
                eps=[3.0, 3.5, 4.0, 4.5], min_samples=[5, 10, 20, 40], budget=128 * 10**9, npr=64,
@@ -56,13 +61,13 @@ CONFIGS = {
                     "U[-20,20]^32, std U[0.8,1.5], 5% noise; 4x4 grid; 128 GB budget, "
                     "neigh_per_row 64 -> 8 batches"),
     "c5": dict(n=200_000, d=64, centers=10, box=5.0, std=(2.0, 2.0), noise=0.0, zero_cols=0,
-               eps=[6.0, 9.0, 12.0], min_samples=[10, 50, 200], budget=None, npr=0,
+               eps=[6.0, 9.0, 12.0], min_samples=[10, 50, 200], budget=128 * 10**9, npr=0,
                desc="Dense-route stress as written: N=200,000 D=64, 10 centres U[-5,5]^64, std 2.0, "
                     "no noise; 3x3 grid"),
     # the same points with eps at sampled pair-distance quantiles, so that the largest eps links
     # about 20% of all pairs (the dense regime the stress case is meant to exercise)
     "c5q": dict(n=200_000, d=64, centers=10, box=5.0, std=(2.0, 2.0), noise=0.0, zero_cols=0,
-                eps=None, eps_quantiles=(0.05, 0.10, 0.20), min_samples=[10, 50, 200], budget=None,
+                eps=None, eps_quantiles=(0.05, 0.10, 0.20), min_samples=[10, 50, 200], budget=128 * 10**9,
                 npr=0,
                 desc="Dense-route stress, calibrated: the C5 points with eps at the 5/10/20% quantiles "
                      "of 200,000 sampled pair distances; 3x3 grid"),
@@ -215,30 +220,88 @@ def sgemm_fp32_peak(torch, dev) -> float:
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-def cpu_baseline(pts: np.ndarray, eps, target_s: float = 12.0) -> dict:
-    """The oracle's fp32 distance/degree loop (the CPU restatement of the path) on a bounded
-    sample of query rows against all N points, every host core."""
+def index_bits(n: int) -> int:
+    """The reference CLI's --index auto: int64 iff N*N >= INT32_MAX (src/main.cu:681-689)."""
+    return 64 if n * n >= 2**31 - 1 else 32
+
+
+def cpu_pipeline(pts: np.ndarray, eps, ms, budget: int, npr: int, target_s: float = 12.0) -> dict:
+    """The CPU restatement of the whole path (oracle.fit_multi_stream: per-eps degrees, per-batch
+    neighbour lists, weak-CC + merge of every configuration, relabel), on every host core, over
+    the first N' points of the workload, N' sized so that one run takes about `target_s`.  The
+    grid time extrapolates to N as (N / N')^2: the two distance passes, O(N^2), are nearly all
+    of it (the labelling is linear in the graph)."""
+    import batching
     import oracle
 
     threads = oracle.default_threads()
-    n = len(pts)
-    # calibrate on a probe long enough (>= 0.5 s) that thread start-up does not skew the rate
-    rows, dt = 32, 0.0
-    while True:
+    n, k, l = len(pts), len(eps), len(ms)
+
+    def run(m):
+        bs = batching.compute_batch_size(m, k, l, budget, use_cuvs=True, neigh_hint=npr, index_bits=index_bits(m))
         t0 = time.perf_counter()
-        oracle.codes_degrees(pts, eps, row0=0, rows=rows, want_codes=False, threads=threads)
-        dt = time.perf_counter() - t0
-        if dt >= 0.5 or rows >= n:
-            break
-        rows = min(n, rows * 4)
-    rows2 = int(min(n, max(rows, rows * target_s / max(dt, 1e-6))))
-    t0 = time.perf_counter()
-    oracle.codes_degrees(pts, eps, row0=0, rows=rows2, want_codes=False, threads=threads)
-    dt = time.perf_counter() - t0
-    return {"value": rows2 * n / dt, "unit": "pair-distances/s", "cores": threads, "kind": "port",
-            "sample": f"{rows2} query rows x all {n} points (codes + per-eps degrees), "
-                      f"{dt:.1f} s; grid wall time extrapolates as N^2 / value",
+        oracle.fit_multi_stream(pts[:m], eps, ms, bs, threads)
+        return time.perf_counter() - t0, bs
+
+    m = min(n, 4096)
+    dt, bs = run(m)
+    while dt < target_s / 8 and m < n:
+        m = min(n, m * 2)
+        dt, bs = run(m)
+    m2 = min(n, int(m * (target_s / max(dt, 1e-6)) ** 0.5))
+    if m2 > m * 1.2:
+        m = m2
+        dt, bs = run(m)
+    grid_s = dt * (n / m) ** 2
+    return {"value": float(n) * n / grid_s, "unit": "pairs/s", "grid_wall_s": grid_s, "cores": threads,
+            "kind": "port",
+            "sample": f"oracle.fit_multi_stream (distance passes + per-batch lists + weak-CC/merge of all "
+                      f"{k * l} configurations + relabel) on the first {m} of {n} points ({dt:.1f} s, "
+                      f"batch size {bs}); grid time extrapolated by (N/{m})^2",
             "seconds": dt}
+
+
+def dv_baseline(pts: np.ndarray, eps, ms, target_s: float = 10.0) -> dict:
+    """The reference's own CPU validation DBSCAN (tools/dbscan_validation.py: build_epsilon_graph
+    per eps + structure per minPts, dense float64) when the reference's tools are importable (a
+    checkout named by DBM_REFERENCE_ROOT, or an install under baseline/_ref), on the first N''
+    points, extrapolated by (N/N'')^2 (its dense N x N graph makes the full size infeasible)."""
+    roots = [os.environ.get("DBM_REFERENCE_ROOT", ""), str(ROOT / "baseline" / "_ref")]
+    dv = None
+    for r in roots:
+        if r and (Path(r) / "tools" / "dbscan_validation.py").exists():
+            sys.path.insert(0, str(Path(r) / "tools"))
+            try:
+                import dbscan_validation as dv  # noqa: F401
+            except Exception:
+                dv = None
+            finally:
+                sys.path.pop(0)
+            break
+    if dv is None:
+        return {"unavailable": "the reference's tools/dbscan_validation.py is not installed here: the reference "
+                               "has no setup.py or pyproject.toml, so its offline pip install fails, and its "
+                               "checkout is not present on this machine"}
+    n = len(pts)
+
+    def run(m):
+        t0 = time.perf_counter()
+        for e in eps:
+            g = dv.build_epsilon_graph(pts[:m].astype(np.float64), float(e), max_n=m)
+            for v in ms:
+                g.structure(int(v))
+        return time.perf_counter() - t0
+
+    m = min(n, 1024)
+    dt = run(m)
+    while dt < target_s / 4 and m < n:
+        m = min(n, m * 2)
+        dt = run(m)
+    grid_s = dt * (n / m) ** 2
+    return {"value": float(n) * n / grid_s, "unit": "pairs/s", "grid_wall_s": grid_s,
+            "cores": os.cpu_count(), "kind": "reference (tools/dbscan_validation.py)",
+            "sample": f"build_epsilon_graph x {len(eps)} eps + structure x {len(ms)} minPts on the first {m} of {n} "
+                      f"points ({dt:.1f} s); grid time extrapolated by (N/{m})^2"}
 
 
 def dist_env():
@@ -295,32 +358,40 @@ def e2e_leg_sharded(one_fit, x, pts, labels, flush, steps, rank, dev, torch, dis
 
 
 def run_reference(args, cfg) -> None:
+    """The reference arm: the CPU restatement of the whole path on the host cores, same metric."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
     pts = make_points(cfg)
     cfg["eps"] = workload_eps(cfg, pts)
+    ms = cfg["min_samples"]
     cb = None
-    values = []
+    values, grids = [], []
+    per_step = args.cpu_seconds / max(1, args.steps)
     for _ in range(args.warmup):
-        cpu_baseline(pts, cfg["eps"], target_s=2.0)
+        cpu_pipeline(pts, cfg["eps"], ms, cfg["budget"], cfg["npr"], target_s=min(2.0, per_step))
     for _ in range(args.steps):
-        cb = cpu_baseline(pts, cfg["eps"], target_s=args.cpu_seconds / max(1, args.steps))
+        cb = cpu_pipeline(pts, cfg["eps"], ms, cfg["budget"], cfg["npr"], target_s=per_step)
         values.append(cb["value"])
+        grids.append(cb["grid_wall_s"])
     value = float(np.median(values))
+    grid_s = float(np.median(grids))
     n = cfg["n"]
     out = {
-        "impl": "reference", "metric": "pair_distances_per_s", "value": value, "unit": "pairs/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": n * n / value * 1e3, "higher_is_better": True, "scaling": "strong",
+        "impl": "reference", "metric": "pair_distances_per_s_effective", "grid_wall_s": grid_s, "value": value,
+        "unit": "pairs/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": grid_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.config, "desc": cfg["desc"], "n": n, "d": cfg["d"],
-                   "eps": cfg["eps"], "min_samples": cfg["min_samples"]},
+                   "eps": cfg["eps"], "min_samples": ms, "max_bytes_per_batch": cfg["budget"]},
         "cpu_baseline": {"value": value, "unit": "pairs/s", "cores": cb["cores"], "kind": "port",
-                         "sample": cb["sample"]},
+                         "sample": cb["sample"], "grid_wall_s": grid_s},
         "e2e": {"value": value, "unit": "pairs/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference's own path needs RAFT/cuVS/RMM and cannot be built offline; its CPU "
-                "restatement (oracle/dbm_oracle.c, pthreads, sequential fp32 FMA) is timed instead",
+        "extrapolated": True,
+        "note": "the reference's own path needs RAFT/cuVS/RMM and a GPU and cannot be built offline; its "
+                "CPU restatement (oracle/dbm_oracle.c: sequential fp32 FMA distances, literal weak-CC + "
+                "merge labelling, every host core) is timed over the whole grid on a subset of the "
+                "points and extrapolated to N; ms_per_step is that extrapolated grid time",
     }
     print(json.dumps(out), flush=True)
 
@@ -391,6 +462,37 @@ def exact_roofline(stats, unique_pairs, d, dms, sm_mhz, torch, dev, args, ws) ->
             "full_grid_flops": flops, "attainable_frac": 0.75, "traffic": traffic,
             "accounting": "flops evaluated: unique pairs N(N-1)/2 x 3D flops (D FSUB + D FFMA, FMA = 2) x "
                           "executed_fraction; under this accounting the ceiling is 75% of the FMA-counted peak"}
+
+
+def label_checks(args, labels, one_fit, h, x, eps, ms, kw, ws, rank, dev, torch, dist) -> dict:
+    """One untimed fit, then (N > 1) its labels against a one-GPU fit of the same inputs and
+    budget on rank 0, and (full-size workloads) against the oracle's per-configuration SHA-256
+    digests.  Flags: 1 match, 0 mismatch, 2 not applicable; combined with MIN over ranks."""
+    import hashlib
+
+    one_fit()
+    torch.cuda.synchronize()
+    flags = torch.full((2,), 2, dtype=torch.int32, device=dev)
+    if ws > 1 and rank == 0:
+        single = torch.empty_like(labels)
+        h.fit_multi(x, eps, ms, labels_out=single, **kw)
+        flags[0] = int(torch.equal(single, labels))
+    fx_path = ROOT / "tests" / "golden" / "full_size_labels.json"
+    if rank == 0 and not args.n and fx_path.exists():
+        fx = json.loads(fx_path.read_text()).get(args.config)
+        if fx is not None:
+            host = labels.cpu().numpy()
+            got = [hashlib.sha256(np.ascontiguousarray(r, dtype="<i4").tobytes()).hexdigest() for r in host]
+            flags[1] = int(got == [c["sha256"] for c in fx["configs"]])
+    if ws > 1:
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    f = [int(v) for v in flags.tolist()]
+    out = {}
+    if f[0] != 2:
+        out["labels_match_1gpu"] = bool(f[0])
+    if f[1] != 2:
+        out["labels_match_oracle"] = bool(f[1])
+    return out
 
 
 def main() -> None:
@@ -485,6 +587,9 @@ def main() -> None:
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
+    # correctness before timing: the sharded labels against a one-GPU fit, and the labels against
+    # the oracle's digests of this workload (tests/golden/full_size_labels.json, full size only)
+    checks = label_checks(args, labels, one_fit, h, x, eps, ms, kw, ws, rank, dev, torch, dist)
 
     times, dist_ms, screen_ms, stats = [], [], [], None
     torch.cuda.synchronize()
@@ -552,17 +657,21 @@ def main() -> None:
     if rank == 0:
         cb = None
         if not args.no_cpu_baseline and ws == 1:
-            cb = cpu_baseline(pts, eps, target_s=args.cpu_seconds)
+            cb = cpu_pipeline(pts, eps, ms, cfg["budget"], cfg["npr"], target_s=args.cpu_seconds)
             cb.pop("seconds", None)
+            cb["dv"] = dv_baseline(pts, eps, ms)
         out = {
-            "metric": "pair_distances_per_s",
+            "metric": "pair_distances_per_s_effective",
+            "grid_wall_s": ms_per_step / 1e3,
             "value": value,
             "unit": "pairs/s",
+            "metric_note": "value = N^2 ordered pairs per grid / grid wall time (the reference's pair-distances/s "
+                           "unit); it is an effective rate: pruned and screened pairs are resolved without an "
+                           "fp32 distance evaluation (see roofline.exact_chain_pairs)",
             "n_gpus": ws,
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": ms_per_step,
-            "grid_wall_s": ms_per_step / 1e3,
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
@@ -588,12 +697,15 @@ def main() -> None:
                          "relabel": stats.get("ms_relabel")},
             "cpu_baseline": cb,
             "hbm_peak_gbs": measured_peaks().get("hbm_gbs"),
+            **checks,
         }
         print(json.dumps(out), flush=True)
     h.close()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if checks.get("labels_match_1gpu") is False or checks.get("labels_match_oracle") is False:
+        sys.exit(1)
 
 
 if __name__ == "__main__":

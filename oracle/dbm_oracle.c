@@ -440,3 +440,383 @@ int dbmo_annotate_pays(int64_t nnz, int64_t pairs, int k, int64_t d)
     (long double)(k - 1) * ((long double)pairs * (long double)d + 60000000000.0L);
   return cost_annotate < cost_searches;
 }
+
+/* ------------------------------------------------------------------------------------ */
+/* streaming fit: the same results as dbmo_fit_multi, memory bounded by one row batch     */
+/* ------------------------------------------------------------------------------------ */
+/*
+ * dbmo_fit_multi_stream computes exactly what dbmo_fit_multi computes (same codes, degrees,
+ * labels) with the reference's own pass structure (runner_multi.cuh:624-739): a first pass over
+ * all rows for the per-eps degrees, then per row batch the batch's neighbour lists (rows of the
+ * batch x all points, rebuilt from the distances, as the reference's pass 2 rebuilds each
+ * batch's CSR), labelled and merged for every configuration before the next batch.  Only one
+ * batch's lists are held at a time.  Two changes make it fast enough for the full-size
+ * configurations, neither of which changes a result:
+ *   - four query rows share one read of each 16-point candidate block;
+ *   - after every 8 dims, a block whose 4 x 16 partial sums all exceed the largest eps^2 is
+ *     dropped: fma(diff, diff, acc) >= acc, so those pairs end above the cutoff anyway (the
+ *     reference's generic kernel breaks the same way per pair, eps_neighborhood.cuh:247).
+ * Configurations are labelled in parallel (each has its own label, scratch and merge arrays;
+ * the weak-CC and merge of one configuration stay sequential and literal).
+ */
+#define DBMO_QROWS 4
+
+typedef struct {
+  int32_t hist[DBMO_QROWS][DBMO_MAX_EPS + 1];
+  int32_t* col[DBMO_QROWS];  /* NULL: counts only */
+  uint8_t* code[DBMO_QROWS];
+  int64_t fill[DBMO_QROWS];
+} scan_out_t;
+
+static inline __attribute__((always_inline)) void scan_rows_body(const float* x, const float* xt, int64_t n,
+                                                                 int64_t d, const int64_t* qi, int nr,
+                                                                 const float* eps2, int k, scan_out_t* o)
+{
+  const float cutoff = eps2[k - 1];
+  const float* qp[DBMO_QROWS];
+  for (int r = 0; r < DBMO_QROWS; ++r) qp[r] = x + qi[r < nr ? r : (nr > 1 ? nr - 1 : 0)] * d;
+  for (int64_t j0 = 0, b = 0; j0 < n; j0 += DBMO_LANES, ++b) {
+    const float* blk = xt + (size_t)b * (size_t)d * DBMO_LANES;
+    float acc[DBMO_QROWS][DBMO_LANES];
+    for (int r = 0; r < DBMO_QROWS; ++r)
+      for (int l = 0; l < DBMO_LANES; ++l) acc[r][l] = 0.0f;
+    int alive = 1;
+    int64_t t = 0;
+    while (t < d) {
+      const int64_t te = (t + 8 < d) ? t + 8 : d;
+      for (; t < te; ++t) {
+        const float* col = blk + t * DBMO_LANES;
+        for (int r = 0; r < DBMO_QROWS; ++r) {
+          const float qt = qp[r][t];
+#pragma GCC ivdep
+          for (int l = 0; l < DBMO_LANES; ++l) {
+            const float diff = qt - col[l];
+            acc[r][l] = fmaf(diff, diff, acc[r][l]);
+          }
+        }
+      }
+      if (t < d) {
+        int any = 0;
+        for (int r = 0; r < DBMO_QROWS; ++r)
+          for (int l = 0; l < DBMO_LANES; ++l) any |= acc[r][l] <= cutoff;
+        if (!any) {
+          alive = 0;
+          break;
+        }
+      }
+    }
+    if (!alive) continue;
+    const int64_t cnt = (n - j0) < DBMO_LANES ? (n - j0) : DBMO_LANES;
+    for (int r = 0; r < nr; ++r) {
+      for (int64_t l = 0; l < cnt; ++l) {
+        const uint8_t c = code_of(acc[r][l], eps2, k);
+        if (c == DBMO_NO_NEIGHBOR) continue;
+        o->hist[r][c] += 1;
+        if (o->col[r]) {
+          o->col[r][o->fill[r]] = (int32_t)(j0 + l);
+          o->code[r][o->fill[r]] = c;
+          o->fill[r] += 1;
+        }
+      }
+    }
+  }
+}
+
+__attribute__((target("avx2,fma"))) static void scan_rows_fma(const float* x, const float* xt, int64_t n, int64_t d,
+                                                              const int64_t* qi, int nr, const float* eps2, int k,
+                                                              scan_out_t* o)
+{
+  scan_rows_body(x, xt, n, d, qi, nr, eps2, k, o);
+}
+
+static void scan_rows_generic(const float* x, const float* xt, int64_t n, int64_t d, const int64_t* qi, int nr,
+                              const float* eps2, int k, scan_out_t* o)
+{
+  scan_rows_body(x, xt, n, d, qi, nr, eps2, k, o);
+}
+
+static void scan_rows(const float* x, const float* xt, int64_t n, int64_t d, const int64_t* qi, int nr,
+                      const float* eps2, int k, scan_out_t* o)
+{
+  static int have_fma = -1;
+  if (have_fma < 0) {
+    __builtin_cpu_init();
+    have_fma = __builtin_cpu_supports("fma") && __builtin_cpu_supports("avx2");
+  }
+  if (have_fma)
+    scan_rows_fma(x, xt, n, d, qi, nr, eps2, k, o);
+  else
+    scan_rows_generic(x, xt, n, d, qi, nr, eps2, k, o);
+}
+
+typedef struct {
+  const float* x;
+  const float* xt;
+  int64_t n, d;
+  const float* eps2;
+  int k;
+  int64_t row0, rows;     /* rows [row0, row0 + rows) */
+  int32_t* deg;           /* pass 1: k x n cumulative degrees (NULL in pass 2) */
+  const int64_t* off;     /* pass 2: rows + 1 list offsets (relative to the batch) */
+  int32_t* col;           /* pass 2: neighbour lists */
+  uint8_t* code;
+  int64_t next;           /* shared cursor over groups of DBMO_QROWS rows */
+} stream_job_t;
+
+static void* stream_worker(void* arg)
+{
+  stream_job_t* job = (stream_job_t*)arg;
+  const int64_t groups = (job->rows + DBMO_QROWS - 1) / DBMO_QROWS;
+  for (;;) {
+    const int64_t g = __atomic_fetch_add(&job->next, 1, __ATOMIC_RELAXED);
+    if (g >= groups) break;
+    int64_t qi[DBMO_QROWS];
+    int nr = 0;
+    for (int r = 0; r < DBMO_QROWS; ++r) {
+      const int64_t rr = g * DBMO_QROWS + r;
+      if (rr < job->rows) qi[nr++] = job->row0 + rr;
+    }
+    scan_out_t o;
+    memset(&o, 0, sizeof(o));
+    if (job->col) {
+      for (int r = 0; r < nr; ++r) {
+        const int64_t lr = qi[r] - job->row0;
+        o.col[r] = job->col + job->off[lr];
+        o.code[r] = job->code + job->off[lr];
+      }
+    }
+    scan_rows(job->x, job->xt, job->n, job->d, qi, nr, job->eps2, job->k, &o);
+    if (job->deg) {
+      for (int r = 0; r < nr; ++r) {
+        int32_t run = 0;
+        for (int e = 0; e < job->k; ++e) {
+          run += o.hist[r][e];
+          job->deg[(size_t)e * (size_t)job->n + (size_t)qi[r]] = run;
+        }
+      }
+    }
+  }
+  return NULL;
+}
+
+static void run_stream_job(stream_job_t* job, int threads)
+{
+  pthread_t tid[256];
+  int started = 0;
+  for (int w = 1; w < threads; ++w)
+    if (pthread_create(&tid[started], NULL, stream_worker, job) == 0) ++started;
+  stream_worker(job);
+  for (int w = 0; w < started; ++w) pthread_join(tid[w], NULL);
+}
+
+/* weak_cc_batch over the batch-local lists (row r of the batch at off[r - start]). */
+static void weak_cc_batch_local(int32_t* lab, const int64_t* off, const int32_t* col, const uint8_t* code, int e,
+                                const uint8_t* core, int64_t n, int64_t start, int64_t rows)
+{
+  for (int64_t i = 0; i < n; ++i) lab[i] = core[i] ? (int32_t)(i + 1) : DBMO_LABEL_MAX;
+  int changed = 1;
+  while (changed) {
+    changed = 0;
+    for (int64_t r = start; r < start + rows; ++r) {
+      int32_t ci = lab[r];
+      int ci_mod = 0;
+      const int r_core = core[r];
+      for (int64_t p = off[r - start]; p < off[r - start + 1]; ++p) {
+        if (code[p] > e) continue;
+        const int32_t j = col[p];
+        const int32_t cj = lab[j];
+        if (ci < cj && r_core) {
+          lab[j] = ci;
+          if (core[j]) changed = 1;
+        } else if (ci > cj && core[j]) {
+          ci = cj;
+          ci_mod = 1;
+        }
+      }
+      if (ci_mod && ci < lab[r]) {
+        lab[r] = ci;
+        if (r_core) changed = 1;
+      }
+    }
+  }
+}
+
+typedef struct {
+  int64_t n, start, rows, batch;
+  int k, l;
+  const int32_t* deg;
+  const int32_t* minpts;
+  const int64_t* off;
+  const int32_t* col;
+  const uint8_t* code;
+  int32_t* labels;   /* k*l x n */
+  int32_t* tmp;      /* k*l x n scratch */
+  int32_t* R;        /* k*l x n merge map */
+  uint8_t* core;     /* k*l x n */
+  int64_t next;
+} label_job_t;
+
+static void* label_worker(void* arg)
+{
+  label_job_t* job = (label_job_t*)arg;
+  const int64_t C = (int64_t)job->k * job->l;
+  for (;;) {
+    const int64_t cfg = __atomic_fetch_add(&job->next, 1, __ATOMIC_RELAXED);
+    if (cfg >= C) break;
+    const int e = (int)(cfg / job->l);
+    const size_t base = (size_t)cfg * (size_t)job->n;
+    int32_t* out = job->labels + base;
+    weak_cc_batch_local(job->batch == 0 ? out : job->tmp + base, job->off, job->col, job->code, e, job->core + base,
+                        job->n, job->start, job->rows);
+    if (job->batch > 0) merge_labels(out, job->tmp + base, job->core + base, job->R + base, job->n);
+  }
+  return NULL;
+}
+
+static void* relabel_worker(void* arg)
+{
+  label_job_t* job = (label_job_t*)arg;
+  const int64_t C = (int64_t)job->k * job->l;
+  for (;;) {
+    const int64_t cfg = __atomic_fetch_add(&job->next, 1, __ATOMIC_RELAXED);
+    if (cfg >= C) break;
+    const size_t base = (size_t)cfg * (size_t)job->n;
+    relabel(job->labels + base, job->n, job->tmp + base);
+  }
+  return NULL;
+}
+
+static void run_label_job(label_job_t* job, int threads, void* (*fn)(void*))
+{
+  pthread_t tid[256];
+  int started = 0;
+  job->next = 0;
+  for (int w = 1; w < threads; ++w)
+    if (pthread_create(&tid[started], NULL, fn, job) == 0) ++started;
+  fn(job);
+  for (int w = 0; w < started; ++w) pthread_join(tid[w], NULL);
+}
+
+/*
+ * Same contract as dbmo_fit_multi, plus `threads` (<= 0: every online CPU) and an optional
+ * `nnz_out` (sum over batches of the max-eps list entries, self pairs included).
+ */
+int dbmo_fit_multi_stream(const float* x, int64_t n, int64_t d, const float* eps, int k, const int32_t* minpts,
+                          int l, int64_t batch_size, int32_t* labels, uint8_t* core_out, int32_t* deg_out,
+                          int threads, int64_t* nnz_out)
+{
+  if (n < 1 || d < 1 || k < 1 || k > DBMO_MAX_EPS || l < 1 || batch_size < 1) return -1;
+  if (n >= (int64_t)INT32_MAX) return -1;
+  int t = threads > 0 ? threads : dbmo_default_threads();
+  if (t > 256) t = 256;
+  float eps2[DBMO_MAX_EPS];
+  dbmo_square_eps(eps, k, eps2);
+  const int64_t C = (int64_t)k * l;
+  float* xt = transpose_blocks(x, n, d);
+  int32_t* deg = (int32_t*)malloc(sizeof(int32_t) * (size_t)k * (size_t)n);
+  int32_t* tmp = (int32_t*)malloc(sizeof(int32_t) * (size_t)C * (size_t)n);
+  int32_t* R = (int32_t*)malloc(sizeof(int32_t) * (size_t)C * (size_t)n);
+  uint8_t* core = (uint8_t*)malloc((size_t)C * (size_t)n);
+  int64_t* off = (int64_t*)malloc(sizeof(int64_t) * ((size_t)(batch_size < n ? batch_size : n) + 1));
+  if (!xt || !deg || !tmp || !R || !core || !off) return -2;
+
+  /* pass 1: per-eps degrees of every row */
+  stream_job_t job;
+  memset(&job, 0, sizeof(job));
+  job.x = x;
+  job.xt = xt;
+  job.n = n;
+  job.d = d;
+  job.eps2 = eps2;
+  job.k = k;
+  job.row0 = 0;
+  job.rows = n;
+  job.deg = deg;
+  run_stream_job(&job, t);
+  if (deg_out) memcpy(deg_out, deg, sizeof(int32_t) * (size_t)k * (size_t)n);
+  for (int e = 0; e < k; ++e)
+    for (int m = 0; m < l; ++m) {
+      uint8_t* c = core + ((size_t)e * l + m) * (size_t)n;
+      for (int64_t i = 0; i < n; ++i) c[i] = deg[(size_t)e * (size_t)n + (size_t)i] >= minpts[m];
+    }
+  if (core_out) memcpy(core_out, core, (size_t)C * (size_t)n);
+
+  /* pass 2: per batch, its neighbour lists, then every configuration's weak-CC + merge */
+  const int64_t nb = (n + batch_size - 1) / batch_size;
+  int64_t nnz_total = 0;
+  for (int64_t b = 0; b < nb; ++b) {
+    const int64_t start = b * batch_size;
+    const int64_t rows = (n - start) < batch_size ? (n - start) : batch_size;
+    off[0] = 0;
+    for (int64_t r = 0; r < rows; ++r) off[r + 1] = off[r] + deg[(size_t)(k - 1) * (size_t)n + (size_t)(start + r)];
+    const int64_t nnz = off[rows];
+    nnz_total += nnz;
+    int32_t* col = (int32_t*)malloc(sizeof(int32_t) * (size_t)(nnz > 0 ? nnz : 1));
+    uint8_t* code = (uint8_t*)malloc((size_t)(nnz > 0 ? nnz : 1));
+    if (!col || !code) return -2;
+    memset(&job, 0, sizeof(job));
+    job.x = x;
+    job.xt = xt;
+    job.n = n;
+    job.d = d;
+    job.eps2 = eps2;
+    job.k = k;
+    job.row0 = start;
+    job.rows = rows;
+    job.off = off;
+    job.col = col;
+    job.code = code;
+    run_stream_job(&job, t);
+    label_job_t lj;
+    memset(&lj, 0, sizeof(lj));
+    lj.n = n;
+    lj.start = start;
+    lj.rows = rows;
+    lj.batch = b;
+    lj.k = k;
+    lj.l = l;
+    lj.deg = deg;
+    lj.minpts = minpts;
+    lj.off = off;
+    lj.col = col;
+    lj.code = code;
+    lj.labels = labels;
+    lj.tmp = tmp;
+    lj.R = R;
+    lj.core = core;
+    run_label_job(&lj, t, label_worker);
+    free(col);
+    free(code);
+  }
+  label_job_t rj;
+  memset(&rj, 0, sizeof(rj));
+  rj.n = n;
+  rj.k = k;
+  rj.l = l;
+  rj.labels = labels;
+  rj.tmp = tmp;
+  run_label_job(&rj, t, relabel_worker);
+  if (nnz_out) *nnz_out = nnz_total;
+  free(xt);
+  free(deg);
+  free(tmp);
+  free(R);
+  free(core);
+  free(off);
+  return 0;
+}
+
+/* The reference's per-pair value acc (eps_neighborhood.cuh:151-158: sequential fma over the
+ * dims) for m pairs (a[i*d ..], b[i*d ..]) -> out[i]; used by tests to plant pairs exactly at
+ * an eps boundary. */
+void dbmo_pair_chain(const float* a, const float* b, int64_t m, int64_t d, float* out)
+{
+  for (int64_t i = 0; i < m; ++i) {
+    float acc = 0.0f;
+    for (int64_t t = 0; t < d; ++t) {
+      const float diff = a[i * d + t] - b[i * d + t];
+      acc = fmaf(diff, diff, acc);
+    }
+    out[i] = acc;
+  }
+}

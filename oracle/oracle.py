@@ -36,8 +36,12 @@ def _load():
     i64, i32, p = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
     lib.dbmo_fit_multi.argtypes = [p, i64, i64, p, i32, p, i32, i64, p, p, p]
     lib.dbmo_fit_multi.restype = i32
+    lib.dbmo_fit_multi_stream.argtypes = [p, i64, i64, p, i32, p, i32, i64, p, p, p, i32, p]
+    lib.dbmo_fit_multi_stream.restype = i32
     lib.dbmo_codes_degrees.argtypes = [p, i64, i64, p, i32, i64, i64, p, p, i32]
     lib.dbmo_codes_degrees.restype = i32
+    lib.dbmo_pair_chain.argtypes = [p, p, i64, i64, p]
+    lib.dbmo_pair_chain.restype = None
     lib.dbmo_square_eps.argtypes = [p, i32, p]
     lib.dbmo_square_eps.restype = None
     lib.dbmo_annotate_pays.argtypes = [i64, i64, i32, i64]
@@ -82,6 +86,29 @@ def fit_multi(points, eps, min_samples, batch_size: int | None = None):
     return labels, core.astype(bool), deg
 
 
+def fit_multi_stream(points, eps, min_samples, batch_size: int | None = None, threads: int = 0):
+    """The same labels, core masks and degrees as fit_multi, computed batch by batch with only
+    one batch's neighbour lists in memory (the reference's own two-pass structure), on
+    `threads` host threads (0 = all).  Returns (labels, core, deg, nnz), nnz = the max-eps list
+    entries summed over batches (self pairs included)."""
+    lib = _load()
+    x = np.ascontiguousarray(points, dtype=np.float32)
+    n, d = x.shape
+    e = np.ascontiguousarray(eps, dtype=np.float32)
+    m = np.ascontiguousarray(min_samples, dtype=np.int32)
+    k, l = len(e), len(m)
+    bs = n if batch_size is None else int(batch_size)
+    labels = np.empty((k * l, n), dtype=np.int32)
+    core = np.empty((k * l, n), dtype=np.uint8)
+    deg = np.empty((k, n), dtype=np.int32)
+    nnz = ctypes.c_int64(0)
+    rc = lib.dbmo_fit_multi_stream(_ptr(x), n, d, _ptr(e), k, _ptr(m), l, bs, _ptr(labels), _ptr(core), _ptr(deg),
+                                   int(threads), ctypes.byref(nnz))
+    if rc != 0:
+        raise RuntimeError(f"dbmo_fit_multi_stream failed with {rc}")
+    return labels, core.astype(bool), deg, int(nnz.value)
+
+
 def codes_degrees(points, eps, row0: int = 0, rows: int | None = None, want_codes: bool = True,
                   threads: int = 0):
     """Per-pair codes (rows, N) uint8 (255 = none) and cumulative degrees (k, rows)."""
@@ -98,6 +125,19 @@ def codes_degrees(points, eps, row0: int = 0, rows: int | None = None, want_code
     if rc != 0:
         raise RuntimeError(f"dbmo_codes_degrees failed with {rc}")
     return codes, deg
+
+
+def pair_chain(a, b) -> np.ndarray:
+    """The reference's fp32 value acc(a_i, b_i) (sequential fma over the dims) for each row pair
+    of two (m, d) arrays."""
+    lib = _load()
+    x = np.ascontiguousarray(a, dtype=np.float32)
+    y = np.ascontiguousarray(b, dtype=np.float32)
+    if x.ndim == 1:
+        x, y = x[None], y[None]
+    out = np.empty(x.shape[0], dtype=np.float32)
+    lib.dbmo_pair_chain(_ptr(x), _ptr(y), x.shape[0], x.shape[1], _ptr(out))
+    return out
 
 
 def annotate_pays(nnz: int, pairs: int, k: int, d: int) -> bool:

@@ -145,3 +145,78 @@ def test_large_case_screened_equals_exact(handles, torch_mod):
     lab_s, core_s, st_s = fit(handles["screened"], torch_mod, pts, eps, ms)
     assert st_s["edges"] == st_x["edges"] > 0
     assert np.array_equal(lab_s, lab_x) and np.array_equal(core_s, core_x)
+
+
+# ---- pairs planted exactly at the eps boundary, far from the tile centres ------------------------
+def plant_partners(rng, base, e2, offset):
+    """For each row x_i of `base` a partner x_j whose reference chain value (fp32 sequential fma,
+    src/multi/eps_neighborhood.cuh:151-158) is exactly the float `offset` ulps from e2
+    (0: acc == fl(eps^2), the closed ball's edge; +1: the next float above, not a neighbour;
+    -1: the float below).  The leading D-1 coordinates carry ~3/4 of the distance in a random
+    direction; the last coordinate (kept near 0 in `base`, so its float grid is fine) is scanned
+    over consecutive floats until the chain lands on the target.  Returns (partners, ok mask)."""
+    m, d = base.shape
+    target = np.float32(e2)
+    for _ in range(abs(offset)):
+        target = np.nextafter(target, np.float32(np.inf if offset > 0 else -np.inf))
+    u = rng.standard_normal((m, d - 1))
+    u /= np.linalg.norm(u, axis=1, keepdims=True)
+    part = base.copy()
+    part[:, : d - 1] = (base[:, : d - 1] - u * np.sqrt(0.75 * float(e2))).astype(np.float32)
+    prefix = oracle.pair_chain(base[:, : d - 1], part[:, : d - 1]).astype(np.float64)
+    d_last = np.sqrt(np.maximum(float(target) - prefix, 0.0))
+    v0 = (base[:, d - 1] - d_last).astype(np.float32)  # negative: base's last coordinate is in [0, 1)
+    steps = np.arange(-3000, 3001, dtype=np.int64)
+    ok = np.zeros(m, bool)
+    for r in range(m):
+        bits = v0[r:r + 1].view(np.int32).astype(np.int64) + steps
+        cand = bits.astype(np.int32).view(np.float32)
+        trial = np.repeat(part[r:r + 1], len(cand), axis=0)
+        trial[:, d - 1] = cand
+        acc = oracle.pair_chain(np.repeat(base[r:r + 1], len(cand), axis=0), trial)
+        hit = np.flatnonzero(acc == target)
+        if hit.size:
+            part[r, d - 1] = cand[hit[hit.size // 2]]
+            ok[r] = True
+    return part, ok
+
+
+@pytest.mark.parametrize("d,eps", [(33, [4.0, 4.5]), (64, [9.0, 12.0])])
+def test_screen_keeps_pairs_planted_at_the_eps_boundary(handles, torch_mod, d, eps):
+    """KP = 40 (D = 33) and 72 (D = 64) tf32 columns, the accumulation lengths of the real
+    instances.  Base points are spread over [-1000, 1000] in every leading dim, so each tile's
+    box centre sits ~1000 sqrt(D) from its points (the per-row slack of the bound is largest
+    there, r / s ~ 10^3); partners sit at exactly fl(eps_max^2), one ulp inside and one ulp
+    outside.  Degrees and labels of the screened pass must equal the oracle's, every planted
+    boundary pair must be found, and no tile pair may fall back to the exact kernel (the
+    screen, not the fallback, decided them)."""
+    rng = np.random.default_rng(d)
+    nb, per = 5000, 300
+    base = rng.uniform(-1000, 1000, (nb, d)).astype(np.float32)
+    base[:, d - 1] = rng.uniform(0, 1, nb).astype(np.float32)
+    e2 = np.float32(np.float32(eps[-1]) * np.float32(eps[-1]))
+    parts, oks = [], []
+    for v, off in enumerate((0, -1, 1)):
+        p, ok = plant_partners(rng, base[v * per:(v + 1) * per], e2, off)
+        parts.append(p)
+        oks.append(ok)
+    assert all(ok.mean() > 0.9 for ok in oks), [ok.mean() for ok in oks]
+    pts = np.vstack([base] + parts)
+    # planted chain values, re-checked with the oracle's own chain
+    for v, off in enumerate((0, -1, 1)):
+        acc = oracle.pair_chain(base[v * per:(v + 1) * per][oks[v]], parts[v][oks[v]])
+        assert np.all((acc == e2) if off == 0 else ((acc < e2) if off < 0 else (acc > e2)))
+    ms = [2, 3]
+    want, want_core, want_deg = oracle.fit_multi(pts, eps, ms)
+    x = torch_mod.from_numpy(pts).cuda()
+    deg = handles["screened"].neighbor_counts(x, eps).cpu().numpy()
+    assert np.array_equal(deg, want_deg)
+    lab, core, st = fit(handles["screened"], torch_mod, pts, eps, ms)
+    assert np.array_equal(lab, want) and np.array_equal(core, want_core)
+    assert st["screened_tile_pairs"] > 0 and st["fallback_tile_pairs"] == 0
+    # the boundary pairs themselves: in, in, out
+    for v, off in enumerate((0, -1, 1)):
+        i = np.arange(v * per, (v + 1) * per)[oks[v]]
+        j = nb + v * per + np.flatnonzero(oks[v])
+        same = lab[-2][i] == lab[-2][j]  # minPts 2 at the largest eps: a planted pair is one cluster
+        assert np.all(same & (lab[-2][i] >= 0)) if off <= 0 else np.all(lab[-2][i] == -1)
