@@ -71,6 +71,13 @@ CONFIGS = {
                 npr=0,
                 desc="Dense-route stress, calibrated: the C5 points with eps at the 5/10/20% quantiles "
                      "of 200,000 sampled pair distances; 3x3 grid"),
+    # the same grid under a 64 GB budget: the whole pair list + CSR (~117 GB for 4e9 neighbour
+    # pairs) no longer fits, so the graph is built one row batch at a time
+    "c5qb": dict(n=200_000, d=64, centers=10, box=5.0, std=(2.0, 2.0), noise=0.0, zero_cols=0,
+                 eps=None, eps_quantiles=(0.05, 0.10, 0.20), min_samples=[10, 50, 200], budget=64 * 10**9,
+                 npr=0,
+                 desc="Dense-route stress, calibrated, memory-bounded: the c5q grid under a 64 GB budget "
+                      "(the graph is built per row batch)"),
 }
 
 

@@ -22,6 +22,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <limits>
 #include <vector>
 
@@ -58,12 +59,17 @@ Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32
 Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
                           long long* work, int64_t cap, cudaStream_t s);
 Status spatial_order(const float* x, int64_t n, int32_t d, int32_t* perm, void* scratch, size_t scratch_bytes,
-                     cudaStream_t s);
+                     cudaStream_t s, int64_t batch_rows = 0);
 Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
                       int32_t* deg, int32_t* corecnt, int32_t* rowcnt, uint8_t* core_out,
                       cudaStream_t s);
 Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, int32_t* fill,
                           uint32_t* col, int32_t* row, cudaStream_t s);
+Status launch_csr_scatter_batch(const uint64_t* edges, int64_t cap, const unsigned long long* m_dev, const int64_t* off,
+                                int64_t s0, int64_t s1, int32_t* fill, uint32_t* col, int32_t* row, int32_t* err,
+                                cudaStream_t s);
+Status launch_batch_worklist(const long long* work, int64_t count, int64_t t0, int64_t t1, int32_t* flags,
+                             int64_t* pos, void* scan_scratch, size_t scan_bytes, long long* out, cudaStream_t s);
 Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, int64_t* out,
                         cudaStream_t s);
 Status launch_label_range(const int32_t* labels, int64_t total, int64_t n, unsigned long long* first_bad,
@@ -76,7 +82,7 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
                        int union_limit, cudaStream_t s);
 Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0, int64_t rows, int32_t* counts,
                               cudaStream_t s);
-Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int ne,
+Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t col_base, int64_t s0, int64_t rows, int ne,
                          const int64_t* off_flat, int32_t* col_flat, int32_t* row_flat, cudaStream_t s);
 Status launch_cc_root_bits(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc, int32_t* G,
                            uint32_t* words, int32_t* cnt, int sm_count, cudaStream_t s);
@@ -216,8 +222,11 @@ struct dbm_handle {
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
   dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_scratch, work, fallback;
+  dbm::Buffer subwork, subflags, subpos;  // one batch's tile pairs (streamed fit)
   int distance_mode = DBM_DISTANCE_AUTO;
+  int graph_mode = DBM_GRAPH_AUTO;
   int union_limit = dbm::kUnionRetryLimit;  // test knob (dbm_set_union_retry_limit)
+  int64_t stream_work_count = 0;           // tile pairs of the batch-major worklist (streamed fit)
   dbm::Buffer xdev, labels_dev, core_dev;  // host-buffer entry point only
   int64_t* pinned = nullptr;               // small D2H staging
   size_t pinned_count = 0;
@@ -228,7 +237,7 @@ struct dbm_handle {
                                 &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
                                 &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz,
                                 &perm, &order_scratch, &box_lo, &box_hi, &prune_scratch,
-                                &work, &fallback};
+                                &work, &fallback, &subwork, &subflags, &subpos};
     uint64_t s = 0;
     for (auto* b : all) s += b->bytes;
     return s;
@@ -330,6 +339,8 @@ static Status read_err_flag(dbm_handle* h, cudaStream_t s)
     return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded TMA wait in the distance kernel ran out");
   if (f & kErrUnionLimit)
     return Status::Err(DBM_ERR_NOT_CONVERGED, "union-find retry bound ran out");
+  if (f & kErrGraphMismatch)
+    return Status::Err(DBM_ERR_CUDA, "a row batch's neighbour pairs disagree with the degree pass");
   return Status::Ok();
 }
 
@@ -428,9 +439,12 @@ static Status plan_budget(dbm_handle* h, int64_t n, int k, int l, const dbm_opti
 }
 
 // Distance pass over one shard of the tile pairs into hist (zeroed here) and h->edges.
+// With regrow, a pair buffer that turns out too small is grown to the exact count and the pass
+// repeated; without, the call returns after one pass with *found_out > *cap_out (the histograms are
+// complete either way, the pair list only when found <= cap).
 static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps2, int k,
                              int shard, int nshards, int32_t* hist, uint64_t cap_hint, uint64_t* found_out,
-                             dbm_stats& st, cudaStream_t s)
+                             dbm_stats& st, cudaStream_t s, bool regrow = true, uint64_t* cap_out = nullptr)
 {
   const int32_t di = static_cast<int32_t>(d);
   const int64_t kn = static_cast<int64_t>(k) * n;
@@ -528,7 +542,7 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
       if (work_count > work_cap) {
         // the worklist outgrew the learned capacity: redo the pass with the exact size (the
         // hint is now large enough, so this recursion ends after one level)
-        return distance_stage(h, x, n, d, eps2, k, shard, nshards, hist, cap_hint, found_out, st, s);
+        return distance_stage(h, x, n, d, eps2, k, shard, nshards, hist, cap_hint, found_out, st, s, regrow, cap_out);
       }
     }
     st.tile_pairs_kept = !count_dev ? 1.0 : pairs > 0 ? static_cast<double>(work_count) / static_cast<double>(pairs) : 1.0;
@@ -546,27 +560,38 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     if (flags & kErrNonFinite) return Status::Err(DBM_ERR_NONFINITE, "the input contains NaN or infinity");
     if (flags & kErrTmaTimeout)
       return Status::Err(DBM_ERR_NOT_CONVERGED, "a bounded wait in the distance kernels ran out");
-    if (found <= cap) break;
+    if (found <= cap || !regrow) break;
     if (pass == 1) return Status::Err(DBM_ERR_CUDA, "neighbour-pair buffer overflowed twice");
     cap = found;
   }
-  h->edge_cap_hint = std::max<uint64_t>(h->edge_cap_hint, found);
+  if (found <= cap) h->edge_cap_hint = std::max<uint64_t>(h->edge_cap_hint, found);
   *found_out = found;
+  if (cap_out) *cap_out = cap;
   return Status::Ok();
 }
 
-// Everything after the distance pass, from the complete per-code histograms and the complete
-// list of neighbour pairs: degrees, core masks, CSR, batch plan, labelling of the configs
-// [cfg_begin, cfg_end).
-static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int32_t* minpts, int l,
-                          const int32_t* hist, const uint64_t* edges, uint64_t found, int cfg_begin,
-                          int cfg_end, int32_t* labels, uint8_t* core_out, const dbm_options& opt,
-                          const Plan& plan, dbm_stats& st, std::vector<uint8_t>& routes, cudaStream_t s)
+// ---- after the distance pass ------------------------------------------------------------------
+// Batch plan of one fit: the reference's batch size for the budget, corrected on the measured
+// per-batch nnz (runner_multi.cuh:1340-1456), and the per-batch routes.
+struct BatchPlan {
+  uint64_t bs = 0;
+  int64_t nb = 0;
+  std::vector<int64_t> bnnz;  // per batch, at the largest eps, self pairs included
+  int64_t max_count = 0;      // largest per-batch entry count (self pairs excluded)
+  int64_t rows(int64_t b, int64_t n) const
+  {
+    return std::min<int64_t>(n - b * static_cast<int64_t>(bs), static_cast<int64_t>(bs));
+  }
+};
+
+// Degrees, core counts (and the optional byte core masks), CSR row offsets, batch plan and routes,
+// from the complete per-code histograms.
+static Status graph_prep(dbm_handle* h, int64_t n, int64_t d, int k, const int32_t* minpts, int l,
+                         const int32_t* hist, uint8_t* core_out, const dbm_options& opt, const Plan& plan,
+                         dbm_stats& st, std::vector<uint8_t>& routes, BatchPlan& bp, cudaStream_t s)
 {
   const int64_t kn = static_cast<int64_t>(k) * n;
   const int64_t kln = kn * l;
-  st.unique_pairs = n * (n - 1) / 2;
-  st.edges = static_cast<int64_t>(found);
   DBM_TRY(ensure(h->deg, sizeof(int32_t) * kn));
   DBM_TRY(ensure(h->cc, sizeof(int32_t) * kn));
   DBM_TRY(ensure(h->rowcnt, sizeof(int32_t) * n));
@@ -577,41 +602,31 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
   DBM_TRY(ensure(h->scan_scratch, std::max(scan_scratch_bytes(n + 1), scan_scratch_bytes(kln + 1))));
   DBM_TRY(ensure_pinned(h, 16));
   DBM_CUDA(cudaMemcpyAsync(h->minpts.p, minpts, sizeof(int32_t) * l, cudaMemcpyHostToDevice, s));
-
-  // ---- degrees, core counts, CSR ----
   {
     PhaseTimer t(h, s, &st.ms_graph);
     DBM_TRY(launch_degrees(hist, n, k, as<int32_t>(h->minpts), l, as<int32_t>(h->deg), as<int32_t>(h->cc),
                            as<int32_t>(h->rowcnt), core_out, s));
     DBM_TRY(exclusive_scan_i32(as<int32_t>(h->rowcnt), as<int64_t>(h->off), n, h->scan_scratch.p,
                                h->scan_scratch.bytes, s));
-    DBM_TRY(ensure(h->col, sizeof(uint32_t) * 2 * std::max<uint64_t>(found, 1)));
-    DBM_TRY(ensure(h->crow, sizeof(int32_t) * 2 * std::max<uint64_t>(found, 1)));
-    DBM_CUDA(cudaMemsetAsync(h->fill.p, 0, sizeof(int32_t) * n, s));
-    DBM_TRY(launch_csr_scatter(edges, static_cast<int64_t>(found), as<int64_t>(h->off), as<int32_t>(h->fill),
-                               as<uint32_t>(h->col), as<int32_t>(h->crow), s));
   }
 
   // ---- batch plan with the reference's correction rule ----
   const uint64_t isz = isz_of(plan.index_bits);
   const uint64_t per_entry = csr_bytes_per_entry(k, plan.use_cuvs, isz);
   uint64_t cap_rows = static_cast<uint64_t>(n);
-  std::vector<int64_t> bnnz;
-  uint64_t bs = 0;
-  int64_t nb = 0;
   bool planned = false;
   for (int attempt = 0; attempt < 3 && !planned; ++attempt) {
     uint64_t rule_bs = 0;
     DBM_TRY(batch_size_rule(n, k, l, plan.budget, plan.use_cuvs, opt.neigh_per_row, plan.index_bits, &rule_bs));
-    bs = std::min(rule_bs, cap_rows);
-    nb = ceil_div(n, static_cast<int64_t>(bs));
+    bp.bs = std::min(rule_bs, cap_rows);
+    bp.nb = ceil_div(n, static_cast<int64_t>(bp.bs));
     st.attempts = attempt + 1;
-    DBM_TRY(ensure(h->bnnz, sizeof(int64_t) * nb));
-    DBM_TRY(ensure_pinned(h, static_cast<size_t>(nb)));
-    DBM_TRY(launch_batch_nnz(as<int64_t>(h->off), n, static_cast<int64_t>(bs), nb, as<int64_t>(h->bnnz), s));
-    DBM_CUDA(cudaMemcpyAsync(h->pinned, h->bnnz.p, sizeof(int64_t) * nb, cudaMemcpyDeviceToHost, s));
+    DBM_TRY(ensure(h->bnnz, sizeof(int64_t) * bp.nb));
+    DBM_TRY(ensure_pinned(h, static_cast<size_t>(bp.nb)));
+    DBM_TRY(launch_batch_nnz(as<int64_t>(h->off), n, static_cast<int64_t>(bp.bs), bp.nb, as<int64_t>(h->bnnz), s));
+    DBM_CUDA(cudaMemcpyAsync(h->pinned, h->bnnz.p, sizeof(int64_t) * bp.nb, cudaMemcpyDeviceToHost, s));
     DBM_CUDA(cudaStreamSynchronize(s));
-    bnnz.assign(h->pinned, h->pinned + nb);
+    bp.bnnz.assign(h->pinned, h->pinned + bp.nb);
     uint64_t available = opt.csr_cap_bytes;
     if (available == 0) {
       size_t fr = 0, to = 0;
@@ -620,16 +635,15 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
     }
     int64_t measured = 0;
     if (plan.use_cuvs) {
-      for (int64_t b = nb - 1; b >= 0; --b) {
-        const int64_t rows = std::min<int64_t>(n - b * static_cast<int64_t>(bs), static_cast<int64_t>(bs));
-        if (!csr_fits(bnnz[b], per_entry, available)) {
-          measured = measured_degree(bnnz[b], rows);
+      for (int64_t b = bp.nb - 1; b >= 0; --b) {
+        if (!csr_fits(bp.bnnz[b], per_entry, available)) {
+          measured = measured_degree(bp.bnnz[b], bp.rows(b, n));
           break;
         }
       }
     } else {
-      const int64_t mx = *std::max_element(bnnz.begin(), bnnz.end());
-      if (!csr_fits(mx, per_entry, available)) measured = measured_degree(mx, static_cast<int64_t>(bs));
+      const int64_t mx = *std::max_element(bp.bnnz.begin(), bp.bnnz.end());
+      if (!csr_fits(mx, per_entry, available)) measured = measured_degree(mx, static_cast<int64_t>(bp.bs));
     }
     if (measured == 0) {
       planned = true;
@@ -638,97 +652,144 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
     st.batch_corrections += 1;
     const int64_t degree = attempt == 0 ? measured : n;
     const uint64_t new_cap = csr_rows_that_fit(degree, per_entry, available);
-    if (!(new_cap < bs))
+    if (!(new_cap < bp.bs))
       return Status::Err(DBM_ERR_CSR_NOT_FIT,
-                         "the CSR does not fit in memory even with a batch of " + std::to_string(bs) +
+                         "the CSR does not fit in memory even with a batch of " + std::to_string(bp.bs) +
                            " rows (N=" + std::to_string(n) + ", measured degree " + std::to_string(measured) +
                            "); reduce --max-mbytes-per-batch or revisit eps");
     cap_rows = new_cap;
   }
   if (!planned) return Status::Err(DBM_ERR_CSR_NOT_FIT, "could not size the batch in 3 attempts");
-  st.batch_size = bs;
-  st.batches = static_cast<int32_t>(nb);
-  routes.assign(static_cast<size_t>(nb), DBM_BATCH_NOT_APPLICABLE);
+  st.batch_size = bp.bs;
+  st.batches = static_cast<int32_t>(bp.nb);
+  routes.assign(static_cast<size_t>(bp.nb), DBM_BATCH_NOT_APPLICABLE);
   st.max_nnz = 0;
   st.total_nnz_max_eps = 0;
-  for (int64_t b = 0; b < nb; ++b) {
-    st.max_nnz = std::max<int64_t>(st.max_nnz, bnnz[b]);
-    st.total_nnz_max_eps += bnnz[b];
+  bp.max_count = 0;
+  for (int64_t b = 0; b < bp.nb; ++b) {
+    const int64_t rows = bp.rows(b, n);
+    st.max_nnz = std::max<int64_t>(st.max_nnz, bp.bnnz[b]);
+    st.total_nnz_max_eps += bp.bnnz[b];
+    bp.max_count = std::max<int64_t>(bp.max_count, bp.bnnz[b] - rows);
     if (plan.use_cuvs && k > 1) {
-      const int64_t rows = std::min<int64_t>(n - b * static_cast<int64_t>(bs), static_cast<int64_t>(bs));
       const bool annotate = opt.route == DBM_ROUTE_ANNOTATED ? true
                             : opt.route == DBM_ROUTE_DENSE   ? false
-                                                             : annotate_pays(bnnz[b], n * rows, k, d);
+                                                             : annotate_pays(bp.bnnz[b], n * rows, k, d);
       routes[b] = annotate ? DBM_BATCH_ANNOTATED : DBM_BATCH_DENSE;
       if (annotate) st.annotated_batches += 1; else st.dense_batches += 1;
     }
   }
+  return Status::Ok();
+}
 
-  // ---- labelling of the configs [cfg_begin, cfg_end) ----
-  {
-    PhaseTimer t(h, s, &st.ms_label);
-    int64_t max_slab = 0;
-    for (int64_t b = 0; b < nb; ++b) {
-      const int64_t rows = std::min<int64_t>(n - b * static_cast<int64_t>(bs), static_cast<int64_t>(bs));
-      max_slab = std::max<int64_t>(max_slab, bnnz[b] - rows);
-    }
-    DBM_TRY(ensure(h->G, sizeof(int32_t) * kln));
-    DBM_TRY(ensure(h->cur, sizeof(int32_t) * kln));
-    DBM_TRY(ensure(h->best, sizeof(unsigned long long) * kln));
-    if (nb > 1) DBM_TRY(ensure(h->L, sizeof(int32_t) * kln));
-    const int ne = k - 1;  // smaller eps, compacted on the annotated route
-    if (ne > 0) {
-      DBM_TRY(ensure(h->slab_counts, sizeof(int32_t) * bs * ne));
-      DBM_TRY(ensure(h->slab_off, sizeof(int64_t) * (bs * ne + 1)));
-      DBM_TRY(ensure(h->slab_col, sizeof(int32_t) * std::max<int64_t>(max_slab * ne, 1)));
-      DBM_TRY(ensure(h->slab_row, sizeof(int32_t) * std::max<int64_t>(max_slab * ne, 1)));
-      DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(static_cast<int64_t>(bs) * ne + 1)));
-    }
-    DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur), as<unsigned long long>(h->best), s));
-    int64_t base = 0;  // first max-eps CSR entry of the batch
-    for (int64_t b = 0; b < nb; ++b) {
-      const int64_t s0 = b * static_cast<int64_t>(bs);
-      const int64_t rows = std::min<int64_t>(n - s0, static_cast<int64_t>(bs));
-      const int64_t count = bnnz[b] - rows;  // entries without the self pairs
-      const uint32_t tag = static_cast<uint32_t>(nb - 1 - b);
-      SlabRef max_eps;
-      max_eps.row = as<int32_t>(h->crow) + base;
-      max_eps.col = reinterpret_cast<const int32_t*>(h->col.p) + base;
-      max_eps.count = count;
-      MultiSlab ms;
-      // smaller-eps slabs are only needed when this call owns a config of a smaller eps
-      const bool owns_small_eps = cfg_begin < ne * l;
-      if (routes[b] == DBM_BATCH_DENSE || ne == 0 || !owns_small_eps) {
-        // direct: eps membership straight from each max-eps entry's code, no per-eps copies
-        ms.direct = 1;
-        ms.nslabs = 1;
-        ms.s[0] = max_eps;
-      } else {
-        // annotated: one pass compacts every smaller eps (order-preserving), then all slabs
-        DBM_TRY(launch_slab_counts_all(as<int32_t>(h->deg), n, ne, s0, rows, as<int32_t>(h->slab_counts), s));
-        DBM_TRY(exclusive_scan_i32(as<int32_t>(h->slab_counts), as<int64_t>(h->slab_off), rows * ne,
-                                   h->scan_scratch.p, h->scan_scratch.bytes, s));
-        DBM_TRY(launch_filter_all(as<int64_t>(h->off), as<uint32_t>(h->col), s0, rows, ne, as<int64_t>(h->slab_off),
-                                  as<int32_t>(h->slab_col), as<int32_t>(h->slab_row), s));
-        ms.direct = 0;
-        ms.nslabs = k;
-        for (int e = 0; e < ne; ++e) {
-          ms.s[e].row = as<int32_t>(h->slab_row);
-          ms.s[e].col = as<int32_t>(h->slab_col);
-          ms.s[e].count = count;
-          ms.s[e].begin_dev = as<int64_t>(h->slab_off) + static_cast<int64_t>(e) * rows;
-          ms.s[e].end_dev = as<int64_t>(h->slab_off) + static_cast<int64_t>(e + 1) * rows;
-        }
-        ms.s[ne] = max_eps;
-      }
-      DBM_TRY(launch_cc_batch(ms, count, n, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc), nb == 1,
-                              as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
-                              as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, h->union_limit, s));
-      base += count;
-    }
+// Bytes of the smaller-eps slabs the labelling compacts per batch (annotated batches of a call
+// that owns a config of a smaller eps), sized by the largest batch.
+static uint64_t slab_bytes(const BatchPlan& bp, const std::vector<uint8_t>& routes, int k, int l, int cfg_begin)
+{
+  const int ne = k - 1;
+  if (ne <= 0 || cfg_begin >= ne * l) return 0;
+  bool any = false;
+  for (auto r : routes) any |= r == DBM_BATCH_ANNOTATED;
+  if (!any) return 0;
+  return 2 * sizeof(int32_t) * static_cast<uint64_t>(std::max<int64_t>(bp.max_count, 1)) * ne +
+         sizeof(int32_t) * bp.bs * ne + sizeof(int64_t) * (bp.bs * ne + 1);
+}
+
+// The whole symmetric max-eps CSR from the complete list of neighbour pairs.
+static Status build_csr(dbm_handle* h, int64_t n, const uint64_t* edges, uint64_t found, dbm_stats& st, cudaStream_t s)
+{
+  PhaseTimer t(h, s, &st.ms_graph);
+  DBM_TRY(ensure(h->col, sizeof(uint32_t) * 2 * std::max<uint64_t>(found, 1)));
+  DBM_TRY(ensure(h->crow, sizeof(int32_t) * 2 * std::max<uint64_t>(found, 1)));
+  DBM_CUDA(cudaMemsetAsync(h->fill.p, 0, sizeof(int32_t) * n, s));
+  DBM_TRY(launch_csr_scatter(edges, static_cast<int64_t>(found), as<int64_t>(h->off), as<int32_t>(h->fill),
+                             as<uint32_t>(h->col), as<int32_t>(h->crow), s));
+  return Status::Ok();
+}
+
+// Where one batch's max-eps entries are: rows / cols of its `count` entries (col with the code
+// in the top 4 bits), and the CSR position of col[0] (the per-eps compaction indexes col by CSR
+// position).
+struct BatchSlab {
+  const int32_t* row = nullptr;
+  const uint32_t* col = nullptr;
+  int64_t col_base = 0;
+};
+using SlabSource = std::function<Status(int64_t b, int64_t s0, int64_t rows, int64_t base, BatchSlab& out)>;
+
+// Labelling of the configs [cfg_begin, cfg_end), batches ascending; `source` yields each batch's
+// max-eps entries.
+static Status label_batches(dbm_handle* h, int64_t n, int k, int l, int cfg_begin, int cfg_end, const BatchPlan& bp,
+                            const std::vector<uint8_t>& routes, dbm_stats& st, const SlabSource& source,
+                            cudaStream_t s)
+{
+  const int64_t kln = static_cast<int64_t>(k) * l * n;
+  const uint64_t bs = bp.bs;
+  const int64_t nb = bp.nb;
+  PhaseTimer t(h, s, &st.ms_label);
+  DBM_TRY(ensure(h->G, sizeof(int32_t) * kln));
+  DBM_TRY(ensure(h->cur, sizeof(int32_t) * kln));
+  DBM_TRY(ensure(h->best, sizeof(unsigned long long) * kln));
+  if (nb > 1) DBM_TRY(ensure(h->L, sizeof(int32_t) * kln));
+  const int ne = k - 1;  // smaller eps, compacted on the annotated route
+  if (ne > 0) {
+    DBM_TRY(ensure(h->slab_counts, sizeof(int32_t) * bs * ne));
+    DBM_TRY(ensure(h->slab_off, sizeof(int64_t) * (bs * ne + 1)));
+    DBM_TRY(ensure(h->slab_col, sizeof(int32_t) * std::max<int64_t>(bp.max_count * ne, 1)));
+    DBM_TRY(ensure(h->slab_row, sizeof(int32_t) * std::max<int64_t>(bp.max_count * ne, 1)));
+    DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(static_cast<int64_t>(bs) * ne + 1)));
   }
+  DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur), as<unsigned long long>(h->best), s));
+  int64_t base = 0;  // first max-eps CSR entry of the batch
+  for (int64_t b = 0; b < nb; ++b) {
+    const int64_t s0 = b * static_cast<int64_t>(bs);
+    const int64_t rows = bp.rows(b, n);
+    const int64_t count = bp.bnnz[b] - rows;  // entries without the self pairs
+    const uint32_t tag = static_cast<uint32_t>(nb - 1 - b);
+    BatchSlab slab;
+    DBM_TRY(source(b, s0, rows, base, slab));
+    SlabRef max_eps;
+    max_eps.row = slab.row;
+    max_eps.col = reinterpret_cast<const int32_t*>(slab.col);
+    max_eps.count = count;
+    MultiSlab ms;
+    // smaller-eps slabs are only needed when this call owns a config of a smaller eps
+    const bool owns_small_eps = cfg_begin < ne * l;
+    if (routes[b] == DBM_BATCH_DENSE || ne == 0 || !owns_small_eps) {
+      // direct: eps membership straight from each max-eps entry's code, no per-eps copies
+      ms.direct = 1;
+      ms.nslabs = 1;
+      ms.s[0] = max_eps;
+    } else {
+      // annotated: one pass compacts every smaller eps (order-preserving), then all slabs
+      DBM_TRY(launch_slab_counts_all(as<int32_t>(h->deg), n, ne, s0, rows, as<int32_t>(h->slab_counts), s));
+      DBM_TRY(exclusive_scan_i32(as<int32_t>(h->slab_counts), as<int64_t>(h->slab_off), rows * ne,
+                                 h->scan_scratch.p, h->scan_scratch.bytes, s));
+      DBM_TRY(launch_filter_all(as<int64_t>(h->off), slab.col, slab.col_base, s0, rows, ne, as<int64_t>(h->slab_off),
+                                as<int32_t>(h->slab_col), as<int32_t>(h->slab_row), s));
+      ms.direct = 0;
+      ms.nslabs = k;
+      for (int e = 0; e < ne; ++e) {
+        ms.s[e].row = as<int32_t>(h->slab_row);
+        ms.s[e].col = as<int32_t>(h->slab_col);
+        ms.s[e].count = count;
+        ms.s[e].begin_dev = as<int64_t>(h->slab_off) + static_cast<int64_t>(e) * rows;
+        ms.s[e].end_dev = as<int64_t>(h->slab_off) + static_cast<int64_t>(e + 1) * rows;
+      }
+      ms.s[ne] = max_eps;
+    }
+    DBM_TRY(launch_cc_batch(ms, count, n, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc), nb == 1,
+                            as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
+                            as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, h->union_limit, s));
+    base += count;
+  }
+  return Status::Ok();
+}
 
-  // ---- final relabel of the configs [cfg_begin, cfg_end) ----
+// Roots -> ranks -> labels of the configs [cfg_begin, cfg_end), then the device error word.
+static Status relabel_stage(dbm_handle* h, int64_t n, int k, int l, int cfg_begin, int cfg_end, int32_t* labels,
+                            dbm_stats& st, cudaStream_t s)
+{
   {
     PhaseTimer t(h, s, &st.ms_relabel);
     // roots as a bitmap (one 32-bit word per 32 points and config): the rank of a root is the
@@ -738,6 +799,7 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
     const int64_t words_all = static_cast<int64_t>(k) * l * W, owned = static_cast<int64_t>(cfg_end - cfg_begin) * W;
     DBM_TRY(ensure(h->flags, sizeof(uint32_t) * static_cast<size_t>(words_all + owned)));
     DBM_TRY(ensure(h->rank, sizeof(int64_t) * static_cast<size_t>(owned + 1)));
+    DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(owned + 1)));
     uint32_t* words = as<uint32_t>(h->flags);
     int32_t* cnt = as<int32_t>(h->flags) + words_all;
     DBM_TRY(launch_cc_root_bits(n, l, cfg_begin, cfg_end, W, as<int32_t>(h->cc), as<int32_t>(h->G), words, cnt,
@@ -746,8 +808,123 @@ static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int3
     DBM_TRY(launch_cc_labels(n, l, cfg_begin, cfg_end, W, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->cur),
                              words, as<int64_t>(h->rank), labels, s));
   }
-  DBM_TRY(read_err_flag(h, s));
-  return Status::Ok();
+  return read_err_flag(h, s);
+}
+
+// Everything after the distance pass, from the complete per-code histograms and the complete
+// list of neighbour pairs: degrees, core masks, CSR, batch plan, labelling of the configs
+// [cfg_begin, cfg_end).
+static Status label_stage(dbm_handle* h, int64_t n, int64_t d, int k, const int32_t* minpts, int l,
+                          const int32_t* hist, const uint64_t* edges, uint64_t found, int cfg_begin,
+                          int cfg_end, int32_t* labels, uint8_t* core_out, const dbm_options& opt,
+                          const Plan& plan, dbm_stats& st, std::vector<uint8_t>& routes, cudaStream_t s)
+{
+  st.unique_pairs = n * (n - 1) / 2;
+  st.edges = static_cast<int64_t>(found);
+  BatchPlan bp;
+  DBM_TRY(graph_prep(h, n, d, k, minpts, l, hist, core_out, opt, plan, st, routes, bp, s));
+  DBM_TRY(build_csr(h, n, edges, found, st, s));
+  const SlabSource whole = [&](int64_t, int64_t, int64_t, int64_t base, BatchSlab& out) {
+    out.row = as<int32_t>(h->crow) + base;
+    out.col = as<uint32_t>(h->col) + base;
+    out.col_base = base;
+    return Status::Ok();
+  };
+  DBM_TRY(label_batches(h, n, k, l, cfg_begin, cfg_end, bp, routes, st, whole, s));
+  return relabel_stage(h, n, k, l, cfg_begin, cfg_end, labels, st, s);
+}
+
+// ---- memory-bounded fit: the graph one batch at a time ----------------------------------------
+// Used when the whole max-eps pair list and CSR (24 bytes per neighbour pair, plus the per-batch
+// slabs) would exceed the budget or the free memory.  The points are re-ordered batch-major (row
+// batch, then Z-order), so the rows of batch b are the XT positions [s0, s1) and its tiles a
+// contiguous range; per batch, the tile pairs touching that range are compacted from the pruned
+// worklist, a distance pass emits only the pairs with an endpoint in the batch (the degrees are
+// already complete, so no histogram is counted again), and the batch's rows of the CSR are built
+// into buffers sized by the largest batch.  Each tile pair is evaluated by at most the two batches
+// of its tiles.  The labelling kernels see exactly the entries the one-shot CSR holds for the
+// batch, in another order, which no label depends on (min-index union-find).
+static Status streamed_labels(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps2, int k, int l,
+                              int cfg_begin, int cfg_end, int32_t* labels, const BatchPlan& bp,
+                              const std::vector<uint8_t>& routes, dbm_stats& st, cudaStream_t s)
+{
+  const int32_t di = static_cast<int32_t>(d);
+  const bool screen = n >= kOrderMinPoints && h->distance_mode != DBM_DISTANCE_EXACT && screen_supported(di, eps2[k - 1]);
+  const int32_t xt_rows = screen ? std::max(padded_dims(di), screen_rows(di)) : padded_dims(di);
+  const int64_t T = ceil_div(n, 128);
+  DBM_TRY(ensure(h->perm, sizeof(int32_t) * n));
+  DBM_TRY(ensure(h->order_scratch, order_scratch_bytes(n)));
+  DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(xt_rows) * padded_points(n)));
+  DBM_TRY(ensure(h->box_lo, sizeof(float) * static_cast<size_t>(T) * di));
+  DBM_TRY(ensure(h->box_hi, sizeof(float) * static_cast<size_t>(T) * di));
+  DBM_TRY(ensure(h->prune_scratch, prune_scratch_bytes(T, di)));
+  DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(prune_units(T) + 1)));
+  DBM_TRY(ensure(h->counters, 8 * sizeof(unsigned long long)));
+  {
+    PhaseTimer t(h, s, &st.ms_distance);
+    DBM_TRY(spatial_order(x, n, di, as<int32_t>(h->perm), h->order_scratch.p, h->order_scratch.bytes, s,
+                          static_cast<int64_t>(bp.bs)));
+    DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, as<int32_t>(h->perm), xt_rows));
+    DBM_TRY(launch_tile_boxes(as<float>(h->xt), n, padded_points(n), di, as<float>(h->box_lo), as<float>(h->box_hi), s));
+    const int64_t* count_dev = nullptr;
+    DBM_TRY(launch_prune_count(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
+                               h->prune_scratch.bytes, h->scan_scratch.p, h->scan_scratch.bytes, &count_dev, s));
+    h->pinned[0] = 0;
+    DBM_CUDA(cudaMemcpyAsync(h->pinned, count_dev, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    DBM_CUDA(cudaStreamSynchronize(s));
+    const int64_t W = std::max<int64_t>(h->pinned[0], 1);
+    DBM_TRY(ensure(h->work, sizeof(long long) * W));
+    DBM_TRY(launch_prune_write(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
+                               as<long long>(h->work), W, s));
+    h->stream_work_count = h->pinned[0];
+  }
+  const int64_t W = h->stream_work_count;
+  DBM_TRY(ensure(h->subwork, sizeof(long long) * std::max<int64_t>(W, 1)));
+  DBM_TRY(ensure(h->subflags, sizeof(int32_t) * std::max<int64_t>(W, 1)));
+  DBM_TRY(ensure(h->subpos, sizeof(int64_t) * (std::max<int64_t>(W, 1) + 1)));
+  DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(W + 1)));
+  if (screen) DBM_TRY(ensure(h->fallback, sizeof(long long) * std::max<int64_t>(W, 1)));
+  const uint64_t cap = static_cast<uint64_t>(std::max<int64_t>(bp.max_count, 1));
+  DBM_TRY(ensure(h->edges, sizeof(uint64_t) * cap));
+  DBM_TRY(ensure(h->col, sizeof(uint32_t) * cap));
+  DBM_TRY(ensure(h->crow, sizeof(int32_t) * cap));
+  st.streamed = 1;
+
+  const SlabSource per_batch = [&](int64_t, int64_t s0, int64_t rows, int64_t base, BatchSlab& out) -> Status {
+    const int64_t s1 = s0 + rows;
+    auto* ctr = as<unsigned long long>(h->counters);
+    DBM_CUDA(cudaMemsetAsync(ctr, 0, 8 * sizeof(unsigned long long), s));
+    DBM_TRY(launch_batch_worklist(as<long long>(h->work), W, s0 / 128, ceil_div(s1, 128), as<int32_t>(h->subflags),
+                                  as<int64_t>(h->subpos), h->scan_scratch.p, h->scan_scratch.bytes,
+                                  as<long long>(h->subwork), s));
+    const int64_t* sub_count = as<int64_t>(h->subpos) + W;
+    DistLaunch a{n, di, k, as<float>(h->xt), eps2, ctr, as<uint64_t>(h->edges), cap, nullptr, as<int32_t>(h->err),
+                 h->sm_count, 0, 1, as<int32_t>(h->perm), as<long long>(h->subwork), 0};
+    a.keep_lo = s0;
+    a.keep_hi = s1;
+    if (screen) {
+      a.work_total_dev = sub_count;
+      a.work_cap = W;
+      DBM_TRY(launch_screened_distance(a, as<float>(h->box_lo), as<float>(h->box_hi), as<long long>(h->fallback), s));
+      DistLaunch f = a;
+      f.work = as<long long>(h->fallback);
+      f.work_count_dev = ctr + 5;
+      DBM_TRY(launch_distance(f, s));
+    } else {
+      a.work_count_dev = reinterpret_cast<const unsigned long long*>(sub_count);
+      DBM_TRY(launch_distance(a, s));
+    }
+    DBM_CUDA(cudaMemsetAsync(h->fill.p, 0, sizeof(int32_t) * rows, s));
+    DBM_TRY(launch_csr_scatter_batch(as<uint64_t>(h->edges), static_cast<int64_t>(cap), ctr, as<int64_t>(h->off), s0,
+                                     s1, as<int32_t>(h->fill), as<uint32_t>(h->col), as<int32_t>(h->crow),
+                                     as<int32_t>(h->err), s));
+    out.row = as<int32_t>(h->crow);
+    out.col = as<uint32_t>(h->col);
+    out.col_base = base;
+    return Status::Ok();
+  };
+  DBM_TRY(label_batches(h, n, k, l, cfg_begin, cfg_end, bp, routes, st, per_batch, s));
+  return relabel_stage(h, n, k, l, cfg_begin, cfg_end, labels, st, s);
 }
 
 static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps, int k,
@@ -764,10 +941,45 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
   DBM_TRY(ensure(h->hist, sizeof(int32_t) * static_cast<size_t>(k) * n));
   const uint64_t hint = static_cast<uint64_t>(n) *
                         static_cast<uint64_t>(opt.neigh_per_row > 0 ? opt.neigh_per_row : 16) / 2 + 1024;
-  uint64_t found = 0;
-  DBM_TRY(distance_stage(h, x, n, d, eps2, k, 0, 1, as<int32_t>(h->hist), hint, &found, st, s));
-  return label_stage(h, n, d, k, minpts, l, as<int32_t>(h->hist), as<uint64_t>(h->edges), found, 0, k * l,
-                     labels, core_out, opt, plan, st, routes, s);
+  uint64_t found = 0, cap = 0;
+  const bool forced = h->graph_mode == DBM_GRAPH_STREAMED;
+  DBM_TRY(distance_stage(h, x, n, d, eps2, k, 0, 1, as<int32_t>(h->hist), forced ? 0 : hint, &found, st, s,
+                         /*regrow=*/false, &cap));
+  st.unique_pairs = n * (n - 1) / 2;
+  st.edges = static_cast<int64_t>(found);
+  BatchPlan bp;
+  DBM_TRY(graph_prep(h, n, d, k, minpts, l, as<int32_t>(h->hist), core_out, opt, plan, st, routes, bp, s));
+  bool stream = forced;
+  if (!stream && h->graph_mode == DBM_GRAPH_AUTO) {
+    // the whole pair list (when it outgrew its buffer), the whole CSR and the slabs are held
+    // only if what they add to the workspace fits the budget and the free memory; otherwise the
+    // graph is built one batch at a time
+    size_t free_b = 0, total_b = 0;
+    DBM_TRY(free_memory(h, &free_b, &total_b));
+    const uint64_t ws = h->workspace_bytes();
+    auto grow = [](uint64_t want, const Buffer& b) { return want > b.bytes ? want - b.bytes : uint64_t(0); };
+    const uint64_t slabs = slab_bytes(bp, routes, k, l, 0);
+    const uint64_t need = (found > cap ? grow(8 * found, h->edges) : 0) + grow(8 * found, h->col) +
+                          grow(8 * found, h->crow) + grow(slabs, h->slab_col) / 2 + grow(slabs, h->slab_row) / 2;
+    const uint64_t room = std::min<uint64_t>(plan.budget > ws ? plan.budget - ws : 0, free_b);
+    stream = need > room;
+  }
+  if (stream) return streamed_labels(h, x, n, d, eps2, k, l, 0, k * l, labels, bp, routes, st, s);
+  if (found > cap) {
+    // one more pass with a pair buffer of the exact size (the histograms come out identical)
+    const int32_t passes = st.distance_passes;
+    DBM_TRY(distance_stage(h, x, n, d, eps2, k, 0, 1, as<int32_t>(h->hist), found, &found, st, s));
+    st.distance_passes += passes;
+  }
+  DBM_TRY(build_csr(h, n, as<uint64_t>(h->edges), found, st, s));
+  const SlabSource whole = [&](int64_t, int64_t, int64_t, int64_t base, BatchSlab& out) {
+    out.row = as<int32_t>(h->crow) + base;
+    out.col = as<uint32_t>(h->col) + base;
+    out.col_base = base;
+    return Status::Ok();
+  };
+  DBM_TRY(label_batches(h, n, k, l, 0, k * l, bp, routes, st, whole, s));
+  return relabel_stage(h, n, k, l, 0, k * l, labels, st, s);
 }
 
 static dbm_options default_options()
@@ -828,7 +1040,7 @@ void dbm_destroy(dbm_handle* h)
                         &h->slab_off, &h->slab_col, &h->slab_row, &h->G, &h->L, &h->best, &h->cur,
                         &h->flags, &h->rank, &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev,
                         &h->core_dev, &h->perm, &h->order_scratch, &h->box_lo, &h->box_hi,
-                        &h->prune_scratch, &h->work, &h->fallback};
+                        &h->prune_scratch, &h->work, &h->fallback, &h->subwork, &h->subflags, &h->subpos};
   for (auto* b : all)
     if (b->p) cudaFree(b->p);
   if (h->pinned) cudaFreeHost(h->pinned);
@@ -868,6 +1080,13 @@ int dbm_core_sample_indices(dbm_handle* h, const uint8_t* core_dev, int64_t n, i
   return r.code;
 }
 
+int dbm_set_graph_mode(dbm_handle* h, int mode)
+{
+  if (!h || mode < DBM_GRAPH_AUTO || mode > DBM_GRAPH_STREAMED) return DBM_ERR_INVALID;
+  h->graph_mode = mode;
+  return DBM_OK;
+}
+
 int dbm_set_union_retry_limit(dbm_handle* h, int limit)
 {
   if (!h || limit < 0) return DBM_ERR_INVALID;
@@ -900,6 +1119,7 @@ int dbm_fit_multi(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const
   dbm::Status r = dbm::fit(h, x_dev, n, d, eps_host, k, min_pts_host, l, labels_dev, core_dev, o, st,
                            routes, s);
   st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
+  st.workspace_bytes = h->workspace_bytes();
   if (r.ok()) {
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) r = dbm::Status::Err(DBM_ERR_CUDA, cudaGetErrorString(e));
@@ -999,6 +1219,7 @@ int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, 
     r = dbm::distance_stage(h, x_dev, n, d, eps2, k, shard, nshards, hist_dev, edge_cap, &found, st, s);
     dbm::resolve_phase_timers(h);
     st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
+    st.workspace_bytes = h->workspace_bytes();
     if (stats) *stats = st;
     if (r.ok()) {
       *edges_found = found;
@@ -1049,6 +1270,7 @@ int dbm_fit_multi_from_graph(dbm_handle* h, int64_t n, int64_t d, const float* e
   }
   dbm::resolve_phase_timers(h);
   st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
+  st.workspace_bytes = h->workspace_bytes();
   if (stats) *stats = st;
   if (batch_routes && routes_len > 0) {  // the batches only: the tail is left untouched
     const int nr = std::min(routes_len, static_cast<int>(routes.size()));

@@ -46,6 +46,7 @@ constexpr int32_t kNone = INT32_MAX;       // "no label yet" / noise before rela
 constexpr int kErrTmaTimeout = 1;
 constexpr int kErrUnionLimit = 2;
 constexpr int kErrNonFinite = 4;
+constexpr int kErrGraphMismatch = 8;  // a batch's re-derived pairs disagree with the degree pass
 
 // ---- small device helpers ----------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p)
@@ -185,7 +186,17 @@ struct DistLaunch {
   const int64_t* work_total_dev = nullptr;  // screened pass: the worklist length on the device
   int64_t work_cap = 0;                     // (entries beyond work_cap were not written); each
                                             // shard's slice is computed on the device
+  // Memory-bounded fit: only pairs with an endpoint at an XT position in [keep_lo, keep_hi) are
+  // emitted (hist == nullptr then: the degrees are already known and are not counted again).
+  int64_t keep_lo = 0;
+  int64_t keep_hi = INT64_MAX;
 };
+
+// An emitted pair needs one endpoint (XT positions pi, pj) in [lo, hi).
+__device__ __forceinline__ bool keep_pair(int64_t pi, int64_t pj, int64_t lo, int64_t hi)
+{
+  return (pi >= lo && pi < hi) || (pj >= lo && pj < hi);
+}
 
 // Screened distance pass (dist_tc.cu): tensor-core bound + exact chain for the candidates;
 // tile pairs it cannot screen are appended to `fallback` (count in counters[5]) for

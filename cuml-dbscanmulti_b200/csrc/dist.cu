@@ -56,6 +56,7 @@ struct DistParams {
   const float* xt;                   // dp x npad (for re-evaluating neighbour pairs)
   int64_t npad;
   const int32_t* perm;               // original index of each XT column (nullptr: identity)
+  int64_t keep_lo, keep_hi;          // emit only pairs with an endpoint in [keep_lo, keep_hi)
   float eps2[kMaxEps];
 };
 
@@ -264,7 +265,8 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
             for (int h = 0; h < 2; ++h) {
               const int j = 2 * jp + h;
               const int32_t gj = col0 + ((j < 4) ? (tx * 4 + j) : (64 + tx * 4 + j - 4));
-              const bool hit = (gi < n32) && (gj < n32) && (!diag || gj > gi) && (w[h] <= cutoff);
+              const bool hit = (gi < n32) && (gj < n32) && (!diag || gj > gi) && (w[h] <= cutoff) &&
+                               keep_pair(gi, gj, p.keep_lo, p.keep_hi);
               nb |= static_cast<uint64_t>(hit) << (i * 8 + j);
             }
           }
@@ -317,9 +319,11 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
             p.edges[idx] = (static_cast<uint64_t>(lo) << 32) |
                            (static_cast<uint64_t>(code) << kCodeShift) | static_cast<uint64_t>(hi);
           ++idx;
-          int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
-          atomicAdd(hrow + oi, 1);
-          atomicAdd(hrow + oj, 1);
+          if (p.hist) {
+            int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
+            atomicAdd(hrow + oi, 1);
+            atomicAdd(hrow + oj, 1);
+          }
         }
       }
 #pragma unroll
@@ -504,6 +508,8 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   p.xt = a.xt;
   p.npad = npad;
   p.perm = a.perm;
+  p.keep_lo = a.keep_lo;
+  p.keep_hi = a.keep_hi;
   for (int e = 0; e < kMaxEps; ++e) p.eps2[e] = e < a.k ? a.eps2[e] : a.eps2[a.k - 1];
 
   const size_t smem = dist_smem_bytes(dbox);

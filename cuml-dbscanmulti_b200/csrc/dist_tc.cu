@@ -96,6 +96,7 @@ struct ScreenParams {
   const float* box_hi;
   int64_t tiles;
   long long* fallback;
+  int64_t keep_lo, keep_hi;  // emit only pairs with an endpoint at an XT position in [keep_lo, keep_hi)
   float sqrt_e;         // s of the bound, rounded up
   float eps2[kMaxEps];
 };
@@ -401,9 +402,11 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
       if (idx < p.edge_cap)
         p.edges[idx] = (static_cast<uint64_t>(lo) << 32) | (static_cast<uint64_t>(code) << kCodeShift) |
                        static_cast<uint64_t>(hi);
-      int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
-      atomicAdd(hrow + oi, 1);
-      atomicAdd(hrow + oj, 1);
+      if (p.hist) {
+        int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
+        atomicAdd(hrow + oi, 1);
+        atomicAdd(hrow + oj, 1);
+      }
     }
   };
 
@@ -558,7 +561,7 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
               const float diff = __fsub_rn(xr[t], xjt);
               w = __fmaf_rn(diff, diff, w);
             }
-            if (w <= cutoff) {
+            if (w <= cutoff && keep_pair(I * kScreenTile + tid, J * kScreenTile + j, p.keep_lo, p.keep_hi)) {
               int code = 0;
               while (w > s_eps2[code]) ++code;
               const int q = atomicAdd(&s_hits[par], 1);
@@ -688,6 +691,8 @@ Status launch_screened_distance(const DistLaunch& a, const float* box_lo, const 
   p.box_hi = box_hi;
   p.tiles = ceil_div(a.n, kScreenTile);
   p.fallback = fallback;
+  p.keep_lo = a.keep_lo;
+  p.keep_hi = a.keep_hi;
   for (int e = 0; e < kMaxEps; ++e) p.eps2[e] = e < a.k ? a.eps2[e] : a.eps2[a.k - 1];
   {
     const double e = static_cast<double>(a.eps2[a.k - 1]) * (1.0 + (a.d + 3) * std::ldexp(1.0, -24));

@@ -209,6 +209,102 @@ Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, 
   return Status::Ok();
 }
 
+// The rows [s0, s1) of the max-eps CSR only, from neighbour pairs that each have at least one
+// endpoint in the batch (memory-bounded fit): entry positions are relative to off[s0], fill holds
+// one cursor per batch row.
+__global__ void csr_scatter_batch_kernel(const uint64_t* __restrict__ edges, int64_t cap,
+                                         const unsigned long long* __restrict__ m_dev,
+                                         const int64_t* __restrict__ off, int64_t s0, int64_t s1,
+                                         int32_t* __restrict__ fill, uint32_t* __restrict__ col,
+                                         int32_t* __restrict__ row, int32_t* __restrict__ err)
+{
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t m = static_cast<int64_t>(*m_dev) < cap ? static_cast<int64_t>(*m_dev) : cap;
+  if (q >= m) return;
+  const uint64_t w = edges[q];
+  const uint32_t i = static_cast<uint32_t>(w >> 32);
+  const uint32_t lo = static_cast<uint32_t>(w);
+  const uint32_t j = lo & kColMask;
+  const uint32_t code = lo & ~kColMask;
+  const int64_t base = off[s0];
+  // a row never receives more entries than its degree (same pairs as the degree pass); the
+  // checks keep every write inside the buffers all the same and report a violation
+  if (i >= s0 && i < s1) {
+    const int32_t k = atomicAdd(fill + (i - s0), 1);
+    const int64_t qi = off[i] - base + k;
+    if (qi < off[i + 1] - base && qi < cap) {
+      col[qi] = code | j;
+      row[qi] = static_cast<int32_t>(i);
+    } else {
+      atomicOr(err, kErrGraphMismatch);
+    }
+  }
+  if (j >= s0 && j < s1) {
+    const int32_t k = atomicAdd(fill + (j - s0), 1);
+    const int64_t qj = off[j] - base + k;
+    if (qj < off[j + 1] - base && qj < cap) {
+      col[qj] = code | i;
+      row[qj] = static_cast<int32_t>(j);
+    } else {
+      atomicOr(err, kErrGraphMismatch);
+    }
+  }
+}
+
+// m_dev: the number of pairs (the distance pass's cursor, read on the device), at most cap.
+Status launch_csr_scatter_batch(const uint64_t* edges, int64_t cap, const unsigned long long* m_dev, const int64_t* off,
+                                int64_t s0, int64_t s1, int32_t* fill, uint32_t* col, int32_t* row, int32_t* err,
+                                cudaStream_t s)
+{
+  if (cap <= 0) return Status::Ok();
+  count_launch();
+  csr_scatter_batch_kernel<<<static_cast<unsigned>(ceil_div(cap, 256)), 256, 0, s>>>(edges, cap, m_dev, off, s0, s1,
+                                                                                     fill, col, row, err);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// ---- the tile pairs of one row batch (memory-bounded fit) ----------------------------------
+// flags[q] = 1 iff worklist entry q (J << 32 | I) has tile I or tile J in [t0, t1)
+__global__ void work_flags_kernel(const long long* __restrict__ work, int64_t count, int64_t t0, int64_t t1,
+                                  int32_t* __restrict__ flags)
+{
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= count) return;
+  const long long e = work[q];
+  const int64_t I = e & 0xffffffffLL, J = e >> 32;
+  flags[q] = ((I >= t0 && I < t1) || (J >= t0 && J < t1)) ? 1 : 0;
+}
+
+// order-preserving compaction: out[pos[q]] = work[q] for flagged q
+__global__ void work_compact_kernel(const long long* __restrict__ work, int64_t count,
+                                    const int32_t* __restrict__ flags, const int64_t* __restrict__ pos,
+                                    long long* __restrict__ out)
+{
+  const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (q >= count) return;
+  if (flags[q]) out[pos[q]] = work[q];
+}
+
+// The worklist entries touching tiles [t0, t1), in worklist order; *pos_out + count is the
+// device word holding their number.
+Status launch_batch_worklist(const long long* work, int64_t count, int64_t t0, int64_t t1, int32_t* flags,
+                             int64_t* pos, void* scan_scratch, size_t scan_bytes, long long* out, cudaStream_t s)
+{
+  if (count <= 0) {
+    DBM_CUDA(cudaMemsetAsync(pos, 0, sizeof(int64_t), s));
+    return Status::Ok();
+  }
+  count_launch();
+  work_flags_kernel<<<static_cast<unsigned>(ceil_div(count, 256)), 256, 0, s>>>(work, count, t0, t1, flags);
+  DBM_CUDA(cudaGetLastError());
+  DBM_TRY(exclusive_scan_i32(flags, pos, count, scan_scratch, scan_bytes, s));
+  count_launch();
+  work_compact_kernel<<<static_cast<unsigned>(ceil_div(count, 256)), 256, 0, s>>>(work, count, flags, pos, out);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
 // per-batch nnz at the largest eps, self pairs included (the reference's vd[n_points])
 __global__ void batch_nnz_kernel(const int64_t* __restrict__ off, int64_t n, int64_t bs, int64_t nb,
                                  int64_t* __restrict__ out)
@@ -241,9 +337,10 @@ __global__ void slab_counts_all_kernel(const int32_t* __restrict__ deg, int64_t 
 }
 
 // One warp per batch row: one pass over its max-eps entries writes every smaller-eps slab e
-// (entries with code <= e), order-preserving, at off_flat[e*rows + r].
-__global__ void filter_all_kernel(const int64_t* __restrict__ off, const uint32_t* __restrict__ col, int64_t s0,
-                                  int64_t rows, int ne, const int64_t* __restrict__ off_flat,
+// (entries with code <= e), order-preserving, at off_flat[e*rows + r].  Entry q of the max-eps
+// CSR is col[q - col_base] (col_base = off[s0] when col holds only this batch's rows).
+__global__ void filter_all_kernel(const int64_t* __restrict__ off, const uint32_t* __restrict__ col, int64_t col_base,
+                                  int64_t s0, int64_t rows, int ne, const int64_t* __restrict__ off_flat,
                                   int32_t* __restrict__ col_flat, int32_t* __restrict__ row_flat)
 {
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -260,7 +357,7 @@ __global__ void filter_all_kernel(const int64_t* __restrict__ off, const uint32_
       const int64_t q = q0 + lane;
       uint32_t code = 0xffu, j = 0;
       if (q < end) {
-        const uint32_t w = col[q];
+        const uint32_t w = col[q - col_base];
         code = w >> kCodeShift;
         j = w & kColMask;
       }
@@ -286,13 +383,13 @@ Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0,
   return Status::Ok();
 }
 
-Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t s0, int64_t rows, int ne,
+Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t col_base, int64_t s0, int64_t rows, int ne,
                          const int64_t* off_flat, int32_t* col_flat, int32_t* row_flat, cudaStream_t s)
 {
   if (ne <= 0 || rows <= 0) return Status::Ok();
   count_launch();
-  filter_all_kernel<<<static_cast<unsigned>(ceil_div(rows * 32, 256)), 256, 0, s>>>(off, col, s0, rows, ne, off_flat,
-                                                                                  col_flat, row_flat);
+  filter_all_kernel<<<static_cast<unsigned>(ceil_div(rows * 32, 256)), 256, 0, s>>>(off, col, col_base, s0, rows, ne,
+                                                                                  off_flat, col_flat, row_flat);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }

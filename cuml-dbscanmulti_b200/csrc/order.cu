@@ -87,36 +87,66 @@ __global__ void morton_kernel(const float* __restrict__ x, int64_t n, int32_t d,
   val[i] = static_cast<int32_t>(i);
 }
 
-size_t order_scratch_bytes(int64_t n)
+// Batch-major variant: key = (row batch of the original index) << 32 | Morton code, so the points
+// of row batch b occupy exactly positions [b * batch_rows, (b + 1) * batch_rows) of the order,
+// Z-ordered among themselves (the memory-bounded fit evaluates one batch's tile range at a time).
+__global__ void batch_key_kernel(const uint32_t* __restrict__ morton, int64_t n, int64_t batch_rows,
+                                 unsigned long long* __restrict__ key)
 {
-  size_t temp = 0;
-  cub::DeviceRadixSort::SortPairs(nullptr, temp, static_cast<const uint32_t*>(nullptr),
-                                  static_cast<uint32_t*>(nullptr), static_cast<const int32_t*>(nullptr),
-                                  static_cast<int32_t*>(nullptr), static_cast<int>(n));
-  // keys in/out + values in + the sort's temporary storage + the bounding box
-  return align_up(sizeof(uint32_t) * n, 256) * 3 + align_up(temp, 256) + 256;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  key[i] = (static_cast<unsigned long long>(i / batch_rows) << 32) | morton[i];
 }
 
-// perm[r] = original index of the r-th point in Z-order of the leading coordinates.
+size_t order_scratch_bytes(int64_t n)
+{
+  size_t temp32 = 0, temp64 = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, temp32, static_cast<const uint32_t*>(nullptr),
+                                  static_cast<uint32_t*>(nullptr), static_cast<const int32_t*>(nullptr),
+                                  static_cast<int32_t*>(nullptr), static_cast<int>(n));
+  cub::DeviceRadixSort::SortPairs(nullptr, temp64, static_cast<const unsigned long long*>(nullptr),
+                                  static_cast<unsigned long long*>(nullptr), static_cast<const int32_t*>(nullptr),
+                                  static_cast<int32_t*>(nullptr), static_cast<int>(n));
+  // 32-bit keys in/out + values in + two 64-bit key arrays (batch-major order) + the sort's
+  // temporary storage + the bounding box
+  return align_up(sizeof(uint32_t) * n, 256) * 3 + align_up(sizeof(unsigned long long) * n, 256) * 2 +
+         align_up(std::max(temp32, temp64), 256) + 256;
+}
+
+// perm[r] = original index of the r-th point in Z-order of the leading coordinates; with
+// batch_rows > 0, batch-major: row batch first (original index / batch_rows), then Z-order.
 Status spatial_order(const float* x, int64_t n, int32_t d, int32_t* perm, void* scratch, size_t scratch_bytes,
-                     cudaStream_t s)
+                     cudaStream_t s, int64_t batch_rows)
 {
   if (scratch_bytes < order_scratch_bytes(n)) return Status::Err(DBM_ERR_INVALID, "order scratch too small");
   const int m = d < 4 ? d : 4;
   unsigned char* p = static_cast<unsigned char*>(scratch);
   const size_t kb = align_up(sizeof(uint32_t) * n, 256);
+  const size_t kb64 = align_up(sizeof(unsigned long long) * n, 256);
   uint32_t* keys_in = reinterpret_cast<uint32_t*>(p);
   uint32_t* keys_out = reinterpret_cast<uint32_t*>(p + kb);
   int32_t* vals_in = reinterpret_cast<int32_t*>(p + 2 * kb);
-  uint32_t* lohi = reinterpret_cast<uint32_t*>(p + 3 * kb);
-  void* temp = p + 3 * kb + 256;
-  size_t temp_bytes = scratch_bytes - 3 * kb - 256;
+  unsigned long long* bkeys_in = reinterpret_cast<unsigned long long*>(p + 3 * kb);
+  unsigned long long* bkeys_out = reinterpret_cast<unsigned long long*>(p + 3 * kb + kb64);
+  uint32_t* lohi = reinterpret_cast<uint32_t*>(p + 3 * kb + 2 * kb64);
+  void* temp = p + 3 * kb + 2 * kb64 + 256;
+  size_t temp_bytes = scratch_bytes - 3 * kb - 2 * kb64 - 256;
   count_launch(3);
   bbox_init_kernel<<<1, 32, 0, s>>>(lohi);
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(ceil_div(n, 256), 1184));
   bbox_kernel<<<blocks, 256, 0, s>>>(x, n, d, m, lohi);
   morton_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(x, n, d, m, lohi, keys_in, vals_in);
   DBM_CUDA(cudaGetLastError());
+  if (batch_rows > 0) {
+    count_launch();
+    batch_key_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(keys_in, n, batch_rows, bkeys_in);
+    DBM_CUDA(cudaGetLastError());
+    int end_bit = 33;  // batch ids below 2^(end_bit - 32)
+    while ((int64_t(1) << (end_bit - 32)) <= ceil_div(n, batch_rows)) ++end_bit;
+    DBM_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, bkeys_in, bkeys_out, vals_in, perm,
+                                             static_cast<int>(n), 0, end_bit, s));
+    return Status::Ok();
+  }
   DBM_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, perm,
                                            static_cast<int>(n), 0, 32, s));
   return Status::Ok();

@@ -52,13 +52,14 @@ MAX_EPS = 16
 
 # every symbol include/dbm.h declares
 DISTANCE_MODES = {"auto": 0, "exact": 1, "screened": 2}
+GRAPH_MODES = {"auto": 0, "oneshot": 1, "streamed": 2}
 
 EXPORTED = (
     "dbm_create", "dbm_destroy", "dbm_workspace_bytes", "dbm_set_phase_timing", "dbm_set_distance_mode", "dbm_core_sample_indices",
     "dbm_fit_multi", "dbm_fit_multi_host", "dbm_neighbor_counts", "dbm_batch_size", "dbm_max_bytes_for_batch_size",
     "dbm_annotate_pays", "dbm_auto_index_bits", "dbm_build_info_json",
     "dbm_neighbor_counts_noalloc", "dbm_distance_shard", "dbm_fit_multi_from_graph",
-    "dbm_set_union_retry_limit",
+    "dbm_set_union_retry_limit", "dbm_set_graph_mode",
 )
 
 
@@ -106,6 +107,9 @@ class Stats(ctypes.Structure):
         ("fallback_tile_pairs", ctypes.c_int64),
         ("screen_candidates", ctypes.c_int64),
         ("ms_screen", ctypes.c_double),
+        ("streamed", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("workspace_bytes", ctypes.c_uint64),
     ]
 
     def as_dict(self) -> dict[str, Any]:
@@ -135,6 +139,8 @@ def load_library():
     lib.dbm_set_phase_timing.restype = None
     lib.dbm_set_distance_mode.argtypes = [p, i32]
     lib.dbm_set_distance_mode.restype = i32
+    lib.dbm_set_graph_mode.argtypes = [p, i32]
+    lib.dbm_set_graph_mode.restype = i32
     lib.dbm_set_union_retry_limit.argtypes = [p, i32]
     lib.dbm_set_union_retry_limit.restype = i32
     lib.dbm_core_sample_indices.argtypes = [p, p, i64, i32, p, p, cp, sz]
@@ -280,6 +286,13 @@ class DbscanMulti:
         rc = self._lib.dbm_set_distance_mode(self._h, DISTANCE_MODES[mode])
         if rc != DBM_OK:
             raise DbmError(rc, f"bad distance mode {mode!r}")
+
+    def set_graph_mode(self, mode: str) -> None:
+        """'auto' (the whole graph at once when it fits the budget and the free memory, else one
+        row batch at a time), 'oneshot' or 'streamed'.  Labels are identical in every mode."""
+        rc = self._lib.dbm_set_graph_mode(self._h, GRAPH_MODES[mode])
+        if rc != DBM_OK:
+            raise DbmError(rc, f"bad graph mode {mode!r}")
 
     def set_union_retry_limit(self, limit: int) -> None:
         """Test knob: the retry bound of every union-find hook (default 2**20; 0 makes the

@@ -109,6 +109,9 @@ typedef struct dbm_stats {
   int64_t fallback_tile_pairs;  /* of those and the unscreenable ones, handed to the exact tile kernel */
   int64_t screen_candidates;    /* pairs the screen could not exclude (each re-evaluated exactly) */
   double ms_screen;             /* device time of the screened-pass kernel alone, if timing enabled */
+  int32_t streamed;             /* 1: the graph was built one row batch at a time (memory-bounded) */
+  int32_t reserved0;
+  uint64_t workspace_bytes;     /* the handle's device workspace after the call */
 } dbm_stats;
 
 typedef struct dbm_handle dbm_handle;
@@ -134,6 +137,21 @@ void dbm_set_phase_timing(dbm_handle* h, int enabled);
 #define DBM_DISTANCE_EXACT 1
 #define DBM_DISTANCE_SCREENED 2
 int dbm_set_distance_mode(dbm_handle* h, int mode);
+
+/* How the neighbour graph is held (the reference always rebuilds it per row batch, bounded by
+ * its memory budget, runner_multi.cuh:1020-1041, 1100-1226).  AUTO: one pass writes every
+ * neighbour pair and the whole max-eps CSR is built at once (24 bytes per neighbour pair) when
+ * that, with the per-batch slabs, fits both the budget (dbm_options.max_bytes_per_batch, or its
+ * automatic value) and the free device memory; otherwise the fit is memory-bounded: the degrees
+ * come from the first pass, then each row batch's pairs are re-derived by a distance pass over the
+ * tile pairs touching that batch and its rows of the CSR built into buffers sized by the largest
+ * batch.  ONESHOT / STREAMED force one or the other (tests).  Labels are identical in every mode;
+ * dbm_stats.streamed reports which ran.  dbm_distance_shard / dbm_fit_multi_from_graph always
+ * hold the whole graph. */
+#define DBM_GRAPH_AUTO 0
+#define DBM_GRAPH_ONESHOT 1
+#define DBM_GRAPH_STREAMED 2
+int dbm_set_graph_mode(dbm_handle* h, int mode);
 
 /* Test knob (fault injection without a GPU fault, like the reference's thread-local test knobs
  * csr_teto_de_teste / rota_forcada, runner_multi.cuh:145-160, 426-430): the retry bound of every

@@ -12,7 +12,7 @@ neighbour lists in memory) on every host core.
     python tests/golden/make_full_size_fixtures.py [c1 c2 ...]     # default: all workloads
 
 Each workload is written as soon as it finishes (existing entries of other workloads are kept).
-Rough cost on 8 cores: c1, c2 seconds; c5 2 min; c3 ~6 min; c5q ~15 min; c4 ~25 min.
+Rough cost on 8 cores: c1, c2 seconds; c5 2 min; c3 7 min; c5q, c5qb 5 min; c4 ~25 min.
 """
 
 from __future__ import annotations
@@ -88,4 +88,4 @@ def main(names: list[str]) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1:] or ["c1", "c2", "c5", "c3", "c5q", "c4"])
+    main(sys.argv[1:] or ["c1", "c2", "c5", "c3", "c5q", "c4", "c5qb"])
