@@ -342,18 +342,19 @@ def e2e_leg(h, pts, eps, ms, kw, labels, flush, steps, ws, dev, torch, dist, pai
 
 
 def e2e_leg_sharded(one_fit, x, pts, labels, flush, steps, rank, dev, torch, dist, pairs, ws):
-    """Sharded e2e: every rank copies the pinned points in, the sharded fit runs, rank 0 copies
-    the gathered labels out; wall clock per step, max over ranks."""
+    """Sharded e2e through dbscan_multi.parallel.sharded_fit_multi with host points: each rank
+    copies its 1/G row slice from pinned memory and the points are all-gathered over NCCL, the
+    sharded fit runs, rank 0 copies the gathered labels out; wall clock per step, max over ranks."""
     xp = torch.from_numpy(pts).pin_memory()
     lab_host = torch.empty(tuple(labels.shape), dtype=torch.int32).pin_memory()
+    one_fit(xp)
     ts = []
     for _ in range(steps):
         flush.zero_()
         torch.cuda.synchronize()
         dist.barrier()
         t0 = time.perf_counter()
-        x.copy_(xp, non_blocking=True)
-        one_fit()
+        one_fit(xp)
         if rank == 0:
             lab_host.copy_(labels, non_blocking=True)
         torch.cuda.synchronize()
@@ -471,6 +472,29 @@ def exact_roofline(stats, unique_pairs, d, dms, sm_mhz, torch, dev, args, ws) ->
                           "executed_fraction; under this accounting the ceiling is 75% of the FMA-counted peak"}
 
 
+def label_roofline(nnz_eps, n, l, stats, label_ms, ws) -> dict:
+    """HBM roofline of the labelling (per-batch compaction, batched connected components, border
+    fold, relabel).  Algorithmic bytes per grid, the CC accounting of one sweep per configuration
+    (a column index and a label gather per entry, the labels read and written, the core mask):
+    sum over configs of 8 * nnz(eps of the config) + 8 N + N / 8; plus, on annotated batches, the
+    compaction's 4 bytes read per max-eps entry and 8 bytes written per kept smaller-eps entry.
+    Over the phase's event time (the labelling kernels' share of the step)."""
+    mp = measured_peaks()
+    peak = mp.get("hbm_gbs") or 6650.0
+    bytes_cc = sum(l * (8.0 * v + 8.0 * n + n / 8.0) for v in nnz_eps)
+    annotated = int(stats.get("annotated_batches", 0) or 0) > 0
+    bytes_compact = (4.0 * nnz_eps[-1] + 8.0 * sum(nnz_eps[:-1])) if annotated and len(nnz_eps) > 1 else 0.0
+    ms = float(np.mean(label_ms)) if label_ms else float("nan")
+    achieved = (bytes_cc + bytes_compact) / (ms * 1e-3) / 1e9 if ms and ms > 0 else None
+    return {"bound": "hbm", "kernels": "filter_all, cc_touch/union/best/border, cc_root_bits/labels",
+            "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak if achieved else None,
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs" if mp.get("hbm_gbs") else "fallback 6650 GB/s",
+            "bytes_per_grid": bytes_cc + bytes_compact, "ms_per_grid": ms, "traffic": None,
+            "note": "the union-find gathers are latency-bound and mostly L2-resident, so the phase runs far "
+                    "below the HBM roofline; on several GPUs this is the rank's own share"
+                    + (" (max over ranks not taken)" if ws > 1 else "")}
+
+
 def label_checks(args, labels, one_fit, h, x, eps, ms, kw, ws, rank, dev, torch, dist) -> dict:
     """One untimed fit, then (N > 1) its labels against a one-GPU fit of the same inputs and
     budget on rank 0, and (full-size workloads) against the oracle's per-configuration SHA-256
@@ -556,25 +580,31 @@ def main() -> None:
         stages = parallel.DeviceStages(h)
         if "max_bytes_per_batch" not in kw:
             kw["max_bytes_per_batch"] = stages.default_budget()
-        dist_ms_box = []
+        # budget and CSR memory cap agreed once (one collective), not in every step
+        limits = parallel.agree_limits(stages, kw["max_bytes_per_batch"], 0, device=dev)
+        dist_events = []
         orig_shard = stages.distance_shard
 
         def timed_shard(*a, **k2):
+            # events around the distance stage, read after the step (no extra synchronisation)
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             out = orig_shard(*a, **k2)
             e1.record(stream)
-            e1.synchronize()
-            dist_ms_box.append(e0.elapsed_time(e1))
+            dist_events.append((e0, e1))
             return out
 
         stages.distance_shard = timed_shard
 
-        def one_fit():
-            r = parallel.sharded_fit_multi(stages, x, eps, ms, **kw)
+        def one_fit(x_in=None):
+            r = parallel.sharded_fit_multi(stages, x if x_in is None else x_in, eps, ms, limits=limits,
+                                           device=None if x_in is None else dev, **kw)
             labels.copy_(r.labels)
-            r.stats["ms_distance"] = dist_ms_box[-1]
+            e0, e1 = dist_events.pop()
+            e1.synchronize()
+            dist_events.clear()
+            r.stats["ms_distance"] = e0.elapsed_time(e1)
             sh = stages.last_shard_stats
             for key in ("ms_screen", "screened_tile_pairs", "fallback_tile_pairs", "screen_candidates",
                         "tile_pairs_kept", "dist_work_fraction"):
@@ -597,6 +627,7 @@ def main() -> None:
     # correctness before timing: the sharded labels against a one-GPU fit, and the labels against
     # the oracle's digests of this workload (tests/golden/full_size_labels.json, full size only)
     checks = label_checks(args, labels, one_fit, h, x, eps, ms, kw, ws, rank, dev, torch, dist)
+    label_ms = []
 
     times, dist_ms, screen_ms, stats = [], [], [], None
     torch.cuda.synchronize()
@@ -613,6 +644,7 @@ def main() -> None:
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
         dist_ms.append(r.stats["ms_distance"])
+        label_ms.append((r.stats.get("ms_label") or 0.0) + (r.stats.get("ms_relabel") or 0.0))
         screen_ms.append(r.stats.get("ms_screen", 0.0))
         stats = r.stats
     torch.cuda.synchronize()
@@ -620,6 +652,8 @@ def main() -> None:
     if ws > 1:
         dist.barrier()
     clk = clocks.stop()
+    # per-eps directed neighbour entries (self pairs excluded), for the labelling roofline
+    nnz_eps = [int(v) for v in list(stats.get("nnz_per_eps", []))[:k]]
     total_ms = float(np.sum(times))
     rank_spread = None
     if ws > 1:
@@ -694,10 +728,15 @@ def main() -> None:
             "roofline": roofline,
             "e2e": None if e2e_value is None else {
                 "value": e2e_value, "unit": "pairs/s",
-                "h2d_bytes_per_step": int(n * d * 4), "d2h_bytes_per_step": int(k * l * n * 4),
+                # per rank: its 1/G slice of the points in (the rest arrives over NVLink); rank 0
+                # copies the labels out
+                "h2d_bytes_per_step": int(-(-n // ws) * d * 4), "d2h_bytes_per_step": int(k * l * n * 4),
                 "ms_per_step": e2e_s / args.steps * 1e3},
             "graph": {"edges": stats["edges"], "total_nnz_max_eps": stats["total_nnz_max_eps"],
-                      "distance_passes": stats["distance_passes"]},
+                      "distance_passes": stats["distance_passes"], "nnz_per_eps": nnz_eps,
+                      "streamed": bool(stats.get("streamed", 0)),
+                      "workspace_bytes": int(stats.get("workspace_bytes", 0) or 0)},
+            "roofline_labelling": label_roofline(nnz_eps, n, l, stats, label_ms, ws),
             "rank_ms_per_step_min_max": rank_spread,
             "phase_ms": {"distance": dms, "screen_kernel": float(np.mean(screen_ms)) if screen_ms else None,
                          "graph": stats.get("ms_graph"), "label": stats.get("ms_label"),

@@ -72,6 +72,7 @@ Status launch_batch_worklist(const long long* work, int64_t count, int64_t t0, i
                              int64_t* pos, void* scan_scratch, size_t scan_bytes, long long* out, cudaStream_t s);
 Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, int64_t* out,
                         cudaStream_t s);
+Status launch_eps_totals(const int32_t* deg, int64_t n, int k, unsigned long long* out, int sm_count, cudaStream_t s);
 Status launch_label_range(const int32_t* labels, int64_t total, int64_t n, unsigned long long* first_bad,
                           int sm_count, cudaStream_t s);
 Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigned long long* best,
@@ -451,7 +452,7 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
   // Screened pass (dist_tc.cu) when the worklist exists (ordered points) and the bound applies;
   // the exact tile kernel takes the tile pairs it hands back, or everything when it is off.
   const bool screen = n >= kOrderMinPoints && h->distance_mode != DBM_DISTANCE_EXACT && screen_supported(di, eps2[k - 1]);
-  if (h->distance_mode == DBM_DISTANCE_SCREENED && !screen)
+  if ((h->distance_mode == DBM_DISTANCE_SCREENED || h->distance_mode == DBM_DISTANCE_SCREENED_SERIAL) && !screen)
     return Status::Err(DBM_ERR_INVALID, "the screened distance pass needs N >= 4096, D <= 64 and eps^2 >= 1e-20");
   const int32_t xt_rows = screen ? std::max(padded_dims(di), screen_rows(di)) : padded_dims(di);
   DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(xt_rows) * padded_points(n)));
@@ -513,6 +514,7 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
                  as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards, perm,
                  work, work_count};
+    a.screen_serial = h->distance_mode == DBM_DISTANCE_SCREENED_SERIAL;
     if (screen) {
       a.work_total_dev = count_dev;
       a.work_cap = work_cap;
@@ -621,12 +623,15 @@ static Status graph_prep(dbm_handle* h, int64_t n, int64_t d, int k, const int32
     bp.bs = std::min(rule_bs, cap_rows);
     bp.nb = ceil_div(n, static_cast<int64_t>(bp.bs));
     st.attempts = attempt + 1;
-    DBM_TRY(ensure(h->bnnz, sizeof(int64_t) * bp.nb));
-    DBM_TRY(ensure_pinned(h, static_cast<size_t>(bp.nb)));
+    // per-batch nnz, then the per-eps entry totals, in one read-back
+    DBM_TRY(ensure(h->bnnz, sizeof(int64_t) * (bp.nb + kMaxEps)));
+    DBM_TRY(ensure_pinned(h, static_cast<size_t>(bp.nb + kMaxEps)));
     DBM_TRY(launch_batch_nnz(as<int64_t>(h->off), n, static_cast<int64_t>(bp.bs), bp.nb, as<int64_t>(h->bnnz), s));
-    DBM_CUDA(cudaMemcpyAsync(h->pinned, h->bnnz.p, sizeof(int64_t) * bp.nb, cudaMemcpyDeviceToHost, s));
+    DBM_TRY(launch_eps_totals(as<int32_t>(h->deg), n, k, as<unsigned long long>(h->bnnz) + bp.nb, h->sm_count, s));
+    DBM_CUDA(cudaMemcpyAsync(h->pinned, h->bnnz.p, sizeof(int64_t) * (bp.nb + k), cudaMemcpyDeviceToHost, s));
     DBM_CUDA(cudaStreamSynchronize(s));
     bp.bnnz.assign(h->pinned, h->pinned + bp.nb);
+    for (int e = 0; e < k; ++e) st.nnz_per_eps[e] = h->pinned[bp.nb + e];
     uint64_t available = opt.csr_cap_bytes;
     if (available == 0) {
       size_t fr = 0, to = 0;
@@ -902,6 +907,7 @@ static Status streamed_labels(dbm_handle* h, const float* x, int64_t n, int64_t 
                  h->sm_count, 0, 1, as<int32_t>(h->perm), as<long long>(h->subwork), 0};
     a.keep_lo = s0;
     a.keep_hi = s1;
+    a.screen_serial = h->distance_mode == DBM_DISTANCE_SCREENED_SERIAL;
     if (screen) {
       a.work_total_dev = sub_count;
       a.work_cap = W;
@@ -1096,7 +1102,7 @@ int dbm_set_union_retry_limit(dbm_handle* h, int limit)
 
 int dbm_set_distance_mode(dbm_handle* h, int mode)
 {
-  if (!h || mode < DBM_DISTANCE_AUTO || mode > DBM_DISTANCE_SCREENED) return DBM_ERR_INVALID;
+  if (!h || mode < DBM_DISTANCE_AUTO || mode > DBM_DISTANCE_SCREENED_SERIAL) return DBM_ERR_INVALID;
   h->distance_mode = mode;
   return DBM_OK;
 }

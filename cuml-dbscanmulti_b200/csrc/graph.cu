@@ -316,6 +316,37 @@ __global__ void batch_nnz_kernel(const int64_t* __restrict__ off, int64_t n, int
   out[b] = off[t0] - off[s0] + (t0 - s0);
 }
 
+// out[e] = sum over rows of (deg[e][i] - 1): directed entries per eps without the self pairs
+// (out zeroed by the caller)
+__global__ void eps_totals_kernel(const int32_t* __restrict__ deg, int64_t n, int k,
+                                  unsigned long long* __restrict__ out)
+{
+  __shared__ unsigned long long part[kMaxEps];
+  if (threadIdx.x < kMaxEps) part[threadIdx.x] = 0;
+  __syncthreads();
+  for (int e = 0; e < k; ++e) {
+    unsigned long long s = 0;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+      s += static_cast<unsigned long long>(deg[static_cast<int64_t>(e) * n + i] - 1);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0 && s) atomicAdd(&part[e], s);
+  }
+  __syncthreads();
+  if (threadIdx.x < k && part[threadIdx.x]) atomicAdd(out + threadIdx.x, part[threadIdx.x]);
+}
+
+Status launch_eps_totals(const int32_t* deg, int64_t n, int k, unsigned long long* out, int sm_count, cudaStream_t s)
+{
+  DBM_CUDA(cudaMemsetAsync(out, 0, sizeof(unsigned long long) * k, s));
+  count_launch();
+  const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, 256), sm_count * 4)));
+  eps_totals_kernel<<<blocks, 256, 0, s>>>(deg, n, k, out);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
 Status launch_batch_nnz(const int64_t* off, int64_t n, int64_t bs, int64_t nb, int64_t* out,
                         cudaStream_t s)
 {

@@ -254,10 +254,52 @@ def _gather_config_rows(dist, labels, C: int, n: int, group, ranges=None):
     return torch.cat([out[r * mx: r * mx + sizes[r]] for r in range(world)])
 
 
+def agree_limits(stages, max_bytes_per_batch: int = 0, csr_cap_bytes: int = 0, group=None, device=None):
+    """The budget and the CSR memory cap every rank will use (minimum over ranks), so that all
+    ranks compute the same batch plan.  One collective and one host synchronisation: callers that
+    fit repeatedly compute it once and pass it to sharded_fit_multi(limits=...)."""
+    import torch
+    import torch.distributed as dist
+
+    agree = torch.tensor([max_bytes_per_batch or stages.default_budget(), csr_cap_bytes or stages.free_bytes()],
+                         dtype=torch.int64, device=device)
+    dist.all_reduce(agree, op=dist.ReduceOp.MIN, group=group)
+    return int(agree[0].item()), int(agree[1].item())
+
+
+def gather_points(x_host, device, group=None, out=None):
+    """Host points -> the full (N, D) float32 tensor on every rank's device: rank r copies only its
+    row slice [N r / G, N (r + 1) / G) from (pinned) host memory, then one all-gather over the
+    process group (NVLink on B200s) assembles the rest, instead of every rank copying all N rows
+    across PCIe.  `out` (>= G * ceil(N / G) rows) is reused when given."""
+    import torch
+    import torch.distributed as dist
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    xh = x_host if type(x_host).__module__.startswith("torch") else torch.from_numpy(np.ascontiguousarray(x_host, np.float32))
+    n, d = int(xh.shape[0]), int(xh.shape[1])
+    chunk = -(-n // world)
+    if out is None or out.shape[0] < world * chunk or out.shape[1] != d:
+        out = torch.empty((world * chunk, d), dtype=torch.float32, device=device)
+    buf = out[: world * chunk]
+    a, b = min(n, rank * chunk), min(n, (rank + 1) * chunk)
+    mine = buf[rank * chunk:(rank + 1) * chunk]
+    if b > a:
+        mine[: b - a].copy_(xh[a:b], non_blocking=True)
+    dist.all_gather_into_tensor(buf, mine, group=group)
+    return buf[:n], out
+
+
 def sharded_fit_multi(stages, x, eps, min_samples, *, group=None, max_bytes_per_batch: int = 0,
                       backend: str = "cuvs", index: str = "auto", route: str = "auto",
-                      neigh_per_row: int = 0, csr_cap_bytes: int = 0) -> FitResult:
-    """fit_multi over all ranks of ``group``; every rank returns the full (k*l, N) labels."""
+                      neigh_per_row: int = 0, csr_cap_bytes: int = 0, limits=None,
+                      device=None) -> FitResult:
+    """fit_multi over all ranks of ``group``; every rank returns the full (k*l, N) labels.
+
+    ``x`` is the (N, D) float32 tensor present on every rank; with ``device`` set, ``x`` is the
+    host copy (NumPy array or CPU tensor, pinned for asynchronous copies) and gather_points puts
+    it on ``device`` (each rank copies 1/G of the rows, one all-gather assembles the rest).
+    ``limits`` = agree_limits(...) skips the per-call agreement of the budget and CSR cap."""
     import torch
     import torch.distributed as dist
 
@@ -265,18 +307,18 @@ def sharded_fit_multi(stages, x, eps, min_samples, *, group=None, max_bytes_per_
     e = normalize_eps(eps)
     m = normalize_min_samples(min_samples)
     k, l = len(e), len(m)
-    n, d = int(x.shape[0]), int(x.shape[1])
     if backend not in BACKENDS or index not in INDEX or route not in ROUTES:
         raise DbmError(-1, "unknown backend, index or route")
     if route != "auto" and backend != "cuvs":
         raise DbmError(-1, "--route only applies to the cuvs backend")
+    if device is not None:
+        x, stages._points_buf = gather_points(x, device, group, getattr(stages, "_points_buf", None))
+    n, d = int(x.shape[0]), int(x.shape[1])
     dev = x.device
 
     # identical batch plans on every rank: agree on the budget and the CSR memory cap
-    agree = torch.tensor([max_bytes_per_batch or stages.default_budget(), csr_cap_bytes or stages.free_bytes()],
-                         dtype=torch.int64, device=dev)
-    dist.all_reduce(agree, op=dist.ReduceOp.MIN, group=group)
-    budget, cap = int(agree[0].item()), int(agree[1].item())
+    budget, cap = limits if limits is not None else agree_limits(stages, max_bytes_per_batch, csr_cap_bytes,
+                                                                 group, dev)
     opt = Options(BACKENDS[backend], INDEX[index], ROUTES[route], int(neigh_per_row), budget, cap)
 
     hint = n * (neigh_per_row if neigh_per_row > 0 else 16) // (2 * world) + 1024

@@ -255,3 +255,50 @@ def test_labelling_ranges_scale_to_large_grids():
     rs = parallel.labelling_ranges(per_eps, 100, 1_000_000, 8)
     assert time.perf_counter() - t0 < 1.0
     assert len(rs) == 8 and rs[0][0] == 0 and rs[-1][1] == 1600 and all(b > a for a, b in rs)
+
+
+def _points_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        from dbscan_multi import parallel
+
+        pts = make_points()
+        out = None
+        for _ in range(2):  # the second call reuses the buffer
+            full, out = parallel.gather_points(torch.from_numpy(pts), torch.device("cpu"), out=out)
+        budget, cap = parallel.agree_limits(_LimitStages(rank), 0, 0, device=torch.device("cpu"))
+        np.save(os.path.join(result_dir, f"g{rank}.npy"), full.numpy())
+        np.save(os.path.join(result_dir, f"l{rank}.npy"), np.array([budget, cap]))
+    finally:
+        dist.destroy_process_group()
+
+
+class _LimitStages:
+    """Per-rank free-memory figures differ; the agreed limits must be the minimum over ranks."""
+
+    def __init__(self, rank):
+        self.rank = rank
+
+    def default_budget(self):
+        return 1000 + 10 * self.rank
+
+    def free_bytes(self):
+        return 500 - self.rank
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_points_gathered_from_host_slices_and_limits_agreed(tmp_path, world):
+    """gather_points: each rank copies only its row slice, one all-gather assembles the rest,
+    identical to the host array on every rank (N not a multiple of the world size); agree_limits:
+    the minimum budget and cap over ranks, identical everywhere."""
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    mp.spawn(_points_worker, args=(world, port, str(tmp_path)), nprocs=world, join=True)
+    pts = make_points()
+    for r in range(world):
+        assert np.array_equal(np.load(tmp_path / f"g{r}.npy"), pts)
+        assert list(np.load(tmp_path / f"l{r}.npy")) == [1000, 500 - (world - 1)]
