@@ -452,7 +452,7 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
   // Screened pass (dist_tc.cu) when the worklist exists (ordered points) and the bound applies;
   // the exact tile kernel takes the tile pairs it hands back, or everything when it is off.
   const bool screen = n >= kOrderMinPoints && h->distance_mode != DBM_DISTANCE_EXACT && screen_supported(di, eps2[k - 1]);
-  if ((h->distance_mode == DBM_DISTANCE_SCREENED || h->distance_mode == DBM_DISTANCE_SCREENED_SERIAL) && !screen)
+  if (h->distance_mode == DBM_DISTANCE_SCREENED && !screen)
     return Status::Err(DBM_ERR_INVALID, "the screened distance pass needs N >= 4096, D <= 64 and eps^2 >= 1e-20");
   const int32_t xt_rows = screen ? std::max(padded_dims(di), screen_rows(di)) : padded_dims(di);
   DBM_TRY(ensure(h->xt, sizeof(float) * static_cast<size_t>(xt_rows) * padded_points(n)));
@@ -514,7 +514,6 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     DistLaunch a{n, di, k, as<float>(h->xt), eps2, as<unsigned long long>(h->counters),
                  as<uint64_t>(h->edges), cap, hist, as<int32_t>(h->err), h->sm_count, shard, nshards, perm,
                  work, work_count};
-    a.screen_serial = h->distance_mode == DBM_DISTANCE_SCREENED_SERIAL;
     if (screen) {
       a.work_total_dev = count_dev;
       a.work_cap = work_cap;
@@ -907,7 +906,6 @@ static Status streamed_labels(dbm_handle* h, const float* x, int64_t n, int64_t 
                  h->sm_count, 0, 1, as<int32_t>(h->perm), as<long long>(h->subwork), 0};
     a.keep_lo = s0;
     a.keep_hi = s1;
-    a.screen_serial = h->distance_mode == DBM_DISTANCE_SCREENED_SERIAL;
     if (screen) {
       a.work_total_dev = sub_count;
       a.work_cap = W;
@@ -1102,7 +1100,7 @@ int dbm_set_union_retry_limit(dbm_handle* h, int limit)
 
 int dbm_set_distance_mode(dbm_handle* h, int mode)
 {
-  if (!h || mode < DBM_DISTANCE_AUTO || mode > DBM_DISTANCE_SCREENED_SERIAL) return DBM_ERR_INVALID;
+  if (!h || mode < DBM_DISTANCE_AUTO || mode > DBM_DISTANCE_SCREENED) return DBM_ERR_INVALID;
   h->distance_mode = mode;
   return DBM_OK;
 }

@@ -190,7 +190,6 @@ struct DistLaunch {
   // emitted (hist == nullptr then: the degrees are already known and are not counted again).
   int64_t keep_lo = 0;
   int64_t keep_hi = INT64_MAX;
-  int screen_serial = 0;  // screened pass: the one-role kernel even where the pipelined one applies
 };
 
 // An emitted pair needs one endpoint (XT positions pi, pj) in [lo, hi).

@@ -190,9 +190,10 @@ __device__ __forceinline__ void load_row(const float* __restrict__ xt, int64_t n
 }
 
 // Writes the centred tf32 coordinates (zeros past d: x and the centre are 0 there) and returns
-// the fp32 sum of their squares.
+// the fp32 sum of their squares.  The centre comes in registers: read from shared memory inside
+// this loop, each load would wait behind the preceding operand stores (they may alias).
 template <int KP>
-__device__ __forceinline__ float build_row(const float (&x)[KP], const float* __restrict__ cs, int r, unsigned char* op)
+__device__ __forceinline__ float build_row(const float (&x)[KP], const float (&cs)[KP], int r, unsigned char* op)
 {
   float nq[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // four partial sums: independent FMA chains
 #pragma unroll
@@ -447,7 +448,10 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
 #pragma unroll
           for (int t = 0; t < KP; ++t) xj[t] = s_c[t];  // centred to zero
         }
-        mj = build_row<KP>(xj, s_c, tid, opB);
+        float cj[KP];
+#pragma unroll
+        for (int t = 0; t < KP; ++t) cj[t] = s_c[t];
+        mj = build_row<KP>(xj, cj, tid, opB);
       } else {
         __syncthreads();  // s_c
         mj = build_row_xt<KP>(p.xt, p.npad, J * kScreenTile + tid, valid, s_c, tid, opB);
@@ -465,7 +469,10 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
 #pragma unroll
       for (int t = 0; t < KP; ++t) xr[t] = s_c[t];  // centred to zero
     }
-    const float nrow = build_row<KP>(xr, s_c, tid, opA);
+    float ci[KP];
+#pragma unroll
+    for (int t = 0; t < KP; ++t) ci[t] = s_c[t];
+    const float nrow = build_row<KP>(xr, ci, tid, opA);
     const bool bad_i = valid_i && !(nrow < 1e30f);
     put_ext(opA, tid, d, true, valid_i && !bad_i ? row_slack(nrow, se) : 1e30f);
     fence_proxy_async_smem();
@@ -605,503 +612,6 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
 
-// ---- warp-specialised screened pass (D <= 36) -----------------------------------------------------
-// The same bound, operands and outputs as dist_screen_kernel, with the per-item chain split across
-// roles that run concurrently on one persistent CTA per SM, connected by mbarrier rings:
-//   warp 0        producer: takes worklist chunks, TMA-loads tile I's fp32 rows into a ring of
-//                 kWsStages stages and records each item (entry, B slot, new-J flag);
-//   warp 1        MMA: one thread issues the KS tcgen05.mma of an item into one of two TMEM
-//                 accumulators (128 columns each) and commits them to the barriers that free the
-//                 operand-A slot, publish the accumulator and (on a new J) free the old B slot;
-//   warps 2..5    builders: centred tf32 operand A of every item into one of two A slots, and on a
-//                 new tile J its operand B (centre, tf32 columns, slack column) into one of two B
-//                 slots;
-//   warps 6..9    epilogue: thread q reads TMEM lane q (row q of tile I) of the item's
-//                 accumulator, releases it, and runs the exact fp32 chain for its candidates from
-//                 the staged fp32 row and tile J's rows in XT; pairs go through a per-warp queue
-//                 with one cursor atomic per warp and item; the stage is released at the end.
-// So the MMA of item i+1 runs while item i is screened, the operands of item i+2 are built
-// meanwhile and the TMA loads run kWsStages items ahead.  Every wait is bounded; a role that
-// gives up sets s_abort, which every other wait polls, and the kernel reports kErrTmaTimeout.
-// Within the builder and epilogue groups (which also meet at named barriers) every give-up
-// decision is made by the whole group at once, so no thread is ever left at a named barrier.
-constexpr int kWsStages = 4;
-constexpr int kWsA = 2;
-constexpr int kWsB = 2;
-constexpr int kWsAcc = 2;
-constexpr int kWsThreads = 320;
-constexpr int kWsQueue = kScreenCap;  // pairs per epilogue warp and item (an item has <= kScreenCap)
-
-__device__ __forceinline__ void mbar_arrive_n(uint64_t* bar, uint32_t cnt)
-{
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(cnt) : "memory");
-}
-__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads)
-{
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-// OR / AND of a predicate over the `threads` threads meeting at named barrier `id`
-__device__ __forceinline__ bool named_or(uint32_t id, uint32_t threads, bool v)
-{
-  uint32_t r;
-  asm volatile(
-    "{\n\t.reg .pred p, q;\n\t"
-    "setp.ne.u32 p, %1, 0;\n\t"
-    "bar.red.or.pred q, %2, %3, p;\n\t"
-    "selp.u32 %0, 1, 0, q;\n\t}"
-    : "=r"(r)
-    : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(threads)
-    : "memory");
-  return r != 0;
-}
-__device__ __forceinline__ bool named_and(uint32_t id, uint32_t threads, bool v)
-{
-  uint32_t r;
-  asm volatile(
-    "{\n\t.reg .pred p, q;\n\t"
-    "setp.ne.u32 p, %1, 0;\n\t"
-    "bar.red.and.pred q, %2, %3, p;\n\t"
-    "selp.u32 %0, 1, 0, q;\n\t}"
-    : "=r"(r)
-    : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(threads)
-    : "memory");
-  return r != 0;
-}
-
-struct WsItem {
-  long long e;  // worklist entry (J << 32 | I); -1: end of the stream
-  int bslot;    // B slot of the item's tile J
-  int newj;     // 1: the first item of a new tile J (its B slot must be built)
-};
-
-// Bounded wait that also gives up as soon as another role has given up.
-__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag)
-{
-  for (uint32_t it = 0; it < kScreenPolls; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 63u && *abort_flag) return false;
-  }
-  return false;
-}
-
-template <int KS>
-__global__ void __launch_bounds__(kWsThreads, 1)
-dist_screen_ws_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParams p)
-{
-  constexpr int KP = 8 * KS;
-  constexpr uint32_t kBuf = KS * kKStepBytes;  // one [KP][128] fp32 stage == one tf32 operand
-  extern __shared__ unsigned char dyn_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(dyn_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* stage_buf = base;                          // kWsStages x kBuf
-  unsigned char* opA = stage_buf + kWsStages * kBuf;        // kWsA x kBuf
-  unsigned char* opB = opA + kWsA * kBuf;                   // kWsB x kBuf
-  uint32_t* queue = reinterpret_cast<uint32_t*>(opB + kWsB * kBuf);  // 4 warps x kWsQueue
-
-  __shared__ __align__(8) uint64_t stage_full[kWsStages], stage_empty[kWsStages];
-  __shared__ __align__(8) uint64_t a_full[kWsA], a_empty[kWsA];
-  __shared__ __align__(8) uint64_t b_full[kWsB], b_empty[kWsB];
-  __shared__ __align__(8) uint64_t acc_full[kWsAcc], acc_empty[kWsAcc];
-  __shared__ __align__(8) uint64_t mma_done;
-  __shared__ WsItem items[kWsStages];
-  __shared__ int a_skip[kWsA], a_bslot[kWsA], a_newj[kWsA], a_end[kWsA];
-  __shared__ int acc_skip[kWsAcc], acc_end[kWsAcc];
-  __shared__ int b_bad[kWsB];
-  __shared__ float s_c[kWsB][KP];
-  __shared__ float s_eps2[kMaxEps];
-  __shared__ int s_cnt[2];
-  __shared__ int s_qn[4];
-  __shared__ uint32_t s_tmem;
-  __shared__ int s_abort;
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int d = p.d;
-  const int64_t n = p.n;
-  const float cutoff = p.eps2[p.k - 1];
-  const float se = p.sqrt_e;
-  volatile int* abort_flag = &s_abort;
-  int64_t item_begin = p.item_begin, item_count = p.item_count;
-  if (p.total_dev) {
-    const int64_t total = *p.total_dev < p.cap ? *p.total_dev : p.cap;
-    item_begin = total * p.shard / p.nshards;
-    item_count = total * (p.shard + 1) / p.nshards - item_begin;
-  }
-  if (tid < kMaxEps) s_eps2[tid] = p.eps2[tid];
-  if (warp == 1) {
-    tmem_alloc(&s_tmem, kWsAcc * 128);
-    tmem_relinquish();
-  }
-  if (tid == 0) {
-    for (int i = 0; i < kWsStages; ++i) {
-      mbar_init(&stage_full[i], 1);
-      mbar_init(&stage_empty[i], 4);
-    }
-    for (int i = 0; i < kWsA; ++i) {
-      mbar_init(&a_full[i], 4);
-      mbar_init(&a_empty[i], 1);
-    }
-    for (int i = 0; i < kWsB; ++i) {
-      mbar_init(&b_full[i], 4);
-      mbar_init(&b_empty[i], 1);
-    }
-    for (int i = 0; i < kWsAcc; ++i) {
-      mbar_init(&acc_full[i], 2);
-      mbar_init(&acc_empty[i], 4);
-    }
-    mbar_init(&mma_done, 1);
-    mbar_fence_init();
-    s_cnt[0] = s_cnt[1] = 0;
-    s_abort = 0;
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = s_tmem;
-
-  if (warp == 0) {
-    // ================= producer (lane 0 acts, the warp follows) =================
-    long long seen = 0, cstart = 0;
-    int clen = 0, pos = 0;
-    long long curJ = -1;
-    int bslot = 1;
-    // one parity bit per slot: the phase each barrier is waited on next
-    uint32_t ph_empty = (1u << kWsStages) - 1u;  // every stage starts free
-    uint32_t ph_load = 0, loaded = 0;
-    bool ok = true;
-    for (long long it = 0;; ++it) {
-      long long e = -1;
-      if (lane == 0) {
-        if (pos == clen) {  // next chunk: an eighth of the work left over the grid, 16..64 entries
-          long long g = (item_count - seen) / (8LL * gridDim.x);
-          g = g < kScreenGrab ? kScreenGrab : (g > kScreenGrabMax ? kScreenGrabMax : g);
-          cstart = static_cast<long long>(atomicAdd(p.counters + 4, static_cast<unsigned long long>(g)));
-          clen = static_cast<int>(g);
-          seen = cstart + g;
-          pos = 0;
-        }
-        const long long idx = cstart + pos;
-        ++pos;
-        e = idx < item_count ? __ldg(p.work + item_begin + idx) : -1;
-      }
-      e = __shfl_sync(0xffffffffu, e, 0);
-      const int s = static_cast<int>(it % kWsStages);
-      if (!__all_sync(0xffffffffu, ws_wait(&stage_empty[s], (ph_empty >> s) & 1u, abort_flag))) {
-        ok = false;
-        break;
-      }
-      ph_empty ^= 1u << s;
-      if (lane == 0) {
-        WsItem w;
-        w.e = e;
-        w.newj = 0;
-        if (e >= 0 && (e >> 32) != curJ) {
-          curJ = e >> 32;
-          bslot ^= 1;
-          w.newj = 1;
-        }
-        w.bslot = bslot;
-        items[s] = w;
-        if (e < 0) {
-          mbar_arrive_n(&stage_full[s], 1);
-        } else {
-          mbar_arrive_expect_tx(&stage_full[s], kBuf);
-          tma_load_2d(stage_buf + s * kBuf, &xt_map, static_cast<int32_t>((e & 0xffffffffLL) * kScreenTile), 0,
-                      &stage_full[s]);
-        }
-      }
-      if (e < 0) break;
-      loaded |= 1u << s;
-      ph_load ^= 1u << s;  // the load just issued completes phase (bit s of ph_load) ^ 1 of stage_full[s]
-    }
-    if (!ok) {
-      s_abort = 1;
-      // a stage load still in flight lands before the CTA can exit (bounded): the last load issued
-      // to slot s completes phase (bit s of ph_load) ^ 1
-      if (lane == 0)
-        for (int s = 0; s < kWsStages; ++s)
-          if ((loaded >> s) & 1u) mbar_wait_bounded(&stage_full[s], ((ph_load >> s) & 1u) ^ 1u, kScreenPolls);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ================= MMA issue (lane 0 issues, the warp follows) =================
-    uint32_t ph_a = 0, ph_b = 0, ph_acc_empty = (1u << kWsAcc) - 1u;  // parity bit per slot
-    int cur_b = -1;
-    bool ok = true;
-    for (long long it = 0;; ++it) {
-      const int a = static_cast<int>(it % kWsA), t = static_cast<int>(it % kWsAcc);
-      if (!__all_sync(0xffffffffu, ws_wait(&a_full[a], (ph_a >> a) & 1u, abort_flag))) {
-        ok = false;
-        break;
-      }
-      ph_a ^= 1u << a;
-      if (!__all_sync(0xffffffffu, ws_wait(&acc_empty[t], (ph_acc_empty >> t) & 1u, abort_flag))) {
-        ok = false;
-        break;
-      }
-      ph_acc_empty ^= 1u << t;
-      if (a_end[a]) {
-        if (lane == 0) {
-          acc_end[t] = 1;
-          mbar_arrive_n(&acc_full[t], 2);
-        }
-        break;
-      }
-      const int b = a_bslot[a];
-      if (a_newj[a]) {
-        if (lane == 0 && cur_b >= 0) umma_commit(&b_empty[cur_b]);  // the old B slot frees when its MMAs finish
-        if (!__all_sync(0xffffffffu, ws_wait(&b_full[b], (ph_b >> b) & 1u, abort_flag))) {
-          ok = false;
-          break;
-        }
-        ph_b ^= 1u << b;
-        cur_b = b;
-      }
-      const int skip = a_skip[a];
-      if (lane == 0) {
-        acc_end[t] = 0;
-        acc_skip[t] = skip;
-        if (skip) {
-          mbar_arrive_n(&a_empty[a], 1);
-          mbar_arrive_n(&acc_full[t], 2);
-        } else {
-          tc_fence_after();
-          const uint32_t a0 = smem_u32(opA + a * kBuf), b0 = smem_u32(opB + b * kBuf);
-#pragma unroll
-          for (int s = 0; s < KS; ++s)
-            umma_tf32(tmem + t * 128, smem_desc_kmajor(a0 + s * kKStepBytes), smem_desc_kmajor(b0 + s * kKStepBytes),
-                      s > 0);
-          umma_commit(&a_empty[a]);
-          umma_commit(&acc_full[t]);
-          mbar_arrive_n(&acc_full[t], 1);  // publishes acc_skip / acc_end with release semantics
-        }
-      }
-      __syncwarp();
-    }
-    if (!ok) s_abort = 1;
-    // every MMA this thread issued has completed before the CTA can release the tensor memory
-    if (lane == 0) {
-      umma_commit(&mma_done);
-      mbar_wait_bounded(&mma_done, 0, kScreenPolls);
-    }
-    __syncwarp();
-  } else if (warp < 6) {
-    // ================= operand builders (thread r = row / column r) =================
-    const int r = tid - 64;
-    uint32_t ph_full = 0, ph_a_empty = (1u << kWsA) - 1u, ph_b_empty = (1u << kWsB) - 1u;
-    bool ok = true;
-    for (long long it = 0;; ++it) {
-      const int s = static_cast<int>(it % kWsStages), a = static_cast<int>(it % kWsA);
-      if (!named_and(1, 128, ws_wait(&stage_full[s], (ph_full >> s) & 1u, abort_flag))) {
-        ok = false;
-        break;
-      }
-      ph_full ^= 1u << s;
-      const WsItem w = items[s];
-      if (!named_and(1, 128, ws_wait(&a_empty[a], (ph_a_empty >> a) & 1u, abort_flag))) {
-        ok = false;
-        break;
-      }
-      ph_a_empty ^= 1u << a;
-      if (w.e < 0) {
-        if (r == 0) a_end[a] = 1;
-        __syncwarp();
-        if (lane == 0) mbar_arrive_n(&a_full[a], 1);
-        break;
-      }
-      const long long I = w.e & 0xffffffffLL, J = w.e >> 32;
-      const int b = w.bslot;
-      if (w.newj) {
-        // operand B, its centre and slack column for the new tile J
-        if (!named_and(1, 128, ws_wait(&b_empty[b], (ph_b_empty >> b) & 1u, abort_flag))) {
-          ok = false;
-          break;
-        }
-        ph_b_empty ^= 1u << b;
-        if (r < KP) s_c[b][r] = r < d ? 0.5f * (p.box_lo[r * p.tiles + J] + p.box_hi[r * p.tiles + J]) : 0.0f;
-        named_sync(1, 128);
-        const int cols_j = static_cast<int>(n - J * kScreenTile < kScreenTile ? n - J * kScreenTile : kScreenTile);
-        const bool valid = r < cols_j;
-        float xj[KP];
-        load_row<KP>(p.xt, p.npad, J * kScreenTile + r, valid, xj);
-        if (!valid) {
-#pragma unroll
-          for (int q = 0; q < KP; ++q) xj[q] = s_c[b][q];  // centred to zero
-        }
-        unsigned char* ob = opB + b * kBuf;
-        const float mj = build_row<KP>(xj, s_c[b], r, ob);
-        const bool bad = valid && !(mj < 1e30f);
-        const bool any_bad = named_or(1, 128, bad);
-        put_ext(ob, r, d, false, valid && !any_bad ? col_slack(mj, se) : 1e30f);
-        if (r == 0) b_bad[b] = any_bad;
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_n(&b_full[b], 1);
-      }
-      // operand A from the staged fp32 rows of tile I
-      const int rows_i = static_cast<int>(n - I * kScreenTile < kScreenTile ? n - I * kScreenTile : kScreenTile);
-      const bool valid_i = r < rows_i;
-      const float* st = reinterpret_cast<const float*>(stage_buf + s * kBuf);
-      float xr[KP];
-#pragma unroll
-      for (int q = 0; q < KP; ++q) xr[q] = valid_i ? st[q * kScreenTile + r] : s_c[b][q];
-      unsigned char* oa = opA + a * kBuf;
-      const float nrow = build_row<KP>(xr, s_c[b], r, oa);
-      const bool bad_i = valid_i && !(nrow < 1e30f);
-      const bool skip = named_or(1, 128, bad_i) || b_bad[b];
-      put_ext(oa, r, d, true, valid_i && !bad_i ? row_slack(nrow, se) : 1e30f);
-      if (r == 0) {
-        a_skip[a] = skip;
-        a_bslot[a] = b;
-        a_newj[a] = w.newj;
-        a_end[a] = 0;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_n(&a_full[a], 1);
-    }
-    if (!ok) s_abort = 1;
-  } else {
-    // ================= epilogue (thread q = TMEM lane q = row q of tile I) =================
-    const int ew = warp & 3;  // TMEM lanes 32 ew .. 32 ew + 31
-    const int q = ew * 32 + lane;
-    uint32_t* wq = queue + ew * kWsQueue;
-    uint32_t ph_full = 0, ph_acc = 0;  // parity bit per slot
-    unsigned long long my_candidates = 0, my_screened = 0;
-    bool ok = true;
-    for (long long it = 0;; ++it) {
-      const int s = static_cast<int>(it % kWsStages), t = static_cast<int>(it % kWsAcc);
-      const int par = static_cast<int>(it & 1);
-      if (!named_and(2, 128, ws_wait(&acc_full[t], (ph_acc >> t) & 1u, abort_flag))) {
-        ok = false;
-        break;
-      }
-      ph_acc ^= 1u << t;
-      if (acc_end[t]) break;
-      if (!named_and(2, 128, ws_wait(&stage_full[s], (ph_full >> s) & 1u, abort_flag))) {
-        ok = false;
-        break;
-      }
-      ph_full ^= 1u << s;
-      // every epilogue thread is past the previous item (the barriers above), so its candidate
-      // counter is free; the next item adds to it only after its own barriers
-      if (q == 0) s_cnt[par ^ 1] = 0;
-      const long long e = items[s].e;
-      const long long I = e & 0xffffffffLL, J = e >> 32;
-      const bool diag = I == J;
-      const int rows_i = static_cast<int>(n - I * kScreenTile < kScreenTile ? n - I * kScreenTile : kScreenTile);
-      const int cols_j = static_cast<int>(n - J * kScreenTile < kScreenTile ? n - J * kScreenTile : kScreenTile);
-      if (acc_skip[t]) {
-        // coordinates too large for the bound's arithmetic: exact tile kernel
-        if (q == 0) p.fallback[atomicAdd(p.counters + 5, 1ULL)] = e;
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_n(&acc_empty[t], 1);
-          mbar_arrive_n(&stage_empty[s], 1);
-        }
-        continue;
-      }
-      tc_fence_after();
-      // ---- screen: row q of V, 32 columns per TMEM load ----
-      uint32_t mask[4];
-      const uint32_t trow = tmem + t * 128 + (static_cast<uint32_t>(ew * 32) << 16);
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t v[32];
-        tmem_ld(trow + cc * 32, v);
-        uint32_t all = 0xffffffffu;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) all &= v[j];
-        uint32_t hits = 0;
-        if (!(all >> 31)) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) hits |= ((~v[j]) >> 31) << j;
-          if (diag) {
-            const int lo = q - cc * 32;  // strict upper triangle of the diagonal tile: columns > q
-            hits &= lo >= 31 ? 0u : (lo < 0 ? 0xffffffffu : (0xffffffffu << (lo + 1)));
-          }
-        }
-        mask[cc] = hits;
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_n(&acc_empty[t], 1);  // the accumulator is free for the next MMA
-      const int cnt = __popc(mask[0]) + __popc(mask[1]) + __popc(mask[2]) + __popc(mask[3]);
-      if (cnt) atomicAdd(&s_cnt[par], cnt);
-      if (lane == 0) s_qn[ew] = 0;
-      named_sync(2, 128);
-      const int total = s_cnt[par];
-      my_screened += 1;
-      my_candidates += static_cast<unsigned long long>(total);
-      if (total > kScreenCap) {
-        if (q == 0) p.fallback[atomicAdd(p.counters + 5, 1ULL)] = e;
-      } else if (total > 0) {
-        // ---- exact chain for each candidate of this row ----
-        const float* st = reinterpret_cast<const float*>(stage_buf + s * kBuf);
-        const bool valid_i = q < rows_i;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          uint32_t hits = valid_i ? mask[cc] : 0u;
-          while (hits) {
-            const int j = cc * 32 + __ffs(hits) - 1;
-            hits &= hits - 1;
-            if (j >= cols_j) continue;
-            // rows t >= d are 0 on both sides: fma(0, 0, w) == w
-            float w = 0.0f;
-            const float* qj = p.xt + J * kScreenTile + j;
-#pragma unroll
-            for (int tt = 0; tt < KP; ++tt) {
-              const float diff = __fsub_rn(st[tt * kScreenTile + q], __ldg(qj + tt * p.npad));
-              w = __fmaf_rn(diff, diff, w);
-            }
-            if (w <= cutoff && keep_pair(I * kScreenTile + q, J * kScreenTile + j, p.keep_lo, p.keep_hi)) {
-              int code = 0;
-              while (w > s_eps2[code]) ++code;
-              const int at = atomicAdd(&s_qn[ew], 1);
-              wq[at] = (static_cast<uint32_t>(code) << 28) | (static_cast<uint32_t>(q) << 8) | static_cast<uint32_t>(j);
-            }
-          }
-        }
-        __syncwarp();
-        // ---- this warp's pairs: one cursor atomic, then coalesced writes ----
-        const int nh = s_qn[ew];
-        if (nh > 0) {
-          unsigned long long b0 = 0;
-          if (lane == 0) b0 = atomicAdd(p.counters, static_cast<unsigned long long>(nh));
-          b0 = __shfl_sync(0xffffffffu, b0, 0);
-          const int32_t row0 = static_cast<int32_t>(I) * kScreenTile, col0 = static_cast<int32_t>(J) * kScreenTile;
-          for (int h = lane; h < nh; h += 32) {
-            const uint32_t x = wq[h];
-            const int code = static_cast<int>(x >> 28);
-            const int32_t oi = p.perm[row0 + static_cast<int>((x >> 8) & 0xffu)];
-            const int32_t oj = p.perm[col0 + static_cast<int>(x & 0xffu)];
-            const int32_t lo = min(oi, oj), hi = max(oi, oj);
-            const unsigned long long idx = b0 + static_cast<unsigned long long>(h);
-            if (idx < p.edge_cap)
-              p.edges[idx] = (static_cast<uint64_t>(lo) << 32) | (static_cast<uint64_t>(code) << kCodeShift) |
-                             static_cast<uint64_t>(hi);
-            if (p.hist) {
-              int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
-              atomicAdd(hrow + oi, 1);
-              atomicAdd(hrow + oj, 1);
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive_n(&stage_empty[s], 1);
-    }
-    if (!ok) s_abort = 1;
-    if (q == 0) {
-      if (my_candidates) atomicAdd(p.counters + 6, my_candidates);
-      if (my_screened) atomicAdd(p.counters + 7, my_screened);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (tid == 0 && s_abort) atomicOr(p.err, kErrTmaTimeout);
-  if (warp == 1) tmem_dealloc(tmem, kWsAcc * 128);
-}
-
 // ---- host side ----------------------------------------------------------------------------------
 
 bool screen_supported(int32_t d, float eps2_max)
@@ -1154,25 +664,6 @@ static Status launch_screen_ks(const ScreenParams& p, int sm_count, cudaStream_t
   return Status::Ok();
 }
 
-template <int KS>
-static Status launch_screen_ws(const ScreenParams& p, int sm_count, cudaStream_t s)
-{
-  CUtensorMap map;
-  DBM_TRY(make_tile_map(p.xt, p.n, 8 * KS, &map));
-  const size_t smem = 1024 + static_cast<size_t>(kWsStages + kWsA + kWsB) * KS * kKStepBytes +
-                      4 * kWsQueue * sizeof(uint32_t);
-  DBM_CUDA(cudaFuncSetAttribute(dist_screen_ws_kernel<KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(smem)));
-  int64_t grid = sm_count;  // one persistent CTA per SM (it allocates 256 of the 512 TMEM columns)
-  const int64_t chunks = ceil_div(p.item_count, kScreenGrab);
-  if (grid > chunks) grid = chunks;
-  if (grid < 1) return Status::Ok();
-  count_launch();
-  dist_screen_ws_kernel<KS><<<static_cast<unsigned>(grid), kWsThreads, smem, s>>>(map, p);
-  DBM_CUDA(cudaGetLastError());
-  return Status::Ok();
-}
-
 Status launch_screened_distance(const DistLaunch& a, const float* box_lo, const float* box_hi, long long* fallback,
                                 cudaStream_t s)
 {
@@ -1217,17 +708,6 @@ Status launch_screened_distance(const DistLaunch& a, const float* box_lo, const 
     p.sqrt_e = sq;
   }
   const int ks = (a.d + 4 + 7) / 8;
-  if (!a.screen_serial) {
-    // warp-specialised pipeline wherever its stages fit shared memory (D <= 36)
-    switch (ks) {
-      case 1: return launch_screen_ws<1>(p, a.sm_count, s);
-      case 2: return launch_screen_ws<2>(p, a.sm_count, s);
-      case 3: return launch_screen_ws<3>(p, a.sm_count, s);
-      case 4: return launch_screen_ws<4>(p, a.sm_count, s);
-      case 5: return launch_screen_ws<5>(p, a.sm_count, s);
-      default: break;
-    }
-  }
   switch (ks) {
     case 1: return launch_screen_ks<1>(p, a.sm_count, s);
     case 2: return launch_screen_ks<2>(p, a.sm_count, s);

@@ -51,7 +51,7 @@ ROUTE_NAMES = {0: "not-applicable", 1: "annotated", 2: "dense"}
 MAX_EPS = 16
 
 # every symbol include/dbm.h declares
-DISTANCE_MODES = {"auto": 0, "exact": 1, "screened": 2, "screened_serial": 3}
+DISTANCE_MODES = {"auto": 0, "exact": 1, "screened": 2}
 GRAPH_MODES = {"auto": 0, "oneshot": 1, "streamed": 2}
 
 EXPORTED = (
@@ -284,9 +284,8 @@ class DbscanMulti:
         self._lib.dbm_set_phase_timing(self._h, 1 if enabled else 0)
 
     def set_distance_mode(self, mode: str) -> None:
-        """'auto' (tensor-core screen where it applies), 'exact' (exact tile kernel only),
-        'screened' (require the screen) or 'screened_serial' (require the screen, one-role kernel).
-        Labels are identical in every mode."""
+        """'auto' (tensor-core screen where it applies), 'exact' (exact tile kernel only) or
+        'screened' (require the screen).  Labels are identical in every mode."""
         rc = self._lib.dbm_set_distance_mode(self._h, DISTANCE_MODES[mode])
         if rc != DBM_OK:
             raise DbmError(rc, f"bad distance mode {mode!r}")

@@ -133,14 +133,11 @@ void dbm_set_phase_timing(dbm_handle* h, int enabled);
  * per-pair search).  AUTO: the tensor-core screen bounds every surviving tile pair and the
  * exact fp32 chain re-evaluates each candidate, whenever N >= 4096, D <= 64 and
  * eps_max^2 >= 1e-20; otherwise the exact tile kernel.  EXACT: exact tile kernel only.
- * SCREENED: require the screen (DBM_ERR_INVALID when it does not apply).  SCREENED_SERIAL: as
- * SCREENED, but with the one-role screen kernel (one tile pair in flight per CTA) also where the
- * warp-specialised pipeline would run (D <= 36); for comparisons.  Results are identical in all
- * modes. */
+ * SCREENED: require the screen (DBM_ERR_INVALID when it does not apply).  Results are
+ * identical in all modes. */
 #define DBM_DISTANCE_AUTO 0
 #define DBM_DISTANCE_EXACT 1
 #define DBM_DISTANCE_SCREENED 2
-#define DBM_DISTANCE_SCREENED_SERIAL 3
 int dbm_set_distance_mode(dbm_handle* h, int mode);
 
 /* How the neighbour graph is held (the reference always rebuilds it per row batch, bounded by

@@ -28,7 +28,7 @@ def torch_mod():
 
 @pytest.fixture(scope="module")
 def handles(torch_mod):
-    hs = {m: dm.DbscanMulti(0) for m in ("auto", "exact", "screened", "screened_serial")}
+    hs = {m: dm.DbscanMulti(0) for m in ("auto", "exact", "screened")}
     for m, h in hs.items():
         h.set_distance_mode(m)
     yield hs
@@ -73,16 +73,11 @@ def test_screened_equals_exact_and_oracle(handles, torch_mod, name):
     want, want_core, _ = oracle.fit_multi(pts, eps, ms)
     lab_x, core_x, st_x = fit(handles["exact"], torch_mod, pts, eps, ms)
     lab_s, core_s, st_s = fit(handles["screened"], torch_mod, pts, eps, ms)
-    lab_ss, core_ss, st_ss = fit(handles["screened_serial"], torch_mod, pts, eps, ms)
     lab_a, _, _ = fit(handles["auto"], torch_mod, pts, eps, ms)
     assert np.array_equal(lab_x, want) and np.array_equal(core_x, want_core)
     assert np.array_equal(lab_s, want) and np.array_equal(core_s, want_core)
-    assert np.array_equal(lab_ss, want) and np.array_equal(core_ss, want_core)
     assert np.array_equal(lab_a, want)
-    assert st_s["edges"] == st_x["edges"] == st_ss["edges"]
-    # the pipelined and the serial kernel bound the same tile pairs with the same arithmetic
-    assert (st_s["screened_tile_pairs"], st_s["screen_candidates"], st_s["fallback_tile_pairs"]) == \
-        (st_ss["screened_tile_pairs"], st_ss["screen_candidates"], st_ss["fallback_tile_pairs"])
+    assert st_s["edges"] == st_x["edges"]
     assert st_x["screened_tile_pairs"] == 0
     assert st_s["screened_tile_pairs"] + st_s["fallback_tile_pairs"] > 0
 
