@@ -41,8 +41,16 @@ def _worker(rank, world, port, out_dir):
         x = torch.from_numpy(pts).cuda(rank)
         budget = dm.max_bytes_for_batch_size(len(pts), len(EPS), len(MS), ROWS, "cuvs")
         with dm.DbscanMulti(rank) as h:
-            res = parallel.sharded_fit_multi(parallel.DeviceStages(h), x, EPS, MS, max_bytes_per_batch=budget)
+            stages = parallel.DeviceStages(h)
+            res = parallel.sharded_fit_multi(stages, x, EPS, MS, max_bytes_per_batch=budget)
             np.save(os.path.join(out_dir, f"labels_{rank}.npy"), res.labels.cpu().numpy())
+            # host points: each rank copies its row slice, an all-gather assembles the rest; the
+            # limits agreed once and reused
+            limits = parallel.agree_limits(stages, budget, 0, device=torch.device("cuda", rank))
+            for _ in range(2):
+                res = parallel.sharded_fit_multi(stages, torch.from_numpy(pts).pin_memory(), EPS, MS, limits=limits,
+                                                 device=torch.device("cuda", rank), max_bytes_per_batch=budget)
+            np.save(os.path.join(out_dir, f"labels_host_{rank}.npy"), res.labels.cpu().numpy())
             torch.cuda.synchronize()
         dist.barrier()
     finally:
@@ -71,3 +79,4 @@ def test_two_gpu_sharded_fit_matches_single_gpu_and_oracle(tmp_path):
     assert np.array_equal(single, want)
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"labels_{r}.npy"), want)
+        assert np.array_equal(np.load(tmp_path / f"labels_host_{r}.npy"), want)
