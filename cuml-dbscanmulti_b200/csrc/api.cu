@@ -55,9 +55,12 @@ int64_t prune_units(int64_t tiles);
 Status launch_tile_boxes(const float* xt, int64_t n, int64_t npad, int32_t d, float* lo, float* hi, cudaStream_t s);
 Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
                           size_t scratch_bytes, void* scan_scratch, size_t scan_bytes, const int64_t** count_out_dev,
-                          cudaStream_t s);
+                          cudaStream_t s, const int32_t* ext_counts = nullptr);
 Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
-                          long long* work, int64_t cap, cudaStream_t s);
+                          long long* work, int64_t cap, cudaStream_t s, const uint32_t* ext_masks = nullptr);
+Status launch_prune_bound(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, int64_t u0,
+                          int64_t u1, int32_t* counts, uint32_t* masks, cudaStream_t s);
+int64_t prune_mask_words();
 Status spatial_order(const float* x, int64_t n, int32_t d, int32_t* perm, void* scratch, size_t scratch_bytes,
                      cudaStream_t s, int64_t batch_rows = 0);
 Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
@@ -440,18 +443,46 @@ static Status plan_budget(dbm_handle* h, int64_t n, int k, int l, const dbm_opti
 }
 
 // Distance pass over one shard of the tile pairs into hist (zeroed here) and h->edges.
+// Keep masks and counts of every prune unit, gathered from the ranks of a multi-GPU fit that each
+// bounded a share of the units (dbm_distance_prune_units); the order, XT and tile boxes are
+// already in the handle then.
+struct PruneInput {
+  const int32_t* counts = nullptr;
+  const uint32_t* masks = nullptr;
+};
+
+static bool screen_applies(const dbm_handle* h, int64_t n, int32_t d, const float* eps2, int k)
+{
+  return n >= kOrderMinPoints && h->distance_mode != DBM_DISTANCE_EXACT && screen_supported(d, eps2[k - 1]);
+}
+
+// Order, XT and tile boxes (the prune's inputs) for n >= kOrderMinPoints.
+static Status distance_prepare(dbm_handle* h, const float* x, int64_t n, int32_t di, bool screen, cudaStream_t s)
+{
+  const int32_t xt_rows = screen ? std::max(padded_dims(di), screen_rows(di)) : padded_dims(di);
+  const int64_t T = ceil_div(n, 128);
+  DBM_TRY(ensure(h->perm, sizeof(int32_t) * n));
+  DBM_TRY(ensure(h->order_scratch, order_scratch_bytes(n)));
+  DBM_TRY(spatial_order(x, n, di, as<int32_t>(h->perm), h->order_scratch.p, h->order_scratch.bytes, s));
+  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, as<int32_t>(h->perm), xt_rows));
+  DBM_TRY(ensure(h->box_lo, sizeof(float) * static_cast<size_t>(T) * di));
+  DBM_TRY(ensure(h->box_hi, sizeof(float) * static_cast<size_t>(T) * di));
+  return launch_tile_boxes(as<float>(h->xt), n, padded_points(n), di, as<float>(h->box_lo), as<float>(h->box_hi), s);
+}
+
 // With regrow, a pair buffer that turns out too small is grown to the exact count and the pass
 // repeated; without, the call returns after one pass with *found_out > *cap_out (the histograms are
 // complete either way, the pair list only when found <= cap).
 static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d, const float* eps2, int k,
                              int shard, int nshards, int32_t* hist, uint64_t cap_hint, uint64_t* found_out,
-                             dbm_stats& st, cudaStream_t s, bool regrow = true, uint64_t* cap_out = nullptr)
+                             dbm_stats& st, cudaStream_t s, bool regrow = true, uint64_t* cap_out = nullptr,
+                             const PruneInput* pre = nullptr)
 {
   const int32_t di = static_cast<int32_t>(d);
   const int64_t kn = static_cast<int64_t>(k) * n;
   // Screened pass (dist_tc.cu) when the worklist exists (ordered points) and the bound applies;
   // the exact tile kernel takes the tile pairs it hands back, or everything when it is off.
-  const bool screen = n >= kOrderMinPoints && h->distance_mode != DBM_DISTANCE_EXACT && screen_supported(di, eps2[k - 1]);
+  const bool screen = screen_applies(h, n, di, eps2, k);
   if (h->distance_mode == DBM_DISTANCE_SCREENED && !screen)
     return Status::Err(DBM_ERR_INVALID, "the screened distance pass needs N >= 4096, D <= 64 and eps^2 >= 1e-20");
   const int32_t xt_rows = screen ? std::max(padded_dims(di), screen_rows(di)) : padded_dims(di);
@@ -459,18 +490,17 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
   DBM_TRY(ensure(h->counters, 8 * sizeof(unsigned long long)));
   DBM_TRY(ensure(h->err, 16));
   DBM_TRY(ensure_pinned(h, 16));
-  DBM_CUDA(cudaMemsetAsync(h->err.p, 0, 16, s));
+  if (!pre) DBM_CUDA(cudaMemsetAsync(h->err.p, 0, 16, s));
   PhaseTimer t(h, s, &st.ms_distance);
   // Z-order of the leading coordinates makes tiles spatially coherent, which lets whole warps
   // stop early in the distance kernel; results do not depend on the order.
   const int32_t* perm = nullptr;
   if (n >= kOrderMinPoints) {
-    DBM_TRY(ensure(h->perm, sizeof(int32_t) * n));
-    DBM_TRY(ensure(h->order_scratch, order_scratch_bytes(n)));
-    DBM_TRY(spatial_order(x, n, di, as<int32_t>(h->perm), h->order_scratch.p, h->order_scratch.bytes, s));
+    if (!pre) DBM_TRY(distance_prepare(h, x, n, di, screen, s));
     perm = as<int32_t>(h->perm);
+  } else {
+    DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, nullptr, xt_rows));
   }
-  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, perm, xt_rows));
   // Exact tile-pair pruning by per-tile bounding boxes (prune.cu): only tile pairs that may hold
   // a neighbour pair are evaluated.  Every rank builds the same worklist and takes its slice.
   const int64_t T = ceil_div(n, 128);
@@ -479,13 +509,11 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
   int64_t work_count = 0, work_cap = 0;
   const int64_t* count_dev = nullptr;
   if (perm) {
-    DBM_TRY(ensure(h->box_lo, sizeof(float) * static_cast<size_t>(T) * di));
-    DBM_TRY(ensure(h->box_hi, sizeof(float) * static_cast<size_t>(T) * di));
     DBM_TRY(ensure(h->prune_scratch, prune_scratch_bytes(T, di)));
     DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(prune_units(T) + 1)));
-    DBM_TRY(launch_tile_boxes(as<float>(h->xt), n, padded_points(n), di, as<float>(h->box_lo), as<float>(h->box_hi), s));
     DBM_TRY(launch_prune_count(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
-                               h->prune_scratch.bytes, h->scan_scratch.p, h->scan_scratch.bytes, &count_dev, s));
+                               h->prune_scratch.bytes, h->scan_scratch.p, h->scan_scratch.bytes, &count_dev, s,
+                               pre ? pre->counts : nullptr));
     if (screen && h->work_cap_hint > 0) {
       // the screen reads the worklist length on the device; a capacity learned from earlier
       // calls saves the host round trip (an overflow is seen at the pass's own sync below)
@@ -500,7 +528,7 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
     DBM_TRY(ensure(h->work, sizeof(long long) * work_cap));
     work_cap = static_cast<int64_t>(h->work.bytes / sizeof(long long));
     DBM_TRY(launch_prune_write(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
-                               as<long long>(h->work), work_cap, s));
+                               as<long long>(h->work), work_cap, s, pre ? pre->masks : nullptr));
     work = as<long long>(h->work);
   }
   if (screen) DBM_TRY(ensure(h->fallback, sizeof(long long) * std::max<int64_t>(work_cap, 1)));
@@ -543,7 +571,8 @@ static Status distance_stage(dbm_handle* h, const float* x, int64_t n, int64_t d
       if (work_count > work_cap) {
         // the worklist outgrew the learned capacity: redo the pass with the exact size (the
         // hint is now large enough, so this recursion ends after one level)
-        return distance_stage(h, x, n, d, eps2, k, shard, nshards, hist, cap_hint, found_out, st, s, regrow, cap_out);
+        return distance_stage(h, x, n, d, eps2, k, shard, nshards, hist, cap_hint, found_out, st, s, regrow, cap_out,
+                              pre);
       }
     }
     st.tile_pairs_kept = !count_dev ? 1.0 : pairs > 0 ? static_cast<double>(work_count) / static_cast<double>(pairs) : 1.0;
@@ -1221,6 +1250,93 @@ int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, 
     const int64_t launches0 = dbm::launches_so_far();
     uint64_t found = 0;
     r = dbm::distance_stage(h, x_dev, n, d, eps2, k, shard, nshards, hist_dev, edge_cap, &found, st, s);
+    dbm::resolve_phase_timers(h);
+    st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
+    st.workspace_bytes = h->workspace_bytes();
+    if (stats) *stats = st;
+    if (r.ok()) {
+      *edges_found = found;
+      if (found <= edge_cap && found > 0) {
+        const cudaError_t e = cudaMemcpyAsync(edges_dev, h->edges.p, found * sizeof(uint64_t),
+                                              cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess) cudaStreamSynchronize(s);
+        else r = dbm::Status::Err(DBM_ERR_CUDA, cudaGetErrorString(e));
+      }
+    }
+  }
+  dbm::set_err(err, err_len, r.msg);
+  return r.code;
+}
+
+int64_t dbm_prune_units(int64_t n)
+{
+  return n >= dbm::kOrderMinPoints ? dbm::prune_units(dbm::ceil_div(n, 128)) : 0;
+}
+
+int dbm_prune_mask_words(void) { return static_cast<int>(dbm::prune_mask_words()); }
+
+int dbm_distance_prune_units(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host, int k,
+                             int64_t unit_begin, int64_t unit_end, int32_t* counts_dev, uint32_t* masks_dev,
+                             void* stream, char* err, size_t err_len)
+{
+  if (!h) {
+    dbm::set_err(err, err_len, "null handle");
+    return DBM_ERR_INVALID;
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  const int32_t one = 1;
+  dbm::Status r = dbm::validate(n, d, eps_host, k, &one, 1);
+  const int64_t units = dbm_prune_units(n);
+  if (r.ok() && (!x_dev || !counts_dev || !masks_dev || units == 0 || unit_begin < 0 || unit_begin > unit_end ||
+                 unit_end > units))
+    r = dbm::Status::Err(DBM_ERR_INVALID, "x, counts and masks are required, N >= 4096 and 0 <= begin <= end <= units");
+  if (r.ok()) {
+    cudaSetDevice(h->device);
+    float eps2[dbm::kMaxEps];
+    dbm::square_eps(eps_host, k, eps2);
+    const int32_t di = static_cast<int32_t>(d);
+    const bool screen = dbm::screen_applies(h, n, di, eps2, k);
+    const int32_t xt_rows = screen ? std::max(dbm::padded_dims(di), dbm::screen_rows(di)) : dbm::padded_dims(di);
+    r = dbm::ensure(h->xt, sizeof(float) * static_cast<size_t>(xt_rows) * dbm::padded_points(n));
+    if (r.ok()) r = dbm::ensure(h->err, 16);
+    if (r.ok() && cudaMemsetAsync(h->err.p, 0, 16, s) != cudaSuccess)
+      r = dbm::Status::Err(DBM_ERR_CUDA, "cudaMemsetAsync failed");
+    if (r.ok()) r = dbm::distance_prepare(h, x_dev, n, di, screen, s);
+    if (r.ok())
+      r = dbm::launch_prune_bound(dbm::ceil_div(n, 128), dbm::as<float>(h->box_lo), dbm::as<float>(h->box_hi), di,
+                                  eps2[k - 1], unit_begin, unit_end, counts_dev, masks_dev, s);
+  }
+  dbm::set_err(err, err_len, r.msg);
+  return r.code;
+}
+
+int dbm_distance_shard_pruned(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host, int k,
+                              int shard, int nshards, const int32_t* counts_dev, const uint32_t* masks_dev,
+                              int32_t* hist_dev, uint64_t* edges_dev, uint64_t edge_cap, uint64_t* edges_found,
+                              dbm_stats* stats, void* stream, char* err, size_t err_len)
+{
+  if (!h) {
+    dbm::set_err(err, err_len, "null handle");
+    return DBM_ERR_INVALID;
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  const int32_t one = 1;
+  dbm::Status r = dbm::validate(n, d, eps_host, k, &one, 1);
+  if (r.ok() && (!x_dev || !hist_dev || !edges_found || !counts_dev || !masks_dev || nshards < 1 || shard < 0 ||
+                 shard >= nshards || dbm_prune_units(n) == 0))
+    r = dbm::Status::Err(DBM_ERR_INVALID, "x, hist, counts, masks and edges_found are required, N >= 4096 and "
+                                          "0 <= shard < nshards");
+  if (r.ok()) {
+    cudaSetDevice(h->device);
+    float eps2[dbm::kMaxEps];
+    dbm::square_eps(eps_host, k, eps2);
+    dbm_stats st;
+    std::memset(&st, 0, sizeof(st));
+    const int64_t launches0 = dbm::launches_so_far();
+    uint64_t found = 0;
+    const dbm::PruneInput pre{counts_dev, masks_dev};
+    r = dbm::distance_stage(h, x_dev, n, d, eps2, k, shard, nshards, hist_dev, edge_cap, &found, st, s, true, nullptr,
+                            &pre);
     dbm::resolve_phase_timers(h);
     st.launches = static_cast<int32_t>(dbm::launches_so_far() - launches0);
     st.workspace_bytes = h->workspace_bytes();

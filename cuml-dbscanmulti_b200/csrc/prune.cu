@@ -80,13 +80,13 @@ __device__ __forceinline__ void unit_coords(int64_t u, int64_t tiles, int64_t& J
 // always).  The bound's chain is checked every 4 dims, after loading those dims together (lb
 // only grows along the dims, so stopping later is as exact).  Writes the unit's keep mask
 // (bit q of word c: I = block start + 32 c + q) and its count.
-__global__ void tile_pairs_kernel(int64_t tiles, int64_t units, const float* __restrict__ lo,
+__global__ void tile_pairs_kernel(int64_t tiles, int64_t u0, int64_t u1, const float* __restrict__ lo,
                                   const float* __restrict__ hi, int32_t d, float cutoff, int32_t* __restrict__ counts,
                                   uint32_t* __restrict__ masks)
 {
-  const int64_t u = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t u = u0 + ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
-  if (u >= units) return;
+  if (u >= u1) return;
   int64_t J, blk;
   unit_coords(u, tiles, J, blk);
   int32_t total = 0;
@@ -166,10 +166,25 @@ Status launch_tile_boxes(const float* xt, int64_t n, int64_t npad, int32_t d, fl
   return Status::Ok();
 }
 
-// per-J counts and their scan: afterwards the worklist length is at *count_out_dev
+// The bound pass over the units [u0, u1) only: their keep masks (kUnitTiles / 32 words per unit)
+// and counts, at their unit positions of the full-size arrays (a multi-GPU rank bounds its share
+// and the ranks all-gather the rest).
+Status launch_prune_bound(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, int64_t u0,
+                          int64_t u1, int32_t* counts, uint32_t* masks, cudaStream_t s)
+{
+  if (u1 <= u0) return Status::Ok();
+  count_launch();
+  tile_pairs_kernel<<<static_cast<unsigned>(ceil_div((u1 - u0) * 32, 256)), 256, 0, s>>>(tiles, u0, u1, lo, hi, d,
+                                                                                       cutoff, counts, masks);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
+// Per-unit counts and their scan: afterwards the worklist length is at *count_out_dev.  With
+// ext_counts / ext_masks (all units, e.g. gathered from every rank), the bound pass is skipped.
 Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
                           size_t scratch_bytes, void* scan_scratch, size_t scan_bytes, const int64_t** count_out_dev,
-                          cudaStream_t s)
+                          cudaStream_t s, const int32_t* ext_counts)
 {
   if (scratch_bytes < prune_scratch_bytes(tiles, d)) return Status::Err(DBM_ERR_INVALID, "prune scratch too small");
   const int64_t units = units_before(tiles);
@@ -178,18 +193,16 @@ Status launch_prune_count(int64_t tiles, const float* lo, const float* hi, int32
   int64_t* off = reinterpret_cast<int64_t*>(sp + align_up(sizeof(int32_t) * units, 256));
   uint32_t* masks = reinterpret_cast<uint32_t*>(sp + align_up(sizeof(int32_t) * units, 256) +
                                                 align_up(sizeof(int64_t) * (units + 1), 256));
-  count_launch();
-  tile_pairs_kernel<<<static_cast<unsigned>(ceil_div(units * 32, 256)), 256, 0, s>>>(tiles, units, lo, hi, d, cutoff,
-                                                                                   counts, masks);
-  DBM_CUDA(cudaGetLastError());
-  DBM_TRY(exclusive_scan_i32(counts, off, units, scan_scratch, scan_bytes, s));
+  if (!ext_counts) DBM_TRY(launch_prune_bound(tiles, lo, hi, d, cutoff, 0, units, counts, masks, s));
+  DBM_TRY(exclusive_scan_i32(ext_counts ? ext_counts : counts, off, units, scan_scratch, scan_bytes, s));
   *count_out_dev = off + units;
   return Status::Ok();
 }
 
-// the packed worklist entries, J ascending then I ascending (the first `cap` of them)
+// the packed worklist entries, J ascending then I ascending (the first `cap` of them), from the
+// scratch's masks or ext_masks
 Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32_t d, float cutoff, void* scratch,
-                          long long* work, int64_t cap, cudaStream_t s)
+                          long long* work, int64_t cap, cudaStream_t s, const uint32_t* ext_masks)
 {
   (void)lo;
   (void)hi;
@@ -198,13 +211,16 @@ Status launch_prune_write(int64_t tiles, const float* lo, const float* hi, int32
   const int64_t units = units_before(tiles);
   const unsigned char* sp = static_cast<const unsigned char*>(scratch);
   const int64_t* off = reinterpret_cast<const int64_t*>(sp + align_up(sizeof(int32_t) * units, 256));
-  const uint32_t* masks = reinterpret_cast<const uint32_t*>(sp + align_up(sizeof(int32_t) * units, 256) +
-                                                            align_up(sizeof(int64_t) * (units + 1), 256));
+  const uint32_t* masks = ext_masks ? ext_masks
+                                    : reinterpret_cast<const uint32_t*>(sp + align_up(sizeof(int32_t) * units, 256) +
+                                                                        align_up(sizeof(int64_t) * (units + 1), 256));
   count_launch();
   tile_pairs_write_kernel<<<static_cast<unsigned>(ceil_div(units * 32, 256)), 256, 0, s>>>(tiles, units, masks, off,
                                                                                          work, cap);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
+
+int64_t prune_mask_words() { return kUnitTiles / 32; }
 
 }  // namespace dbm

@@ -60,6 +60,7 @@ EXPORTED = (
     "dbm_annotate_pays", "dbm_auto_index_bits", "dbm_build_info_json",
     "dbm_neighbor_counts_noalloc", "dbm_distance_shard", "dbm_fit_multi_from_graph",
     "dbm_set_union_retry_limit", "dbm_set_graph_mode",
+    "dbm_prune_units", "dbm_prune_mask_words", "dbm_distance_prune_units", "dbm_distance_shard_pruned",
 )
 
 
@@ -121,6 +122,16 @@ class Stats(ctypes.Structure):
 
 _lib = None
 
+# cudaStreamLegacy: the legacy default stream as a stream handle.  A torch stream whose handle is 0
+# is that stream; 0 itself (NULL) would mean "the handle's own stream" to the C ABI.
+CUDA_STREAM_LEGACY = 1
+
+
+def stream_arg(s: int) -> ctypes.c_void_p:
+    """A torch stream handle as the C ABI's `stream` argument, preserving the legacy default
+    stream (handle 0) so the library's work is ordered with torch's on that stream."""
+    return ctypes.c_void_p(int(s) if s else CUDA_STREAM_LEGACY)
+
 
 def load_library():
     """Loads libdbm.so; raises if it has not been built (no fallback exists)."""
@@ -157,6 +168,15 @@ def load_library():
     lib.dbm_distance_shard.argtypes = [p, p, i64, i64, p, i32, i32, i32, p, p, u64, ctypes.POINTER(u64),
                                        ctypes.POINTER(Stats), p, cp, sz]
     lib.dbm_distance_shard.restype = i32
+    lib.dbm_prune_units.argtypes = [i64]
+    lib.dbm_prune_units.restype = i64
+    lib.dbm_prune_mask_words.argtypes = []
+    lib.dbm_prune_mask_words.restype = i32
+    lib.dbm_distance_prune_units.argtypes = [p, p, i64, i64, p, i32, i64, i64, p, p, p, cp, sz]
+    lib.dbm_distance_prune_units.restype = i32
+    lib.dbm_distance_shard_pruned.argtypes = [p, p, i64, i64, p, i32, i32, i32, p, p, p, p, u64, ctypes.POINTER(u64),
+                                              ctypes.POINTER(Stats), p, cp, sz]
+    lib.dbm_distance_shard_pruned.restype = i32
     lib.dbm_fit_multi_from_graph.argtypes = [p, i64, i64, p, i32, p, i32, p, p, u64, i32, i32, p, p,
                                              ctypes.POINTER(Options), ctypes.POINTER(Stats), p, i32, p, cp, sz]
     lib.dbm_fit_multi_from_graph.restype = i32
@@ -332,7 +352,7 @@ class DbscanMulti:
         err = ctypes.create_string_buffer(1024)
         rc = self._lib.dbm_neighbor_counts(self._h, ctypes.c_void_p(x.data_ptr()), n, d,
                                            e.ctypes.data_as(ctypes.c_void_p), len(e),
-                                           ctypes.c_void_p(deg.data_ptr()), ctypes.c_void_p(s), err, len(err))
+                                           ctypes.c_void_p(deg.data_ptr()), stream_arg(s), err, len(err))
         if rc != DBM_OK:
             raise DbmError(rc, err.value.decode())
         return deg
@@ -353,7 +373,7 @@ class DbscanMulti:
         s = stream if stream is not None else torch.cuda.current_stream(c.device).cuda_stream
         err = ctypes.create_string_buffer(1024)
         rc = self._lib.dbm_core_sample_indices(self._h, ctypes.c_void_p(c.data_ptr()), int(c.shape[1]),
-                                               int(c.shape[0]), ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(s),
+                                               int(c.shape[0]), ctypes.c_void_p(out.data_ptr()), stream_arg(s),
                                                err, len(err))
         if rc != DBM_OK:
             raise DbmError(rc, err.value.decode())
@@ -394,7 +414,7 @@ class DbscanMulti:
                 self._h, ctypes.c_void_p(x.data_ptr()), n, d, e.ctypes.data_as(ctypes.c_void_p), k,
                 m.ctypes.data_as(ctypes.c_void_p), l, ctypes.c_void_p(labels.data_ptr()),
                 ctypes.c_void_p(core.data_ptr()) if core is not None else None, ctypes.byref(opt),
-                ctypes.byref(st), routes, maxb, ctypes.c_void_p(s), err, len(err))
+                ctypes.byref(st), routes, maxb, stream_arg(s), err, len(err))
         else:
             xh = np.ascontiguousarray(x, dtype=np.float32)
             if xh.ndim != 2:

@@ -28,7 +28,7 @@ from typing import Any
 import numpy as np
 
 from . import (DBM_OK, DbmError, DbscanMulti, FitResult, Options, Stats, ROUTE_NAMES, BACKENDS,
-               INDEX, ROUTES, normalize_eps, normalize_min_samples)
+               INDEX, ROUTES, normalize_eps, normalize_min_samples, stream_arg)
 
 TILE = 128
 
@@ -128,12 +128,16 @@ def labelling_ranges(per_eps: list[float], l: int, n: int, world: int) -> list[t
 
 
 class DeviceStages:
-    """The C-ABI stages on this rank's GPU."""
+    """The C-ABI stages on this rank's GPU.  With a process group of several ranks, the distance
+    stage shards the prune's bound pass by work units and all-gathers the per-unit counts and keep
+    masks over the group (``group=None``: the default group)."""
 
-    def __init__(self, handle: DbscanMulti):
+    def __init__(self, handle: DbscanMulti, group=None):
         self.h = handle
         self.lib = handle._lib
+        self.group = group
         self.last_shard_stats: dict[str, Any] = {}
+        self._prune_bufs = None
 
     def _mem_info(self) -> tuple[int, int]:
         """(free, total) device memory, queried at most once a second (the query costs
@@ -160,6 +164,37 @@ class DeviceStages:
         """Free device memory for the CSR-fits check (the workspace is reused across calls)."""
         return self._mem_info()[0]
 
+    def _gathered_prune(self, x, eps: np.ndarray, shard: int, nshards: int, s: int):
+        """This rank bounds its equal share of the prune units; one all-gather of the counts and
+        one of the keep masks give every rank all of them.  None when there is no prune (N < 4096)
+        or a single rank."""
+        import torch
+        import torch.distributed as dist
+
+        n, d = int(x.shape[0]), int(x.shape[1])
+        units = int(self.lib.dbm_prune_units(n))
+        if nshards <= 1 or units == 0:
+            return None
+        words = int(self.lib.dbm_prune_mask_words())
+        chunk = -(-units // nshards)
+        if self._prune_bufs is None or self._prune_bufs[0].numel() != nshards * chunk or \
+                self._prune_bufs[0].device != x.device:
+            self._prune_bufs = (torch.zeros(nshards * chunk, dtype=torch.int32, device=x.device),
+                                torch.zeros(nshards * chunk * words, dtype=torch.int32, device=x.device))
+        counts, masks = self._prune_bufs
+        u0, u1 = min(units, shard * chunk), min(units, (shard + 1) * chunk)
+        err = ctypes.create_string_buffer(1024)
+        rc = self.lib.dbm_distance_prune_units(self.h._h, ctypes.c_void_p(x.data_ptr()), n, d,
+                                               eps.ctypes.data_as(ctypes.c_void_p), len(eps), u0, u1,
+                                               ctypes.c_void_p(counts.data_ptr()), ctypes.c_void_p(masks.data_ptr()),
+                                               stream_arg(s), err, len(err))
+        if rc != DBM_OK:
+            raise DbmError(rc, err.value.decode())
+        dist.all_gather_into_tensor(counts, counts[shard * chunk:(shard + 1) * chunk].clone(), group=self.group)
+        dist.all_gather_into_tensor(masks, masks[shard * chunk * words:(shard + 1) * chunk * words].clone(),
+                                    group=self.group)
+        return counts, masks
+
     def distance_shard(self, x, eps: np.ndarray, shard: int, nshards: int, cap_hint: int):
         import torch
 
@@ -169,15 +204,23 @@ class DeviceStages:
         cap = max(int(cap_hint), 1024)
         s = torch.cuda.current_stream(x.device).cuda_stream
         err = ctypes.create_string_buffer(1024)
+        pruned = self._gathered_prune(x, eps, shard, nshards, s)
         for _ in range(2):
             edges = torch.empty(cap, dtype=torch.int64, device=x.device)
             found = ctypes.c_uint64(0)
             st = Stats()
-            rc = self.lib.dbm_distance_shard(self.h._h, ctypes.c_void_p(x.data_ptr()), n, d,
-                                             eps.ctypes.data_as(ctypes.c_void_p), k, shard, nshards,
-                                             ctypes.c_void_p(hist.data_ptr()), ctypes.c_void_p(edges.data_ptr()),
-                                             cap, ctypes.byref(found), ctypes.byref(st), ctypes.c_void_p(s), err,
-                                             len(err))
+            if pruned is not None:
+                rc = self.lib.dbm_distance_shard_pruned(
+                    self.h._h, ctypes.c_void_p(x.data_ptr()), n, d, eps.ctypes.data_as(ctypes.c_void_p), k, shard,
+                    nshards, ctypes.c_void_p(pruned[0].data_ptr()), ctypes.c_void_p(pruned[1].data_ptr()),
+                    ctypes.c_void_p(hist.data_ptr()), ctypes.c_void_p(edges.data_ptr()), cap, ctypes.byref(found),
+                    ctypes.byref(st), stream_arg(s), err, len(err))
+            else:
+                rc = self.lib.dbm_distance_shard(self.h._h, ctypes.c_void_p(x.data_ptr()), n, d,
+                                                 eps.ctypes.data_as(ctypes.c_void_p), k, shard, nshards,
+                                                 ctypes.c_void_p(hist.data_ptr()), ctypes.c_void_p(edges.data_ptr()),
+                                                 cap, ctypes.byref(found), ctypes.byref(st), stream_arg(s), err,
+                                                 len(err))
             if rc != DBM_OK:
                 raise DbmError(rc, err.value.decode())
             self.last_shard_stats = st.as_dict()
@@ -200,7 +243,7 @@ class DeviceStages:
             self.h._h, n, d, eps.ctypes.data_as(ctypes.c_void_p), k, ms.ctypes.data_as(ctypes.c_void_p), l,
             ctypes.c_void_p(hist.data_ptr()), ctypes.c_void_p(edges.data_ptr()) if edges.numel() else None,
             int(edges.numel()), cfg_begin, cfg_end, ctypes.c_void_p(labels.data_ptr()), None,
-            ctypes.byref(opt), ctypes.byref(st), routes, n + 1, ctypes.c_void_p(s), err, len(err))
+            ctypes.byref(opt), ctypes.byref(st), routes, n + 1, stream_arg(s), err, len(err))
         if rc != DBM_OK:
             raise DbmError(rc, err.value.decode())
         return labels, st.as_dict(), [ROUTE_NAMES[int(routes[i])] for i in range(int(st.batches))]

@@ -209,6 +209,27 @@ int dbm_distance_shard(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, 
                        distance-pass fields (timers, screen and pruning counts) */, void* stream,
                        char* err, size_t err_len);
 
+/* The exact tile-pair prune, sharded by work units (multi-GPU).  The prune's bound pass tests
+ * every 128 x 128 tile pair (30.5M on 1M points); each rank tests a share of the
+ * dbm_prune_units(n) units and the ranks all-gather the per-unit counts (int32 each) and keep masks
+ * (dbm_prune_mask_words() uint32 words each), instead of every rank testing all of them.
+ * dbm_prune_units: the number of units for n points (0 when n < 4096: no ordering and no prune
+ * then, use dbm_distance_shard).
+ * dbm_distance_prune_units: orders the points, builds XT and the tile boxes in the handle, and
+ * writes the counts and masks of the units [unit_begin, unit_end) at their unit positions of
+ * counts_dev / masks_dev (full-size arrays).  Asynchronous on `stream`.
+ * dbm_distance_shard_pruned: dbm_distance_shard on the same handle and points, with the complete
+ * counts and masks (gathered from every rank) in place of its own bound pass. */
+int64_t dbm_prune_units(int64_t n);
+int dbm_prune_mask_words(void);
+int dbm_distance_prune_units(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host, int k,
+                             int64_t unit_begin, int64_t unit_end, int32_t* counts_dev, uint32_t* masks_dev,
+                             void* stream, char* err, size_t err_len);
+int dbm_distance_shard_pruned(dbm_handle* h, const float* x_dev, int64_t n, int64_t d, const float* eps_host, int k,
+                              int shard, int nshards, const int32_t* counts_dev, const uint32_t* masks_dev,
+                              int32_t* hist_dev, uint64_t* edges_dev, uint64_t edge_cap, uint64_t* edges_found,
+                              dbm_stats* stats, void* stream, char* err, size_t err_len);
+
 /* Everything after the distance pass, from the complete per-code histograms (summed over all
  * shards) and the complete list of neighbour pairs: degrees, core masks, CSR, batch plan and
  * the labels of the configs [cfg_begin, cfg_end) (labels_dev rows outside the range are not
