@@ -80,8 +80,8 @@ Status launch_label_range(const int32_t* labels, int64_t total, int64_t n, unsig
                           int sm_count, cudaStream_t s);
 Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigned long long* best,
                       cudaStream_t s);
-Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int k, int l, int cfg_begin,
-                       int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
+Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int64_t rows, int k, int l,
+                       int cfg_begin, int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
                        unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
                        int union_limit, cudaStream_t s);
 Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0, int64_t rows, int32_t* counts,
@@ -811,7 +811,7 @@ static Status label_batches(dbm_handle* h, int64_t n, int k, int l, int cfg_begi
       }
       ms.s[ne] = max_eps;
     }
-    DBM_TRY(launch_cc_batch(ms, count, n, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc), nb == 1,
+    DBM_TRY(launch_cc_batch(ms, count, n, rows, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc), nb == 1,
                             as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
                             as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, h->union_limit, s));
     base += count;

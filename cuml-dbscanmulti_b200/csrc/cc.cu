@@ -172,6 +172,17 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
   if (!ok) atomicOr(err, kErrUnionLimit);
 }
 
+// P[x] = x for every x of the configs [c0, c1): a fresh forest (the batch-local one of a dense
+// batch, which is then compressed over every point and so must hold no stale parents from an
+// earlier batch or fit)
+__global__ void cc_reset_kernel(int64_t n, int c0, int c1, int32_t* __restrict__ P)
+{
+  const int64_t total = static_cast<int64_t>(c1 - c0) * n;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total; x += stride)
+    P[c0 * n + x] = static_cast<int32_t>(x % n);
+}
+
 // P[x] = root of x for every x of the configs [c0, c1) (full path compression)
 __global__ void cc_compress_kernel(int64_t n, int c0, int c1, int32_t* __restrict__ P)
 {
@@ -305,8 +316,8 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 
 // One batch, every eps: local components (when there is more than one batch), border
 // candidates, global union, border fold.
-Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int k, int l, int cfg_begin,
-                       int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
+Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int64_t rows, int k, int l,
+                       int cfg_begin, int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
                        unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
                        int union_limit, cudaStream_t s)
 {
@@ -336,6 +347,24 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
     count_launch(2);
     cc_union_kernel<<<nbu, 256, 0, s>>>(a, G, nullptr, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, G, best, tag);
+  } else if (upper_entries >= kDenseEntriesPerRow * rows) {
+    // a dense batch of a multi-batch fit: the same sampling for the batch-local and the global
+    // forest at once, then the full union.  The batch-local forest is reset over the owned
+    // configs (a superset of what cc_touch sets), because the compression walks every point's
+    // chain and stale parents from earlier batches or fits need not be valid chains of this one;
+    // the global forest holds only this fit's chains (cc_init).
+    CcArgs sa = a;
+    sa.sample_shift = 3;
+    const unsigned nbs = static_cast<unsigned>(std::max<int64_t>(1, nbu / 8));
+    const unsigned nbc = static_cast<unsigned>(std::max<int64_t>(
+      1, std::min<int64_t>(ceil_div(static_cast<int64_t>(cfg_end - cfg_begin) * n, 256), static_cast<int64_t>(sm_count) * 16)));
+    count_launch(6);
+    cc_reset_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, L);
+    cc_union_kernel<<<nbs, 256, 0, s>>>(sa, L, G, err);
+    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, L);
+    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, G);
+    cc_union_kernel<<<nbu, 256, 0, s>>>(a, L, G, err);
+    cc_best_kernel<<<nb, 256, 0, s>>>(a, L, best, tag);
   } else {
     // the global union needs only to precede the border fold, so it rides along with the local
     // one; the border candidates read the finished local union-find

@@ -111,7 +111,10 @@ __host__ __device__ constexpr size_t dist_smem_bytes(int dbox)
   return static_cast<size_t>(dbox) * kTile * sizeof(float) * 4;
 }
 
-__global__ void __launch_bounds__(kDistThreads, 2)
+// MinBlocks: CTAs per SM the register budget is sized for (2 when the tile buffers let two CTAs
+// share an SM, 1 for the 64-dim boxes, whose 128 KB of buffers admit only one anyway).
+template <int MinBlocks>
+__global__ void __launch_bounds__(kDistThreads, MinBlocks)
 dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
 {
   extern __shared__ __align__(128) unsigned char dyn_smem[];
@@ -120,6 +123,10 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   float* Bs0 = As0 + box_floats;
   float* As1 = Bs0 + box_floats;
   float* Bs1 = As1 + box_floats;
+  // per-(code, local row) pair counts of the current tile pair: rows of tile I at [0, 128), of
+  // tile J at [128, 256); flushed to hist once per tile pair (a dense tile pair has up to 16,384
+  // neighbour pairs, i.e. 32,768 global atomics otherwise)
+  int32_t* s_hist = reinterpret_cast<int32_t*>(Bs1 + box_floats);
   __shared__ __align__(8) uint64_t full[2];
   __shared__ long long s_tile[2];  // tile pair index held by each stage (< 0: none)
   __shared__ float s_eps2[kMaxEps];
@@ -128,6 +135,8 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   const int tx = tid & 15, ty = tid >> 4;
   const int lane = tid & 31;
   if (tid < kMaxEps) s_eps2[tid] = p.eps2[tid];
+  if (p.hist)
+    for (int q = tid; q < p.k * 2 * kTile; q += kDistThreads) s_hist[q] = 0;
   const uint32_t box_bytes = static_cast<uint32_t>(box_floats) * sizeof(float);
 
   auto next_tile = [&]() -> long long {
@@ -173,6 +182,7 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
   for (;;) {
     const long long c = s_tile[stage];
     if (c < 0) break;
+    bool warp_hits = false;     // this warp found neighbour pairs in the tile pair's epilogue
     if (chunk == 0) warp_done = false;
     const bool ok = mbar_wait_bounded(&full[stage], phase[stage], kWaitPolls);
     if (__syncthreads_or(!ok)) {
@@ -283,55 +293,66 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
         if (lane == 31 && total > 0) base = atomicAdd(p.counters, static_cast<unsigned long long>(total));
         base = __shfl_sync(0xffffffffu, base, 31);
         unsigned long long idx = base + static_cast<unsigned long long>(incl - cnt);
-        // Each (rare) neighbour pair is re-evaluated with the same sequential FMA chain -- from
-        // the tile still in shared memory when all dims fit one chunk, else from XT -- which is
-        // bit-identical to the packed lanes and keeps the register budget for the main loop.
-        while (nb) {
-          const int bit = __ffsll(static_cast<long long>(nb)) - 1;
-          nb &= nb - 1;
-          const int i = bit >> 3, j = bit & 7;
+        // Codes straight from the accumulators: each lane of acc[i][jp] is the reference's
+        // sequential fp32 chain of its pair over all D dims (per-lane IEEE rounding of
+        // sub.rn.f32x2 / fma.rn.f32x2, dims in order, across chunks); the loops are unrolled so
+        // the accumulators stay in registers.
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
           const int lr = (i < 4) ? (ty * 4 + i) : (64 + ty * 4 + i - 4);
-          const int lc = (j < 4) ? (tx * 4 + j) : (64 + tx * 4 + j - 4);
-          const int32_t gi = row0 + lr, gj = col0 + lc;
-          float w = 0.0f;
-          if (p.nchunks == 1) {
-            for (int t = 0; t < p.d; ++t) {
-              const float diff = __fsub_rn(As[t * kTile + lr], Bs[t * kTile + lc]);
-              w = __fmaf_rn(diff, diff, w);
+#pragma unroll
+          for (int jp = 0; jp < 4; ++jp) {
+            float w[2];
+            unpack2(acc[i][jp], w[0], w[1]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int j = 2 * jp + h;
+              if (!((nb >> (i * 8 + j)) & 1ull)) continue;
+              const int lc = (j < 4) ? (tx * 4 + j) : (64 + tx * 4 + j - 4);
+              const int32_t gi = row0 + lr, gj = col0 + lc;
+              int code = 0;
+              while (w[h] > s_eps2[code]) ++code;  // terminates: w <= eps2[k-1]
+              int32_t oi = gi, oj = gj;  // original point indices
+              if (p.perm) {
+                oi = p.perm[gi];
+                oj = p.perm[gj];
+              }
+              const int32_t lo = min(oi, oj), hi = max(oi, oj);
+              if (idx < p.edge_cap)
+                p.edges[idx] = (static_cast<uint64_t>(lo) << 32) |
+                               (static_cast<uint64_t>(code) << kCodeShift) | static_cast<uint64_t>(hi);
+              ++idx;
+              if (p.hist) {
+                atomicAdd(s_hist + code * 2 * kTile + lr, 1);
+                atomicAdd(s_hist + code * 2 * kTile + kTile + lc, 1);
+              }
             }
-          } else {
-            const float* xt = p.xt;
-            for (int t = 0; t < p.d; ++t) {
-              const float* col = xt + static_cast<int64_t>(t) * p.npad;
-              const float diff = __fsub_rn(col[gi], col[gj]);
-              w = __fmaf_rn(diff, diff, w);
-            }
-          }
-          int code = 0;
-          while (w > s_eps2[code]) ++code;  // terminates: w <= eps2[k-1]
-          int32_t oi = gi, oj = gj;  // original point indices
-          if (p.perm) {
-            oi = p.perm[gi];
-            oj = p.perm[gj];
-          }
-          const int32_t lo = min(oi, oj), hi = max(oi, oj);
-          if (idx < p.edge_cap)
-            p.edges[idx] = (static_cast<uint64_t>(lo) << 32) |
-                           (static_cast<uint64_t>(code) << kCodeShift) | static_cast<uint64_t>(hi);
-          ++idx;
-          if (p.hist) {
-            int32_t* hrow = p.hist + static_cast<int64_t>(code) * n;
-            atomicAdd(hrow + oi, 1);
-            atomicAdd(hrow + oj, 1);
           }
         }
+        warp_hits = true;
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
     }
-    __syncthreads();  // this stage's buffers are free; the next item's descriptor is visible
+    // this stage's buffers are free; the next item's descriptor is visible; the tile pair's counts
+    // are complete
+    const bool flush = __syncthreads_or(warp_hits) && p.hist;
+    if (flush) {
+      // thread r owns local row r: tile I's rows below 128, tile J's from 128
+      long long I, J;
+      item_coords(p, c, I, J);
+      const int32_t g = tid < kTile ? static_cast<int32_t>(I) * kTile + tid : static_cast<int32_t>(J) * kTile + tid - kTile;
+      for (int e = 0; e < p.k; ++e) {
+        const int32_t v = s_hist[e * 2 * kTile + tid];
+        if (v) {
+          atomicAdd(p.hist + static_cast<int64_t>(e) * n + (p.perm ? p.perm[g] : g), v);
+          s_hist[e * 2 * kTile + tid] = 0;
+        }
+      }
+      __syncthreads();  // cleared before the next tile pair counts
+    }
     stage ^= 1;
     chunk = last_chunk ? 0 : chunk + 1;
   }
@@ -512,18 +533,18 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   p.keep_hi = a.keep_hi;
   for (int e = 0; e < kMaxEps; ++e) p.eps2[e] = e < a.k ? a.eps2[e] : a.eps2[a.k - 1];
 
-  const size_t smem = dist_smem_bytes(dbox);
-  DBM_CUDA(cudaFuncSetAttribute(dist_tri_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(smem)));
+  const size_t smem = dist_smem_bytes(dbox) + (a.hist ? sizeof(int32_t) * a.k * 2 * kTile : 0);
+  const bool one_per_sm = smem > 100 * 1024;
+  auto kernel = one_per_sm ? dist_tri_kernel<1> : dist_tri_kernel<2>;
+  DBM_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   int per_sm = 0;
-  DBM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dist_tri_kernel, kDistThreads,
-                                                         smem));
+  DBM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kDistThreads, smem));
   if (per_sm < 1) per_sm = 1;
   int64_t grid = static_cast<int64_t>(a.sm_count) * per_sm;
   if (!a.work_count_dev && grid > p.item_count) grid = p.item_count;
   if (grid < 1) return Status::Ok();
   count_launch();
-  dist_tri_kernel<<<static_cast<unsigned>(grid), kDistThreads, smem, s>>>(map, p);
+  kernel<<<static_cast<unsigned>(grid), kDistThreads, smem, s>>>(map, p);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }

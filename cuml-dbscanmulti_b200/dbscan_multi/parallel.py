@@ -166,14 +166,15 @@ class DeviceStages:
 
     def _gathered_prune(self, x, eps: np.ndarray, shard: int, nshards: int, s: int):
         """This rank bounds its equal share of the prune units; one all-gather of the counts and
-        one of the keep masks give every rank all of them.  None when there is no prune (N < 4096)
-        or a single rank."""
+        one of the keep masks give every rank all of them.  None when there is no prune (N < 4096),
+        a single shard, or no process group of nshards ranks (shards driven from one process)."""
         import torch
         import torch.distributed as dist
 
         n, d = int(x.shape[0]), int(x.shape[1])
         units = int(self.lib.dbm_prune_units(n))
-        if nshards <= 1 or units == 0:
+        if (nshards <= 1 or units == 0 or not dist.is_available() or not dist.is_initialized()
+                or dist.get_world_size(self.group) != nshards):
             return None
         words = int(self.lib.dbm_prune_mask_words())
         chunk = -(-units // nshards)
