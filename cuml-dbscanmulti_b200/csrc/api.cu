@@ -83,7 +83,7 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int64_t rows, int k, int l,
                        int cfg_begin, int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
                        unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
-                       int union_limit, cudaStream_t s);
+                       int union_limit, int32_t* snap, cudaStream_t s);
 Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0, int64_t rows, int32_t* counts,
                               cudaStream_t s);
 Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t col_base, int64_t s0, int64_t rows, int ne,
@@ -225,6 +225,7 @@ struct dbm_handle {
   std::chrono::steady_clock::time_point free_cached_at{};
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
+  dbm::Buffer snap;  // root snapshot of dense batches (labelling)
   dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_scratch, work, fallback;
   dbm::Buffer subwork, subflags, subpos;  // one batch's tile pairs (streamed fit)
   int distance_mode = DBM_DISTANCE_AUTO;
@@ -241,7 +242,7 @@ struct dbm_handle {
                                 &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
                                 &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz,
                                 &perm, &order_scratch, &box_lo, &box_hi, &prune_scratch,
-                                &work, &fallback, &subwork, &subflags, &subpos};
+                                &work, &fallback, &subwork, &subflags, &subpos, &snap};
     uint64_t s = 0;
     for (auto* b : all) s += b->bytes;
     return s;
@@ -764,6 +765,9 @@ static Status label_batches(dbm_handle* h, int64_t n, int k, int l, int cfg_begi
   DBM_TRY(ensure(h->cur, sizeof(int32_t) * kln));
   DBM_TRY(ensure(h->best, sizeof(unsigned long long) * kln));
   if (nb > 1) DBM_TRY(ensure(h->L, sizeof(int32_t) * kln));
+  bool dense_any = false;
+  for (int64_t b = 0; b < nb; ++b) dense_any |= bp.bnnz[b] - bp.rows(b, n) >= kDenseEntriesPerRow * bp.rows(b, n);
+  if (dense_any) DBM_TRY(ensure(h->snap, kSnapBytesPerPoint * static_cast<uint64_t>(k) * n));
   const int ne = k - 1;  // smaller eps, compacted on the annotated route
   if (ne > 0) {
     DBM_TRY(ensure(h->slab_counts, sizeof(int32_t) * bs * ne));
@@ -813,7 +817,8 @@ static Status label_batches(dbm_handle* h, int64_t n, int k, int l, int cfg_begi
     }
     DBM_TRY(launch_cc_batch(ms, count, n, rows, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc), nb == 1,
                             as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
-                            as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, h->union_limit, s));
+                            as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, h->union_limit,
+                            dense_any ? as<int32_t>(h->snap) : nullptr, s));
     base += count;
   }
   return Status::Ok();
@@ -1073,7 +1078,8 @@ void dbm_destroy(dbm_handle* h)
                         &h->slab_off, &h->slab_col, &h->slab_row, &h->G, &h->L, &h->best, &h->cur,
                         &h->flags, &h->rank, &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev,
                         &h->core_dev, &h->perm, &h->order_scratch, &h->box_lo, &h->box_hi,
-                        &h->prune_scratch, &h->work, &h->fallback, &h->subwork, &h->subflags, &h->subpos};
+                        &h->prune_scratch, &h->work, &h->fallback, &h->subwork, &h->subflags, &h->subpos,
+                        &h->snap};
   for (auto* b : all)
     if (b->p) cudaFree(b->p);
   if (h->pinned) cudaFreeHost(h->pinned);

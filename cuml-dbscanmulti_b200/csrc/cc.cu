@@ -93,20 +93,43 @@ __device__ __forceinline__ void for_each_entry(const CcArgs& a, F&& f)
 // requests in flight (the kernel is bound by the latency of dependent L2 accesses, not by
 // bandwidth).  The lighter kernels (one find or store per config) keep one thread per entry.  f(e, m, r, j)
 // runs for every eps e the entry belongs to and every m of e owned by this call.
+// The flat index x = entry * span + m walks the grid-stride loop as the pair (entry, m), advanced
+// by the stride's own quotient and remainder (two divisions per thread, none per item: a 64-bit
+// division per item made the dense-graph union instruction-bound).
+struct FlatCursor {
+  int64_t q, dq;  // entry index and its step
+  int m, dm;      // minPts index and its step
+  __device__ __forceinline__ FlatCursor(int64_t t0, int64_t stride, int span)
+  {
+    q = t0 / span;
+    m = static_cast<int>(t0 - q * span);
+    dq = stride / span;
+    dm = static_cast<int>(stride - dq * span);
+  }
+  __device__ __forceinline__ void advance(int span)
+  {
+    q += dq;
+    m += dm;
+    if (m >= span) {
+      m -= span;
+      q += 1;
+    }
+  }
+};
+
 template <class F>
 __device__ __forceinline__ void for_each_entry_cfg(const CcArgs& a, F&& f)
 {
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t L = a.l;
+  const int L = a.l;
   const int sh = a.sample_shift;
   if (a.ms.direct) {
     const SlabRef& s = a.ms.s[0];
-    const int64_t total = ((s.count + (int64_t(1) << sh) - 1) >> sh) * L;
-    for (int64_t x = t0; x < total; x += stride) {
-      const int64_t qs = x / L;
-      const int m = static_cast<int>(x - qs * L);
-      const int64_t q = qs << sh;
+    const int64_t entries = (s.count + (int64_t(1) << sh) - 1) >> sh;
+    for (FlatCursor c(t0, stride, L); c.q < entries; c.advance(L)) {
+      const int m = c.m;
+      const int64_t q = c.q << sh;
       const uint32_t w = static_cast<uint32_t>(s.col[q]);
       const int32_t j = static_cast<int32_t>(w & kColMask);
       const int32_t r = s.row[q];
@@ -126,12 +149,11 @@ __device__ __forceinline__ void for_each_entry_cfg(const CcArgs& a, F&& f)
       const SlabRef& s = a.ms.s[e];
       const int64_t b = s.begin_dev ? *s.begin_dev : 0;
       const int64_t lim = s.end_dev ? *s.end_dev : s.count;
-      const int64_t span = m_hi - m_lo;
-      const int64_t total = ((lim - b + (int64_t(1) << sh) - 1) >> sh) * span;
-      for (int64_t x = t0; x < total; x += stride) {
-        const int64_t q = b + ((x / span) << sh);
-        const int m = m_lo + static_cast<int>(x % span);
-        f(e, m, s.row[q], s.col[q] & static_cast<int32_t>(kColMask));
+      const int span = m_hi - m_lo;
+      const int64_t entries = (lim - b + (int64_t(1) << sh) - 1) >> sh;
+      for (FlatCursor c(t0, stride, span); c.q < entries; c.advance(span)) {
+        const int64_t q = b + (c.q << sh);
+        f(e, m_lo + c.m, s.row[q], s.col[q] & static_cast<int32_t>(kColMask));
       }
     }
   }
@@ -183,8 +205,15 @@ __global__ void cc_reset_kernel(int64_t n, int c0, int c1, int32_t* __restrict__
     P[c0 * n + x] = static_cast<int32_t>(x % n);
 }
 
-// P[x] = root of x for every x of the configs [c0, c1) (full path compression)
-__global__ void cc_compress_kernel(int64_t n, int c0, int c1, int32_t* __restrict__ P)
+// Root snapshot of a dense batch: per eps e and point x, kSnapSlots int32 -- slots 0-3 the roots
+// of x in the union's first forest for minPts index m = 0..3, slots 4-7 in its second forest.
+constexpr int kSnapSlots = 8;
+constexpr int kSnapConfigs = 4;
+
+// P[x] = root of x for every x of the configs [c0, c1) (full path compression); with R set, the
+// roots also go to slot `slot + m` of R (configs with m < 4)
+__global__ void cc_compress_kernel(int64_t n, int l, int c0, int c1, int32_t* __restrict__ P,
+                                   int32_t* __restrict__ R, int slot)
 {
   const int64_t total = static_cast<int64_t>(c1 - c0) * n;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -193,7 +222,86 @@ __global__ void cc_compress_kernel(int64_t n, int c0, int c1, int32_t* __restric
     int32_t* g = P + cfg * n;
     const int32_t root = uf_find(g, static_cast<int32_t>(i));
     if (g[i] != root) g[i] = root;
+    const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
+    if (R && m < kSnapConfigs) R[(static_cast<int64_t>(e) * n + i) * kSnapSlots + slot + m] = root;
   }
+}
+
+__device__ __forceinline__ unsigned eq_roots(const int4& a, const int4& b)
+{
+  return static_cast<unsigned>(a.x == b.x) | (static_cast<unsigned>(a.y == b.y) << 1) |
+         (static_cast<unsigned>(a.z == b.z) << 2) | (static_cast<unsigned>(a.w == b.w) << 3);
+}
+
+// The full union pass of a dense batch after the sampled pass and the compression: one thread
+// per entry, U entries in flight per thread.  Both endpoints under one snapshot root (R) make
+// the union a no-op in that forest, since forests only merge; so a typical entry costs one
+// 32-byte load of its column point's roots (the row point's are shared by the warp) instead of
+// two gathers per config and forest.  Entries still open go through the forests as usual.
+// P: the forest of slots 0-3; Q (optional): slots 4-7.
+template <int U>
+__global__ void __launch_bounds__(256) cc_union_snap_kernel(const CcArgs a, int32_t* __restrict__ P,
+                                                            int32_t* __restrict__ Q,
+                                                            const int4* __restrict__ R, int32_t* __restrict__ err)
+{
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int e_lo = a.cfg_begin / a.l, e_hi = min(a.k, (a.cfg_end + a.l - 1) / a.l);
+  bool ok = true;
+  for (int e = e_lo; e < e_hi; ++e) {
+    int m_lo, m_hi;
+    cfg_range(a, e, m_lo, m_hi);
+    if (m_lo >= m_hi) continue;
+    // direct route: every eps walks the max-eps slab and keeps the entries of code <= e
+    const SlabRef& s = a.ms.direct ? a.ms.s[0] : a.ms.s[e];
+    if (!a.ms.direct && e >= a.ms.nslabs) continue;
+    const int64_t b = s.begin_dev ? *s.begin_dev : 0;
+    const int64_t lim = s.end_dev ? *s.end_dev : s.count;
+    const int m4 = min(m_hi, kSnapConfigs);
+    const unsigned owned4 = m_lo < m4 ? ((1u << m4) - 1u) & ~((1u << m_lo) - 1u) : 0u;
+    const bool tail = m_hi > kSnapConfigs;  // configs without a snapshot: always through the forests
+    const int4* Re = R + static_cast<int64_t>(e) * a.n * 2;
+    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
+    for (int64_t q0 = b + t0; q0 < lim; q0 += U * stride) {
+      int32_t r[U], j[U];
+      bool v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t q = q0 + u * stride;
+        v[u] = q < lim;
+        const uint32_t w = v[u] ? static_cast<uint32_t>(s.col[q]) : 0u;
+        r[u] = v[u] ? s.row[q] : 0;
+        j[u] = static_cast<int32_t>(w & kColMask);
+        if (a.ms.direct) v[u] = v[u] && static_cast<int>(w >> kCodeShift) <= e;
+      }
+      int4 pr[U], pj[U], qr[U], qj[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (!v[u]) continue;
+        pr[u] = Re[2 * static_cast<int64_t>(r[u])];
+        pj[u] = Re[2 * static_cast<int64_t>(j[u])];
+        if (Q) {
+          qr[u] = Re[2 * static_cast<int64_t>(r[u]) + 1];
+          qj[u] = Re[2 * static_cast<int64_t>(j[u]) + 1];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (!v[u]) continue;
+        const unsigned open_p = owned4 & ~eq_roots(pr[u], pj[u]);
+        const unsigned open_q = Q ? owned4 & ~eq_roots(qr[u], qj[u]) : 0u;
+        if (!tail && !(open_p | open_q)) continue;
+        const int core_hi = min(m_hi, min(cc[r[u]], cc[j[u]]));
+        for (int m = m_lo; m < core_hi; ++m) {
+          const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
+          const bool snap = m < kSnapConfigs;
+          if (!snap || ((open_p >> m) & 1u)) ok &= uf_unite(P + base, r[u], j[u], a.union_limit);
+          if (Q && (!snap || ((open_q >> m) & 1u))) ok &= uf_unite(Q + base, r[u], j[u], a.union_limit);
+        }
+      }
+    }
+  }
+  if (!ok) atomicOr(err, kErrUnionLimit);
 }
 
 // For every entry with exactly one core endpoint c: best[p] = min(tag << 32 | find(P, c)).
@@ -240,6 +348,30 @@ __global__ void cc_border_kernel(const CcArgs a, int32_t* __restrict__ G,
       *cp = prev < cand ? prev : cand;
     }
   });
+}
+
+// The same fold per point rather than per entry, for batches with many more entries than
+// points x configs: best[p] carries this batch's tag iff some entry of the batch gave p a border
+// candidate, and every such entry folds the same value into cur[p].
+__global__ void cc_border_points_kernel(int64_t n, int l, int c0, int c1, const int32_t* __restrict__ cc,
+                                        int32_t* __restrict__ G, const unsigned long long* __restrict__ best,
+                                        int32_t* __restrict__ cur, uint32_t tag)
+{
+  const int64_t total = static_cast<int64_t>(c1 - c0) * n;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total; x += stride) {
+    const int64_t cfg = c0 + x / n, i = x - (cfg - c0) * n;
+    const int64_t at = cfg * n + i;
+    const unsigned long long v = best[at];
+    if (static_cast<uint32_t>(v >> 32) != tag) continue;
+    const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
+    if (m < cc[static_cast<int64_t>(e) * n + i]) continue;  // core points take no border candidate
+    int32_t* g = G + cfg * n;
+    const int32_t cand = uf_find(g, static_cast<int32_t>(v & 0xffffffffu));
+    const int32_t old = cur[at];
+    const int32_t prev = (old == kNone) ? kNone : uf_find(g, old);
+    cur[at] = prev < cand ? prev : cand;
+  }
 }
 
 // Roots of the configs [c0, c1) as a bitmap: config cfg owns W = ceil(n / 32) words, bit i of its
@@ -297,8 +429,6 @@ __global__ void cc_labels_kernel(int64_t n, int l, int c0, int c1, int64_t W, co
 }
 
 // ---- launchers ----------------------------------------------------------------------------
-// neighbour entries per point from which a one-batch labelling takes the sampled union path
-constexpr int64_t kDenseEntriesPerRow = 64;
 static inline unsigned blocks_for(int64_t work, int threads)
 {
   return static_cast<unsigned>(ceil_div(work > 0 ? work : 1, threads));
@@ -319,7 +449,7 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int64_t rows, int k, int l,
                        int cfg_begin, int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
                        unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
-                       int union_limit, cudaStream_t s)
+                       int union_limit, int32_t* snap, cudaStream_t s)
 {
   if (upper_entries <= 0 || cfg_begin >= cfg_end) return Status::Ok();
   CcArgs a{ms, n, k, l, cfg_begin, cfg_end, cc};
@@ -329,19 +459,27 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
     std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries, 256), static_cast<int64_t>(sm_count) * 16)));
   const unsigned nbu = static_cast<unsigned>(
     std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries * l, 256), static_cast<int64_t>(sm_count) * 32)));
+  // dense batches (afforest-style sampling, Sutton et al. 2018): unite a 1/8 sample of the
+  // entries, compress (recording every point's roots in `snap`), then the full pass finds most
+  // endpoint pairs already under one snapshot root and skips them; the forests' roots are the
+  // same as a plain pass would leave
+  CcArgs sa = a;
+  sa.sample_shift = 3;
+  const unsigned nbs = static_cast<unsigned>(std::max<int64_t>(
+    1, std::min<int64_t>(ceil_div((upper_entries >> 3) * l, 256), static_cast<int64_t>(sm_count) * 32)));
+  const unsigned nbc = static_cast<unsigned>(std::max<int64_t>(
+    1, std::min<int64_t>(ceil_div(static_cast<int64_t>(cfg_end - cfg_begin) * n, 256), static_cast<int64_t>(sm_count) * 16)));
+  constexpr int kSnapUnroll = 4;
+  const unsigned nbe = static_cast<unsigned>(std::max<int64_t>(
+    1, std::min<int64_t>(ceil_div(upper_entries, 256 * kSnapUnroll), static_cast<int64_t>(sm_count) * 32)));
   if (single_batch && upper_entries >= kDenseEntriesPerRow * n) {
-    // dense graph (afforest-style sampling, Sutton et al. 2018): unite a 1/8 sample of the
-    // entries, compress, then the full pass finds most endpoint pairs already under one root and
-    // skips them after two loads; the forest's roots are the same as a plain pass would leave
-    CcArgs sa = a;
-    sa.sample_shift = 3;
-    const unsigned nbs = static_cast<unsigned>(std::max<int64_t>(1, nbu / 8));
-    const unsigned nbc = static_cast<unsigned>(std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(static_cast<int64_t>(cfg_end - cfg_begin) * n, 256), static_cast<int64_t>(sm_count) * 16)));
     count_launch(4);
     cc_union_kernel<<<nbs, 256, 0, s>>>(sa, G, nullptr, err);
-    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, G);
-    cc_union_kernel<<<nbu, 256, 0, s>>>(a, G, nullptr, err);
+    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, l, cfg_begin, cfg_end, G, snap, 0);
+    if (snap)
+      cc_union_snap_kernel<kSnapUnroll><<<nbe, 256, 0, s>>>(a, G, nullptr, reinterpret_cast<const int4*>(snap), err);
+    else
+      cc_union_kernel<<<nbu, 256, 0, s>>>(a, G, nullptr, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, G, best, tag);
   } else if (single_batch) {
     count_launch(2);
@@ -353,17 +491,15 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
     // configs (a superset of what cc_touch sets), because the compression walks every point's
     // chain and stale parents from earlier batches or fits need not be valid chains of this one;
     // the global forest holds only this fit's chains (cc_init).
-    CcArgs sa = a;
-    sa.sample_shift = 3;
-    const unsigned nbs = static_cast<unsigned>(std::max<int64_t>(1, nbu / 8));
-    const unsigned nbc = static_cast<unsigned>(std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(static_cast<int64_t>(cfg_end - cfg_begin) * n, 256), static_cast<int64_t>(sm_count) * 16)));
     count_launch(6);
     cc_reset_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, L);
     cc_union_kernel<<<nbs, 256, 0, s>>>(sa, L, G, err);
-    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, L);
-    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, G);
-    cc_union_kernel<<<nbu, 256, 0, s>>>(a, L, G, err);
+    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, l, cfg_begin, cfg_end, L, snap, 0);
+    cc_compress_kernel<<<nbc, 256, 0, s>>>(n, l, cfg_begin, cfg_end, G, snap, kSnapConfigs);
+    if (snap)
+      cc_union_snap_kernel<kSnapUnroll><<<nbe, 256, 0, s>>>(a, L, G, reinterpret_cast<const int4*>(snap), err);
+    else
+      cc_union_kernel<<<nbu, 256, 0, s>>>(a, L, G, err);
     cc_best_kernel<<<nb, 256, 0, s>>>(a, L, best, tag);
   } else {
     // the global union needs only to precede the border fold, so it rides along with the local
@@ -374,7 +510,14 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
     cc_best_kernel<<<nb, 256, 0, s>>>(a, L, best, tag);
   }
   count_launch();
-  cc_border_kernel<<<nb, 256, 0, s>>>(a, G, best, cur, tag);
+  const int64_t cfg_points = static_cast<int64_t>(cfg_end - cfg_begin) * n;
+  if (cfg_points <= upper_entries) {
+    const unsigned nbp = static_cast<unsigned>(
+      std::max<int64_t>(1, std::min<int64_t>(ceil_div(cfg_points, 256), static_cast<int64_t>(sm_count) * 16)));
+    cc_border_points_kernel<<<nbp, 256, 0, s>>>(n, l, cfg_begin, cfg_end, cc, G, best, cur, tag);
+  } else {
+    cc_border_kernel<<<nb, 256, 0, s>>>(a, G, best, cur, tag);
+  }
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }

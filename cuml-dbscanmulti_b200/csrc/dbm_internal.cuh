@@ -121,6 +121,11 @@ __device__ __forceinline__ int32_t uf_find(int32_t* parent, int32_t x)
   return x;
 }
 
+// Neighbour entries per batch row from which a batch's labelling takes the sampled union path
+// (and needs the root snapshot, kSnapBytesPerPoint per eps and point).
+constexpr int64_t kDenseEntriesPerRow = 64;
+constexpr int64_t kSnapBytesPerPoint = 32;
+
 // Retry bound of uf_unite: a hook can lose its CAS to a concurrent hook at most once per root
 // change, so the bound is never reached in practice; it exists so that no loop can spin forever.
 constexpr int kUnionRetryLimit = 1 << 20;

@@ -180,21 +180,42 @@ Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minp
 }
 
 // ---- max-eps CSR from the neighbour pairs ---------------------------------------------------
+// Slot claims on the per-row cursors: the lanes of a warp that hold the same row share one
+// atomic (the distance pass emits each thread's pairs row by row, so a warp of consecutive pairs
+// holds a few rows many times in a dense graph) and take consecutive slots.  A lane holding
+// kNoRow claims nothing.  All 32 lanes must call it.
+constexpr uint32_t kNoRow = 0xffffffffu;
+
+__device__ __forceinline__ int32_t warp_claim(int32_t* fill, uint32_t v)
+{
+  const unsigned peers = __match_any_sync(0xffffffffu, v);
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(peers) - 1;
+  int32_t base = 0;
+  if (lane == leader && v != kNoRow) base = atomicAdd(fill + v, __popc(peers));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  return base + __popc(peers & ((1u << lane) - 1u));
+}
+
+// grid: whole warps (blocks of 256); lanes past m take part in the claims only
 __global__ void csr_scatter_kernel(const uint64_t* __restrict__ edges, int64_t m,
                                    const int64_t* __restrict__ off, int32_t* __restrict__ fill,
                                    uint32_t* __restrict__ col, int32_t* __restrict__ row)
 {
   const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (q >= m) return;
-  const uint64_t w = edges[q];
+  const bool valid = q < m;
+  const uint64_t w = valid ? edges[q] : 0;
   const uint32_t i = static_cast<uint32_t>(w >> 32);
   const uint32_t lo = static_cast<uint32_t>(w);
   const uint32_t j = lo & kColMask;
   const uint32_t code = lo & ~kColMask;
-  const int64_t qi = off[i] + atomicAdd(fill + i, 1);
+  const int32_t ki = warp_claim(fill, valid ? i : kNoRow);
+  const int32_t kj = warp_claim(fill, valid ? j : kNoRow);
+  if (!valid) return;
+  const int64_t qi = off[i] + ki;
   col[qi] = code | j;
   row[qi] = static_cast<int32_t>(i);
-  const int64_t qj = off[j] + atomicAdd(fill + j, 1);
+  const int64_t qj = off[j] + kj;
   col[qj] = code | i;
   row[qj] = static_cast<int32_t>(j);
 }
@@ -220,18 +241,21 @@ __global__ void csr_scatter_batch_kernel(const uint64_t* __restrict__ edges, int
 {
   const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t m = static_cast<int64_t>(*m_dev) < cap ? static_cast<int64_t>(*m_dev) : cap;
-  if (q >= m) return;
-  const uint64_t w = edges[q];
+  const bool valid = q < m;
+  const uint64_t w = valid ? edges[q] : 0;
   const uint32_t i = static_cast<uint32_t>(w >> 32);
   const uint32_t lo = static_cast<uint32_t>(w);
   const uint32_t j = lo & kColMask;
   const uint32_t code = lo & ~kColMask;
+  const bool own_i = valid && i >= s0 && i < s1, own_j = valid && j >= s0 && j < s1;
+  const int32_t ki = warp_claim(fill, own_i ? static_cast<uint32_t>(i - s0) : kNoRow);
+  const int32_t kj = warp_claim(fill, own_j ? static_cast<uint32_t>(j - s0) : kNoRow);
+  if (!valid) return;
   const int64_t base = off[s0];
   // a row never receives more entries than its degree (same pairs as the degree pass); the
   // checks keep every write inside the buffers all the same and report a violation
-  if (i >= s0 && i < s1) {
-    const int32_t k = atomicAdd(fill + (i - s0), 1);
-    const int64_t qi = off[i] - base + k;
+  if (own_i) {
+    const int64_t qi = off[i] - base + ki;
     if (qi < off[i + 1] - base && qi < cap) {
       col[qi] = code | j;
       row[qi] = static_cast<int32_t>(i);
@@ -239,9 +263,8 @@ __global__ void csr_scatter_batch_kernel(const uint64_t* __restrict__ edges, int
       atomicOr(err, kErrGraphMismatch);
     }
   }
-  if (j >= s0 && j < s1) {
-    const int32_t k = atomicAdd(fill + (j - s0), 1);
-    const int64_t qj = off[j] - base + k;
+  if (own_j) {
+    const int64_t qj = off[j] - base + kj;
     if (qj < off[j + 1] - base && qj < cap) {
       col[qj] = code | i;
       row[qj] = static_cast<int32_t>(j);
