@@ -65,8 +65,8 @@ Status spatial_order(const float* x, int64_t n, int32_t d, int32_t* perm, void* 
                      cudaStream_t s, int64_t batch_rows = 0);
 Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
                       int32_t* deg, int32_t* corecnt, int32_t* rowcnt, uint8_t* core_out,
-                      cudaStream_t s);
-Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, int32_t* fill,
+                      uint8_t* corecnt8, cudaStream_t s);
+Status launch_csr_scatter(const uint64_t* edges, int64_t m, int64_t n, const int64_t* off, int32_t* fill,
                           uint32_t* col, int32_t* row, cudaStream_t s);
 Status launch_csr_scatter_batch(const uint64_t* edges, int64_t cap, const unsigned long long* m_dev, const int64_t* off,
                                 int64_t s0, int64_t s1, int32_t* fill, uint32_t* col, int32_t* row, int32_t* err,
@@ -81,7 +81,8 @@ Status launch_label_range(const int32_t* labels, int64_t total, int64_t n, unsig
 Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigned long long* best,
                       cudaStream_t s);
 Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int64_t rows, int k, int l,
-                       int cfg_begin, int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
+                       int cfg_begin, int cfg_end, const int32_t* cc, const uint8_t* cc8, bool single_batch,
+                       int32_t* G, int32_t* L,
                        unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
                        int union_limit, int32_t* snap, cudaStream_t s);
 Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0, int64_t rows, int32_t* counts,
@@ -226,6 +227,7 @@ struct dbm_handle {
   dbm::Buffer xt, hist, deg, cc, rowcnt, off, fill, edges, col, crow, minpts, counters, err;
   dbm::Buffer slab_counts, slab_off, slab_col, slab_row, G, L, best, cur, flags, rank, scan_scratch, bnnz;
   dbm::Buffer snap;  // root snapshot of dense batches (labelling)
+  dbm::Buffer cc8;   // core counts as bytes (l <= 255)
   dbm::Buffer perm, order_scratch, box_lo, box_hi, prune_scratch, work, fallback;
   dbm::Buffer subwork, subflags, subpos;  // one batch's tile pairs (streamed fit)
   int distance_mode = DBM_DISTANCE_AUTO;
@@ -242,7 +244,7 @@ struct dbm_handle {
                                 &minpts, &counters, &err, &slab_counts, &slab_off, &slab_col,
                                 &slab_row, &G, &L, &best, &cur, &flags, &rank, &scan_scratch, &bnnz,
                                 &perm, &order_scratch, &box_lo, &box_hi, &prune_scratch,
-                                &work, &fallback, &subwork, &subflags, &subpos, &snap};
+                                &work, &fallback, &subwork, &subflags, &subpos, &snap, &cc8};
     uint64_t s = 0;
     for (auto* b : all) s += b->bytes;
     return s;
@@ -381,7 +383,7 @@ static Status neighbor_counts(dbm_handle* h, const float* x, int64_t n, int64_t 
                as<uint64_t>(h->edges), 0, as<int32_t>(h->hist), as<int32_t>(h->err), h->sm_count, 0, 1};
   DBM_TRY(launch_distance(a, s));
   DBM_TRY(launch_degrees(as<int32_t>(h->hist), n, k, as<int32_t>(h->minpts), 1, deg_out,
-                         as<int32_t>(h->cc), as<int32_t>(h->rowcnt), nullptr, s));
+                         as<int32_t>(h->cc), as<int32_t>(h->rowcnt), nullptr, nullptr, s));
   DBM_TRY(ensure_pinned(h, 4));
   h->pinned[0] = 0;
   DBM_CUDA(cudaMemcpyAsync(h->pinned, h->err.p, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
@@ -625,6 +627,7 @@ static Status graph_prep(dbm_handle* h, int64_t n, int64_t d, int k, const int32
   const int64_t kln = kn * l;
   DBM_TRY(ensure(h->deg, sizeof(int32_t) * kn));
   DBM_TRY(ensure(h->cc, sizeof(int32_t) * kn));
+  if (l <= 255) DBM_TRY(ensure(h->cc8, static_cast<size_t>(kn)));
   DBM_TRY(ensure(h->rowcnt, sizeof(int32_t) * n));
   DBM_TRY(ensure(h->off, sizeof(int64_t) * (n + 1)));
   DBM_TRY(ensure(h->fill, sizeof(int32_t) * n));
@@ -636,7 +639,7 @@ static Status graph_prep(dbm_handle* h, int64_t n, int64_t d, int k, const int32
   {
     PhaseTimer t(h, s, &st.ms_graph);
     DBM_TRY(launch_degrees(hist, n, k, as<int32_t>(h->minpts), l, as<int32_t>(h->deg), as<int32_t>(h->cc),
-                           as<int32_t>(h->rowcnt), core_out, s));
+                           as<int32_t>(h->rowcnt), core_out, l <= 255 ? as<uint8_t>(h->cc8) : nullptr, s));
     DBM_TRY(exclusive_scan_i32(as<int32_t>(h->rowcnt), as<int64_t>(h->off), n, h->scan_scratch.p,
                                h->scan_scratch.bytes, s));
   }
@@ -736,7 +739,7 @@ static Status build_csr(dbm_handle* h, int64_t n, const uint64_t* edges, uint64_
   DBM_TRY(ensure(h->col, sizeof(uint32_t) * 2 * std::max<uint64_t>(found, 1)));
   DBM_TRY(ensure(h->crow, sizeof(int32_t) * 2 * std::max<uint64_t>(found, 1)));
   DBM_CUDA(cudaMemsetAsync(h->fill.p, 0, sizeof(int32_t) * n, s));
-  DBM_TRY(launch_csr_scatter(edges, static_cast<int64_t>(found), as<int64_t>(h->off), as<int32_t>(h->fill),
+  DBM_TRY(launch_csr_scatter(edges, static_cast<int64_t>(found), n, as<int64_t>(h->off), as<int32_t>(h->fill),
                              as<uint32_t>(h->col), as<int32_t>(h->crow), s));
   return Status::Ok();
 }
@@ -815,7 +818,8 @@ static Status label_batches(dbm_handle* h, int64_t n, int k, int l, int cfg_begi
       }
       ms.s[ne] = max_eps;
     }
-    DBM_TRY(launch_cc_batch(ms, count, n, rows, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc), nb == 1,
+    DBM_TRY(launch_cc_batch(ms, count, n, rows, k, l, cfg_begin, cfg_end, as<int32_t>(h->cc),
+                            l <= 255 ? as<uint8_t>(h->cc8) : nullptr, nb == 1,
                             as<int32_t>(h->G), as<int32_t>(h->L), as<unsigned long long>(h->best),
                             as<int32_t>(h->cur), tag, as<int32_t>(h->err), h->sm_count, h->union_limit,
                             dense_any ? as<int32_t>(h->snap) : nullptr, s));
@@ -1079,7 +1083,7 @@ void dbm_destroy(dbm_handle* h)
                         &h->flags, &h->rank, &h->scan_scratch, &h->bnnz, &h->xdev, &h->labels_dev,
                         &h->core_dev, &h->perm, &h->order_scratch, &h->box_lo, &h->box_hi,
                         &h->prune_scratch, &h->work, &h->fallback, &h->subwork, &h->subflags, &h->subpos,
-                        &h->snap};
+                        &h->snap, &h->cc8};
   for (auto* b : all)
     if (b->p) cudaFree(b->p);
   if (h->pinned) cudaFreeHost(h->pinned);

@@ -49,10 +49,19 @@ struct CcArgs {
   int64_t n;
   int k, l, cfg_begin, cfg_end;
   const int32_t* cc;  // k x n: core iff m < cc[e*n + i]
+  const uint8_t* cc8 = nullptr;  // the same counts as bytes (l <= 255), read by the entry walks
   int sample_shift = 0;  // union over every 2^s-th entry only (0: all entries)
   bool quick = false;    // union: skip a union-find whose two endpoints already share a parent
   int union_limit = kUnionRetryLimit;  // retry bound of each uf_unite (lowered only by a test knob)
 };
+
+// core count of point x at eps e: the byte copy when there is one (its k x n bytes stay in L1/L2
+// far better than the int32 array under the random gathers of an entry walk)
+__device__ __forceinline__ int core_count(const CcArgs& a, int e, int32_t x)
+{
+  const int64_t at = static_cast<int64_t>(e) * a.n + x;
+  return a.cc8 ? static_cast<int>(__ldg(a.cc8 + at)) : __ldg(a.cc + at);
+}
 
 __device__ __forceinline__ void cfg_range(const CcArgs& a, int e, int& m_lo, int& m_hi)
 {
@@ -165,8 +174,7 @@ __global__ void cc_touch_kernel(const CcArgs a, int32_t* __restrict__ L)
   for_each_entry(a, [&](int e, int32_t r, int32_t j) {
     int m_lo, m_hi;
     cfg_range(a, e, m_lo, m_hi);
-    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
-    const int cr = min(cc[r], m_hi), cj = min(cc[j], m_hi);
+    const int cr = min(core_count(a, e, r), m_hi), cj = min(core_count(a, e, j), m_hi);
     for (int m = m_lo; m < cr; ++m) L[static_cast<int64_t>(e * a.l + m) * a.n + r] = r;
     for (int m = m_lo; m < cj; ++m) L[static_cast<int64_t>(e * a.l + m) * a.n + j] = j;
   });
@@ -186,8 +194,7 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
     const bool skip_p = a.quick && P[base + r] == P[base + j];
     const bool skip_q = !Q || (a.quick && Q[base + r] == Q[base + j]);
     if (skip_p && skip_q) return;
-    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
-    if (m >= cc[r] || m >= cc[j]) return;
+    if (m >= core_count(a, e, r) || m >= core_count(a, e, j)) return;
     if (!skip_p) ok &= uf_unite(P + base, r, j, a.union_limit);
     if (!skip_q) ok &= uf_unite(Q + base, r, j, a.union_limit);
   });
@@ -261,7 +268,6 @@ __global__ void __launch_bounds__(256) cc_union_snap_kernel(const CcArgs a, int3
     const unsigned owned4 = m_lo < m4 ? ((1u << m4) - 1u) & ~((1u << m_lo) - 1u) : 0u;
     const bool tail = m_hi > kSnapConfigs;  // configs without a snapshot: always through the forests
     const int4* Re = R + static_cast<int64_t>(e) * a.n * 2;
-    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
     for (int64_t q0 = b + t0; q0 < lim; q0 += U * stride) {
       int32_t r[U], j[U];
       bool v[U];
@@ -291,7 +297,7 @@ __global__ void __launch_bounds__(256) cc_union_snap_kernel(const CcArgs a, int3
         const unsigned open_p = owned4 & ~eq_roots(pr[u], pj[u]);
         const unsigned open_q = Q ? owned4 & ~eq_roots(qr[u], qj[u]) : 0u;
         if (!tail && !(open_p | open_q)) continue;
-        const int core_hi = min(m_hi, min(cc[r[u]], cc[j[u]]));
+        const int core_hi = min(m_hi, min(core_count(a, e, r[u]), core_count(a, e, j[u])));
         for (int m = m_lo; m < core_hi; ++m) {
           const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
           const bool snap = m < kSnapConfigs;
@@ -311,8 +317,7 @@ __global__ void cc_best_kernel(const CcArgs a, int32_t* __restrict__ P, unsigned
   for_each_entry(a, [&](int e, int32_t r, int32_t j) {
     int m_lo, m_hi;
     cfg_range(a, e, m_lo, m_hi);
-    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
-    const int cr = cc[r], cj = cc[j];
+    const int cr = core_count(a, e, r), cj = core_count(a, e, j);
     const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
     for (int m = lo; m < hi; ++m) {
       const bool r_core = m < cr;
@@ -333,8 +338,7 @@ __global__ void cc_border_kernel(const CcArgs a, int32_t* __restrict__ G,
   for_each_entry(a, [&](int e, int32_t r, int32_t j) {
     int m_lo, m_hi;
     cfg_range(a, e, m_lo, m_hi);
-    const int32_t* cc = a.cc + static_cast<int64_t>(e) * a.n;
-    const int cr = cc[r], cj = cc[j];
+    const int cr = core_count(a, e, r), cj = core_count(a, e, j);
     const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
     for (int m = lo; m < hi; ++m) {
       const int32_t pt = (m < cr) ? j : r;
@@ -447,29 +451,31 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 // One batch, every eps: local components (when there is more than one batch), border
 // candidates, global union, border fold.
 Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, int64_t rows, int k, int l,
-                       int cfg_begin, int cfg_end, const int32_t* cc, bool single_batch, int32_t* G, int32_t* L,
+                       int cfg_begin, int cfg_end, const int32_t* cc, const uint8_t* cc8, bool single_batch,
+                       int32_t* G, int32_t* L,
                        unsigned long long* best, int32_t* cur, uint32_t tag, int32_t* err, int sm_count,
                        int union_limit, int32_t* snap, cudaStream_t s)
 {
   if (upper_entries <= 0 || cfg_begin >= cfg_end) return Status::Ok();
   CcArgs a{ms, n, k, l, cfg_begin, cfg_end, cc};
+  a.cc8 = cc8;
   a.quick = true;
   a.union_limit = union_limit;
   const unsigned nb = static_cast<unsigned>(
     std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries, 256), static_cast<int64_t>(sm_count) * 16)));
   const unsigned nbu = static_cast<unsigned>(
     std::max<int64_t>(1, std::min<int64_t>(ceil_div(upper_entries * l, 256), static_cast<int64_t>(sm_count) * 32)));
-  // dense batches (afforest-style sampling, Sutton et al. 2018): unite a 1/8 sample of the
+  // dense batches (afforest-style sampling, Sutton et al. 2018): unite a 1/16 sample of the
   // entries, compress (recording every point's roots in `snap`), then the full pass finds most
   // endpoint pairs already under one snapshot root and skips them; the forests' roots are the
   // same as a plain pass would leave
   CcArgs sa = a;
-  sa.sample_shift = 3;
+  sa.sample_shift = 4;
   const unsigned nbs = static_cast<unsigned>(std::max<int64_t>(
-    1, std::min<int64_t>(ceil_div((upper_entries >> 3) * l, 256), static_cast<int64_t>(sm_count) * 32)));
+    1, std::min<int64_t>(ceil_div((upper_entries >> sa.sample_shift) * l, 256), static_cast<int64_t>(sm_count) * 32)));
   const unsigned nbc = static_cast<unsigned>(std::max<int64_t>(
     1, std::min<int64_t>(ceil_div(static_cast<int64_t>(cfg_end - cfg_begin) * n, 256), static_cast<int64_t>(sm_count) * 16)));
-  constexpr int kSnapUnroll = 4;
+  constexpr int kSnapUnroll = 1;
   const unsigned nbe = static_cast<unsigned>(std::max<int64_t>(
     1, std::min<int64_t>(ceil_div(upper_entries, 256 * kSnapUnroll), static_cast<int64_t>(sm_count) * 32)));
   if (single_batch && upper_entries >= kDenseEntriesPerRow * n) {

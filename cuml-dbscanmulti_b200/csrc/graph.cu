@@ -141,11 +141,13 @@ Status exclusive_scan_i32(const int32_t* in, int64_t* out, int64_t n, void* scra
 
 // ---- degrees and core counts ----------------------------------------------------------------
 // deg[e][i] = 1 + sum_{c <= e} hist[c][i]; corecnt[e][i] = #{m : deg >= minpts[m]};
-// rowcnt[i] = deg[k-1][i] - 1 (max-eps neighbours without the point itself).
+// rowcnt[i] = deg[k-1][i] - 1 (max-eps neighbours without the point itself); corecnt8 (optional,
+// l <= 255): the core counts as bytes, a quarter of the cache footprint for the labelling's
+// gathers.
 __global__ void degrees_kernel(const int32_t* __restrict__ hist, int64_t n, int k,
                                const int32_t* __restrict__ minpts, int l, int32_t* __restrict__ deg,
                                int32_t* __restrict__ corecnt, int32_t* __restrict__ rowcnt,
-                               uint8_t* __restrict__ core_out)
+                               uint8_t* __restrict__ core_out, uint8_t* __restrict__ corecnt8)
 {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
@@ -160,6 +162,7 @@ __global__ void degrees_kernel(const int32_t* __restrict__ hist, int64_t n, int 
       if (__ldg(minpts + mid) <= run) lo = mid + 1; else hi = mid;
     }
     corecnt[static_cast<int64_t>(e) * n + i] = lo;
+    if (corecnt8) corecnt8[static_cast<int64_t>(e) * n + i] = static_cast<uint8_t>(lo);
     if (core_out) {
       for (int m = 0; m < l; ++m)
         core_out[(static_cast<int64_t>(e) * l + m) * n + i] = static_cast<uint8_t>(m < lo);
@@ -170,11 +173,11 @@ __global__ void degrees_kernel(const int32_t* __restrict__ hist, int64_t n, int 
 
 Status launch_degrees(const int32_t* hist, int64_t n, int k, const int32_t* minpts, int l,
                       int32_t* deg, int32_t* corecnt, int32_t* rowcnt, uint8_t* core_out,
-                      cudaStream_t s)
+                      uint8_t* corecnt8, cudaStream_t s)
 {
   count_launch();
-  degrees_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(hist, n, k, minpts, l, deg,
-                                                                         corecnt, rowcnt, core_out);
+  degrees_kernel<<<static_cast<unsigned>(ceil_div(n, 256)), 256, 0, s>>>(
+    hist, n, k, minpts, l, deg, corecnt, rowcnt, core_out, l <= 255 ? corecnt8 : nullptr);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
@@ -197,10 +200,36 @@ __device__ __forceinline__ int32_t warp_claim(int32_t* fill, uint32_t v)
   return base + __popc(peers & ((1u << lane) - 1u));
 }
 
+// row[q - off[s0]] = r for every CSR position q of the rows r in [s0, s1) (at most cap positions):
+// one warp per row, coalesced stores.  The scatter kernels write only the columns: a row's
+// entries are contiguous, so its row ids need no scattered 4-byte stores.
+__global__ void csr_rows_kernel(const int64_t* __restrict__ off, int64_t s0, int64_t s1, int64_t cap,
+                                int32_t* __restrict__ row)
+{
+  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t base = off[s0];
+  for (int64_t r = s0 + ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); r < s1; r += warps) {
+    const int64_t beg = off[r] - base;
+    const int64_t end = off[r + 1] - base < cap ? off[r + 1] - base : cap;
+    for (int64_t q = beg + lane; q < end; q += 32) row[q] = static_cast<int32_t>(r);
+  }
+}
+
+static Status launch_csr_rows(const int64_t* off, int64_t s0, int64_t s1, int64_t cap, int32_t* row, cudaStream_t s)
+{
+  if (s1 <= s0 || cap <= 0) return Status::Ok();
+  const int64_t blocks = std::min<int64_t>(ceil_div(s1 - s0, 8), int64_t(1) << 20);
+  count_launch();
+  csr_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, s0, s1, cap, row);
+  DBM_CUDA(cudaGetLastError());
+  return Status::Ok();
+}
+
 // grid: whole warps (blocks of 256); lanes past m take part in the claims only
 __global__ void csr_scatter_kernel(const uint64_t* __restrict__ edges, int64_t m,
                                    const int64_t* __restrict__ off, int32_t* __restrict__ fill,
-                                   uint32_t* __restrict__ col, int32_t* __restrict__ row)
+                                   uint32_t* __restrict__ col)
 {
   const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const bool valid = q < m;
@@ -212,22 +241,19 @@ __global__ void csr_scatter_kernel(const uint64_t* __restrict__ edges, int64_t m
   const int32_t ki = warp_claim(fill, valid ? i : kNoRow);
   const int32_t kj = warp_claim(fill, valid ? j : kNoRow);
   if (!valid) return;
-  const int64_t qi = off[i] + ki;
-  col[qi] = code | j;
-  row[qi] = static_cast<int32_t>(i);
-  const int64_t qj = off[j] + kj;
-  col[qj] = code | i;
-  row[qj] = static_cast<int32_t>(j);
+  col[off[i] + ki] = code | j;
+  col[off[j] + kj] = code | i;
 }
 
-Status launch_csr_scatter(const uint64_t* edges, int64_t m, const int64_t* off, int32_t* fill,
+// the max-eps CSR of all n rows (2 m entries): columns scattered from the pairs, row ids per row
+Status launch_csr_scatter(const uint64_t* edges, int64_t m, int64_t n, const int64_t* off, int32_t* fill,
                           uint32_t* col, int32_t* row, cudaStream_t s)
 {
   if (m <= 0) return Status::Ok();
   count_launch();
-  csr_scatter_kernel<<<static_cast<unsigned>(ceil_div(m, 256)), 256, 0, s>>>(edges, m, off, fill, col, row);
+  csr_scatter_kernel<<<static_cast<unsigned>(ceil_div(m, 256)), 256, 0, s>>>(edges, m, off, fill, col);
   DBM_CUDA(cudaGetLastError());
-  return Status::Ok();
+  return launch_csr_rows(off, 0, n, 2 * m, row, s);
 }
 
 // The rows [s0, s1) of the max-eps CSR only, from neighbour pairs that each have at least one
@@ -237,7 +263,7 @@ __global__ void csr_scatter_batch_kernel(const uint64_t* __restrict__ edges, int
                                          const unsigned long long* __restrict__ m_dev,
                                          const int64_t* __restrict__ off, int64_t s0, int64_t s1,
                                          int32_t* __restrict__ fill, uint32_t* __restrict__ col,
-                                         int32_t* __restrict__ row, int32_t* __restrict__ err)
+                                         int32_t* __restrict__ err)
 {
   const int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t m = static_cast<int64_t>(*m_dev) < cap ? static_cast<int64_t>(*m_dev) : cap;
@@ -258,7 +284,6 @@ __global__ void csr_scatter_batch_kernel(const uint64_t* __restrict__ edges, int
     const int64_t qi = off[i] - base + ki;
     if (qi < off[i + 1] - base && qi < cap) {
       col[qi] = code | j;
-      row[qi] = static_cast<int32_t>(i);
     } else {
       atomicOr(err, kErrGraphMismatch);
     }
@@ -267,7 +292,6 @@ __global__ void csr_scatter_batch_kernel(const uint64_t* __restrict__ edges, int
     const int64_t qj = off[j] - base + kj;
     if (qj < off[j + 1] - base && qj < cap) {
       col[qj] = code | i;
-      row[qj] = static_cast<int32_t>(j);
     } else {
       atomicOr(err, kErrGraphMismatch);
     }
@@ -282,9 +306,9 @@ Status launch_csr_scatter_batch(const uint64_t* edges, int64_t cap, const unsign
   if (cap <= 0) return Status::Ok();
   count_launch();
   csr_scatter_batch_kernel<<<static_cast<unsigned>(ceil_div(cap, 256)), 256, 0, s>>>(edges, cap, m_dev, off, s0, s1,
-                                                                                     fill, col, row, err);
+                                                                                     fill, col, err);
   DBM_CUDA(cudaGetLastError());
-  return Status::Ok();
+  return launch_csr_rows(off, s0, s1, cap, row, s);
 }
 
 // ---- the tile pairs of one row batch (memory-bounded fit) ----------------------------------
