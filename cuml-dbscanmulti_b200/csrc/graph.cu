@@ -201,27 +201,35 @@ __device__ __forceinline__ int32_t warp_claim(int32_t* fill, uint32_t v)
 }
 
 // row[q - off[s0]] = r for every CSR position q of the rows r in [s0, s1) (at most cap positions):
-// one warp per row, coalesced stores.  The scatter kernels write only the columns: a row's
-// entries are contiguous, so its row ids need no scattered 4-byte stores.
-__global__ void csr_rows_kernel(const int64_t* __restrict__ off, int64_t s0, int64_t s1, int64_t cap,
+// `lanes` consecutive lanes (a power of two <= 32, about the mean row length) per row, so the
+// stores of a warp are contiguous whether rows hold 4 entries or 40,000.  The scatter kernels
+// write only the columns: a row's entries are contiguous, so its row ids need no scattered
+// 4-byte stores.
+__global__ void csr_rows_kernel(const int64_t* __restrict__ off, int64_t s0, int64_t s1, int64_t cap, int lanes,
                                 int32_t* __restrict__ row)
 {
-  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t groups = (static_cast<int64_t>(gridDim.x) * blockDim.x) / lanes;
+  const int sub = static_cast<int>(t % lanes);
   const int64_t base = off[s0];
-  for (int64_t r = s0 + ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5); r < s1; r += warps) {
+  for (int64_t r = s0 + t / lanes; r < s1; r += groups) {
     const int64_t beg = off[r] - base;
     const int64_t end = off[r + 1] - base < cap ? off[r + 1] - base : cap;
-    for (int64_t q = beg + lane; q < end; q += 32) row[q] = static_cast<int32_t>(r);
+    for (int64_t q = beg + sub; q < end; q += lanes) row[q] = static_cast<int32_t>(r);
   }
 }
 
-static Status launch_csr_rows(const int64_t* off, int64_t s0, int64_t s1, int64_t cap, int32_t* row, cudaStream_t s)
+// entries: the expected number of CSR positions of the rows (sets the lanes per row)
+static Status launch_csr_rows(const int64_t* off, int64_t s0, int64_t s1, int64_t cap, int64_t entries, int32_t* row,
+                              cudaStream_t s)
 {
   if (s1 <= s0 || cap <= 0) return Status::Ok();
-  const int64_t blocks = std::min<int64_t>(ceil_div(s1 - s0, 8), int64_t(1) << 20);
+  const int64_t mean = ceil_div(std::max<int64_t>(entries, 1), s1 - s0);
+  int lanes = 1;
+  while (lanes < 32 && lanes < mean) lanes <<= 1;
+  const int64_t blocks = std::min<int64_t>(ceil_div((s1 - s0) * lanes, 256), int64_t(1) << 20);
   count_launch();
-  csr_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, s0, s1, cap, row);
+  csr_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(off, s0, s1, cap, lanes, row);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
@@ -253,7 +261,7 @@ Status launch_csr_scatter(const uint64_t* edges, int64_t m, int64_t n, const int
   count_launch();
   csr_scatter_kernel<<<static_cast<unsigned>(ceil_div(m, 256)), 256, 0, s>>>(edges, m, off, fill, col);
   DBM_CUDA(cudaGetLastError());
-  return launch_csr_rows(off, 0, n, 2 * m, row, s);
+  return launch_csr_rows(off, 0, n, 2 * m, 2 * m, row, s);
 }
 
 // The rows [s0, s1) of the max-eps CSR only, from neighbour pairs that each have at least one
@@ -308,7 +316,7 @@ Status launch_csr_scatter_batch(const uint64_t* edges, int64_t cap, const unsign
   csr_scatter_batch_kernel<<<static_cast<unsigned>(ceil_div(cap, 256)), 256, 0, s>>>(edges, cap, m_dev, off, s0, s1,
                                                                                      fill, col, err);
   DBM_CUDA(cudaGetLastError());
-  return launch_csr_rows(off, s0, s1, cap, row, s);
+  return launch_csr_rows(off, s0, s1, cap, cap, row, s);
 }
 
 // ---- the tile pairs of one row batch (memory-bounded fit) ----------------------------------
