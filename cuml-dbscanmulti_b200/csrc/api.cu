@@ -43,7 +43,8 @@ int64_t launches_so_far() { return g_launches.load(); }
 // launchers defined in dist.cu / graph.cu / cc.cu
 Status launch_distance(const DistLaunch& a, cudaStream_t s);
 Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s,
-                     const int32_t* perm = nullptr, int32_t rows = 0);
+                     const int32_t* perm = nullptr, int32_t rows = 0, float* box_lo = nullptr,
+                     float* box_hi = nullptr);
 int32_t padded_dims(int32_t d);
 int64_t padded_points(int64_t n);
 size_t order_scratch_bytes(int64_t n);
@@ -467,10 +468,11 @@ static Status distance_prepare(dbm_handle* h, const float* x, int64_t n, int32_t
   DBM_TRY(ensure(h->perm, sizeof(int32_t) * n));
   DBM_TRY(ensure(h->order_scratch, order_scratch_bytes(n)));
   DBM_TRY(spatial_order(x, n, di, as<int32_t>(h->perm), h->order_scratch.p, h->order_scratch.bytes, s));
-  DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, as<int32_t>(h->perm), xt_rows));
   DBM_TRY(ensure(h->box_lo, sizeof(float) * static_cast<size_t>(T) * di));
   DBM_TRY(ensure(h->box_hi, sizeof(float) * static_cast<size_t>(T) * di));
-  return launch_tile_boxes(as<float>(h->xt), n, padded_points(n), di, as<float>(h->box_lo), as<float>(h->box_hi), s);
+  // XT and the tile boxes (written by the transpose while each tile is in shared memory)
+  return transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, as<int32_t>(h->perm), xt_rows,
+                       as<float>(h->box_lo), as<float>(h->box_hi));
 }
 
 // With regrow, a pair buffer that turns out too small is grown to the exact count and the pass
@@ -719,14 +721,30 @@ static Status graph_prep(dbm_handle* h, int64_t n, int64_t d, int k, const int32
   return Status::Ok();
 }
 
-// Bytes of the smaller-eps slabs the labelling compacts per batch (annotated batches of a call
-// that owns a config of a smaller eps), sized by the largest batch.
-static uint64_t slab_bytes(const BatchPlan& bp, const std::vector<uint8_t>& routes, int k, int l, int cfg_begin)
+// Whether batch b's labelling walks compacted per-eps slabs (the reference's annotated route,
+// csr_multi_eps.cuh:194-234) or reads each max-eps entry's eps membership from its code.  The
+// labels are the same either way; compaction pays only for dense batches routed annotated (the
+// walks then cover the smaller eps' entries once each instead of the max-eps entries once per
+// eps), and only when the call owns a config of a smaller eps.  Sparse batches walk directly:
+// on C4 the per-batch compaction cost more than it saved (labelling 2.10 -> 1.76 ms).  The
+// reported route stays the reference's.
+static bool batch_compacts(const BatchPlan& bp, const std::vector<uint8_t>& routes, int64_t b, int64_t n, int k,
+                           int l, int cfg_begin)
 {
   const int ne = k - 1;
-  if (ne <= 0 || cfg_begin >= ne * l) return 0;
+  const int64_t rows = bp.rows(b, n);
+  return routes[b] != DBM_BATCH_DENSE && ne > 0 && cfg_begin < ne * l &&
+         bp.bnnz[b] - rows >= kDenseEntriesPerRow * rows;
+}
+
+// Bytes of the smaller-eps slabs the labelling compacts per batch (batch_compacts), sized by
+// the largest batch.
+static uint64_t slab_bytes(const BatchPlan& bp, const std::vector<uint8_t>& routes, int64_t n, int k, int l,
+                           int cfg_begin)
+{
+  const int ne = k - 1;
   bool any = false;
-  for (auto r : routes) any |= r == DBM_BATCH_ANNOTATED;
+  for (int64_t b = 0; b < bp.nb; ++b) any |= batch_compacts(bp, routes, b, n, k, l, cfg_begin);
   if (!any) return 0;
   return 2 * sizeof(int32_t) * static_cast<uint64_t>(std::max<int64_t>(bp.max_count, 1)) * ne +
          sizeof(int32_t) * bp.bs * ne + sizeof(int64_t) * (bp.bs * ne + 1);
@@ -772,7 +790,9 @@ static Status label_batches(dbm_handle* h, int64_t n, int k, int l, int cfg_begi
   for (int64_t b = 0; b < nb; ++b) dense_any |= bp.bnnz[b] - bp.rows(b, n) >= kDenseEntriesPerRow * bp.rows(b, n);
   if (dense_any) DBM_TRY(ensure(h->snap, kSnapBytesPerPoint * static_cast<uint64_t>(k) * n));
   const int ne = k - 1;  // smaller eps, compacted on the annotated route
-  if (ne > 0) {
+  bool compacts = false;
+  for (int64_t b = 0; b < nb; ++b) compacts |= batch_compacts(bp, routes, b, n, k, l, cfg_begin);
+  if (compacts) {
     DBM_TRY(ensure(h->slab_counts, sizeof(int32_t) * bs * ne));
     DBM_TRY(ensure(h->slab_off, sizeof(int64_t) * (bs * ne + 1)));
     DBM_TRY(ensure(h->slab_col, sizeof(int32_t) * std::max<int64_t>(bp.max_count * ne, 1)));
@@ -793,9 +813,7 @@ static Status label_batches(dbm_handle* h, int64_t n, int k, int l, int cfg_begi
     max_eps.col = reinterpret_cast<const int32_t*>(slab.col);
     max_eps.count = count;
     MultiSlab ms;
-    // smaller-eps slabs are only needed when this call owns a config of a smaller eps
-    const bool owns_small_eps = cfg_begin < ne * l;
-    if (routes[b] == DBM_BATCH_DENSE || ne == 0 || !owns_small_eps) {
+    if (!batch_compacts(bp, routes, b, n, k, l, cfg_begin)) {
       // direct: eps membership straight from each max-eps entry's code, no per-eps copies
       ms.direct = 1;
       ms.nslabs = 1;
@@ -906,8 +924,8 @@ static Status streamed_labels(dbm_handle* h, const float* x, int64_t n, int64_t 
     PhaseTimer t(h, s, &st.ms_distance);
     DBM_TRY(spatial_order(x, n, di, as<int32_t>(h->perm), h->order_scratch.p, h->order_scratch.bytes, s,
                           static_cast<int64_t>(bp.bs)));
-    DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, as<int32_t>(h->perm), xt_rows));
-    DBM_TRY(launch_tile_boxes(as<float>(h->xt), n, padded_points(n), di, as<float>(h->box_lo), as<float>(h->box_hi), s));
+    DBM_TRY(transpose_pad(x, as<float>(h->xt), n, di, as<int32_t>(h->err), s, as<int32_t>(h->perm), xt_rows,
+                          as<float>(h->box_lo), as<float>(h->box_hi)));
     const int64_t* count_dev = nullptr;
     DBM_TRY(launch_prune_count(T, as<float>(h->box_lo), as<float>(h->box_hi), di, eps2[k - 1], h->prune_scratch.p,
                                h->prune_scratch.bytes, h->scan_scratch.p, h->scan_scratch.bytes, &count_dev, s));
@@ -1000,7 +1018,7 @@ static Status fit(dbm_handle* h, const float* x, int64_t n, int64_t d, const flo
     DBM_TRY(free_memory(h, &free_b, &total_b));
     const uint64_t ws = h->workspace_bytes();
     auto grow = [](uint64_t want, const Buffer& b) { return want > b.bytes ? want - b.bytes : uint64_t(0); };
-    const uint64_t slabs = slab_bytes(bp, routes, k, l, 0);
+    const uint64_t slabs = slab_bytes(bp, routes, n, k, l, 0);
     const uint64_t need = (found > cap ? grow(8 * found, h->edges) : 0) + grow(8 * found, h->col) +
                           grow(8 * found, h->crow) + grow(slabs, h->slab_col) / 2 + grow(slabs, h->slab_row) / 2;
     const uint64_t room = std::min<uint64_t>(plan.budget > ws ? plan.budget - ws : 0, free_b);

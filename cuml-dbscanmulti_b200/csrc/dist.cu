@@ -386,37 +386,81 @@ __global__ void transpose_pad_kernel(const float* __restrict__ x, float* __restr
   }
 }
 
-// The same for d <= kTransposeMaxD: 64 points per block and every row of them at once, so each
-// point's row is gathered once (one contiguous 4d-byte read) and every XT row is written as
-// 256-byte runs.  Shared pitch d or d + 1, whichever is odd (conflict-free column reads).
-constexpr int kTransposePts = 64;
+// The same for d <= kTransposeMaxD: PTS points per block and every row of them at once, so each
+// point's row is gathered once (one contiguous 4d-byte read, eight loads in flight per thread)
+// and every XT row is written as 4 PTS-byte runs.  Shared pitch d or d + 1, whichever is odd
+// (conflict-free column reads).  With PTS = 128 a block is one 128-point tile and, given lo / hi,
+// also writes the tile's box (min / max of each dim over its points < n, dim-major
+// lo[t * tiles + tile]: what tile_box_kernel computes from XT) while the tile is in shared memory.
 constexpr int kTransposeMaxD = 128;
-__global__ void transpose_rows_kernel(const float* __restrict__ x, float* __restrict__ xt, int64_t n, int32_t d,
-                                      int32_t dp, int64_t npad, int32_t* __restrict__ err,
-                                      const int32_t* __restrict__ perm)
+constexpr int kTransposeBoxMaxD = 64;  // 128 x 65 floats: the fused box variant stays within 48 KB
+template <int PTS>
+__global__ void __launch_bounds__(256) transpose_rows_kernel(const float* __restrict__ x, float* __restrict__ xt,
+                                                             int64_t n, int32_t d, int32_t dp, int64_t npad,
+                                                             int32_t* __restrict__ err, const int32_t* __restrict__ perm,
+                                                             float* __restrict__ lo, float* __restrict__ hi)
 {
-  extern __shared__ float tile[];  // [kTransposePts][pitch]
-  __shared__ int32_t src[kTransposePts];
+  extern __shared__ float tile[];  // [PTS][pitch]
+  __shared__ int32_t src[PTS];
   const int pitch = d | 1;
-  const int64_t i0 = static_cast<int64_t>(blockIdx.x) * kTransposePts;
-  if (threadIdx.x < kTransposePts) {
+  const int64_t i0 = static_cast<int64_t>(blockIdx.x) * PTS;
+  if (threadIdx.x < PTS) {
     const int64_t i = i0 + threadIdx.x;
     src[threadIdx.x] = i < n ? (perm ? perm[i] : static_cast<int32_t>(i)) : -1;
   }
   __syncthreads();
   bool bad = false;
-  for (int idx = threadIdx.x; idx < kTransposePts * d; idx += blockDim.x) {
-    const int r = idx / d, t = idx - r * d;
-    const int32_t sr = src[r];
-    const float v = sr >= 0 ? x[static_cast<int64_t>(sr) * d + t] : 0.0f;
-    bad |= !isfinite(v);
-    tile[r * pitch + t] = v;
+  const int total = PTS * d;
+  constexpr int kInFlight = 8;
+  for (int base = threadIdx.x; base < total; base += kInFlight * 256) {
+    float v[kInFlight];
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const int idx = base + u * 256;
+      v[u] = 0.0f;
+      if (idx < total) {
+        const int r = idx / d, t = idx - r * d;
+        const int32_t sr = src[r];
+        if (sr >= 0) v[u] = x[static_cast<int64_t>(sr) * d + t];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const int idx = base + u * 256;
+      if (idx < total) {
+        const int r = idx / d, t = idx - r * d;
+        bad |= !isfinite(v[u]);
+        tile[r * pitch + t] = v[u];
+      }
+    }
   }
   if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(err, kErrNonFinite);
-  for (int idx = threadIdx.x; idx < dp * kTransposePts; idx += blockDim.x) {
-    const int t = idx / kTransposePts, r = idx - t * kTransposePts;
+  for (int idx = threadIdx.x; idx < dp * PTS; idx += blockDim.x) {
+    const int t = idx / PTS, r = idx - t * PTS;
     const int64_t i = i0 + r;
     if (i < npad) xt[static_cast<int64_t>(t) * npad + i] = t < d ? tile[r * pitch + t] : 0.0f;
+  }
+  if (PTS == 128 && lo) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int valid = n - i0 < PTS ? static_cast<int>(n - i0) : PTS;
+    const int64_t tiles = gridDim.x;
+    for (int t = warp; t < d; t += 8) {
+      float mn = INFINITY, mx = -INFINITY;
+      for (int r = lane; r < valid; r += 32) {
+        const float v = tile[r * pitch + t];
+        mn = fminf(mn, v);
+        mx = fmaxf(mx, v);
+      }
+#pragma unroll
+      for (int off = 16; off; off >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      }
+      if (lane == 0) {
+        lo[static_cast<int64_t>(t) * tiles + blockIdx.x] = mn;
+        hi[static_cast<int64_t>(t) * tiles + blockIdx.x] = mx;
+      }
+    }
   }
 }
 
@@ -439,21 +483,32 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn()
 int32_t padded_dims(int32_t d) { return (d + 3) / 4 * 4; }
 int64_t padded_points(int64_t n) { return (n + 3) / 4 * 4; }
 
+Status launch_tile_boxes(const float* xt, int64_t n, int64_t npad, int32_t d, float* lo, float* hi, cudaStream_t s);
+
 Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s,
-                     const int32_t* perm, int32_t rows)
+                     const int32_t* perm, int32_t rows, float* box_lo, float* box_hi)
 {
   const int32_t dp = rows > padded_dims(d) ? rows : padded_dims(d);
   const int64_t npad = padded_points(n);
   count_launch();
+  if (d <= kTransposeBoxMaxD) {
+    // one block per 128-point tile (npad <= 128 * tiles), boxes written on the way when asked
+    const size_t smem = sizeof(float) * 128 * static_cast<size_t>(d | 1);
+    transpose_rows_kernel<128><<<static_cast<unsigned>(ceil_div(npad, 128)), 256, smem, s>>>(
+      x, xt, n, d, dp, npad, err, perm, box_lo, box_hi);
+    DBM_CUDA(cudaGetLastError());
+    return Status::Ok();
+  }
   if (d <= kTransposeMaxD) {
-    const size_t smem = sizeof(float) * kTransposePts * static_cast<size_t>(d | 1);
-    transpose_rows_kernel<<<static_cast<unsigned>(ceil_div(npad, kTransposePts)), 256, smem, s>>>(x, xt, n, d, dp, npad,
-                                                                                                  err, perm);
+    const size_t smem = sizeof(float) * 64 * static_cast<size_t>(d | 1);
+    transpose_rows_kernel<64><<<static_cast<unsigned>(ceil_div(npad, 64)), 256, smem, s>>>(x, xt, n, d, dp, npad, err,
+                                                                                           perm, nullptr, nullptr);
   } else {
     dim3 grid(static_cast<unsigned>(ceil_div(npad, 32)), static_cast<unsigned>(ceil_div(dp, 32)));
     transpose_pad_kernel<<<grid, dim3(32, 8), 0, s>>>(x, xt, n, d, dp, npad, err, perm);
   }
   DBM_CUDA(cudaGetLastError());
+  if (box_lo) return launch_tile_boxes(xt, n, npad, d, box_lo, box_hi, s);
   return Status::Ok();
 }
 

@@ -30,7 +30,8 @@ namespace dbm {
 
 Status launch_distance(const DistLaunch& a, cudaStream_t s);
 Status transpose_pad(const float* x, float* xt, int64_t n, int32_t d, int32_t* err, cudaStream_t s,
-                     const int32_t* perm = nullptr, int32_t rows = 0);
+                     const int32_t* perm = nullptr, int32_t rows = 0, float* box_lo = nullptr,
+                     float* box_hi = nullptr);
 int32_t padded_dims(int32_t d);
 int64_t padded_points(int64_t n);
 

@@ -77,13 +77,17 @@ __device__ __forceinline__ void unit_coords(int64_t u, int64_t tiles, int64_t& J
 }
 
 // One warp per unit: the tiles I of the unit's block (I <= J) whose boxes may meet J's (I == J
-// always).  The bound's chain is checked every 4 dims, after loading those dims together (lb
-// only grows along the dims, so stopping later is as exact).  Writes the unit's keep mask
-// (bit q of word c: I = block start + 32 c + q) and its count.
+// always).  The bound's chain runs over the dims in order and is checked after each group of
+// dims loaded together (lb only grows along the dims, so stopping later is as exact).  The
+// first 4 dims of all four 32-tile steps are loaded and chained together (one round of L2
+// latency per unit: the Z-order sorts these dims, so they drop most tile pairs), then each step
+// with survivors continues its chains from dim 4, 8 dims per round of loads.  Writes the unit's
+// keep mask (bit q of word c: I = block start + 32 c + q) and its count.
 __global__ void tile_pairs_kernel(int64_t tiles, int64_t u0, int64_t u1, const float* __restrict__ lo,
                                   const float* __restrict__ hi, int32_t d, float cutoff, int32_t* __restrict__ counts,
                                   uint32_t* __restrict__ masks)
 {
+  constexpr int kSteps = static_cast<int>(kUnitTiles / 32);
   const int64_t u = u0 + ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (u >= u1) return;
@@ -92,16 +96,43 @@ __global__ void tile_pairs_kernel(int64_t tiles, int64_t u0, int64_t u1, const f
   int32_t total = 0;
   const int64_t i0 = blk * kUnitTiles;
   const int64_t i1 = i0 + kUnitTiles - 1 < J ? i0 + kUnitTiles - 1 : J;
-#pragma unroll 1
-  for (int c = 0; c < static_cast<int>(kUnitTiles / 32); ++c) {
+  float jl[4], jh[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    jl[q] = q < d ? __ldg(lo + static_cast<int64_t>(q) * tiles + J) : 0.0f;
+    jh[q] = q < d ? __ldg(hi + static_cast<int64_t>(q) * tiles + J) : 0.0f;
+  }
+  float lb0[kSteps];
+  bool live[kSteps];
+#pragma unroll
+  for (int c = 0; c < kSteps; ++c) {
+    const int64_t I = i0 + 32 * c + lane;
+    live[c] = I <= i1 && I != J;
+    float gq[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      gq[q] = 0.0f;
+      if (live[c] && q < d) {
+        const int64_t ti = static_cast<int64_t>(q) * tiles;
+        gq[q] = fmaxf(0.0f, fmaxf(__fsub_rn(jl[q], __ldg(hi + ti + I)), __fsub_rn(__ldg(lo + ti + I), jh[q])));
+      }
+    }
+    float lb = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) lb = __fmaf_rn(gq[q], gq[q], lb);
+    lb0[c] = lb;
+  }
+#pragma unroll
+  for (int c = 0; c < kSteps; ++c) {
     const int64_t I = i0 + 32 * c + lane;
     bool keep = I <= i1;
-    if (keep && I != J) {
-      float lb = 0.0f;
-      for (int32_t t0 = 0; t0 < d; t0 += 4) {
-        float gq[4];
+    if (live[c]) {
+      float lb = lb0[c];
+      if (lb > cutoff) keep = false;
+      for (int32_t t0 = 4; keep && t0 < d; t0 += 8) {
+        float gq[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 8; ++q) {
           const int32_t t = t0 + q;
           gq[q] = 0.0f;
           if (t < d) {
@@ -111,7 +142,7 @@ __global__ void tile_pairs_kernel(int64_t tiles, int64_t u0, int64_t u1, const f
           }
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q) lb = __fmaf_rn(gq[q], gq[q], lb);
+        for (int q = 0; q < 8; ++q) lb = __fmaf_rn(gq[q], gq[q], lb);
         if (lb > cutoff) {
           keep = false;
           break;
