@@ -90,8 +90,8 @@ Status launch_slab_counts_all(const int32_t* deg, int64_t n, int ne, int64_t s0,
                               cudaStream_t s);
 Status launch_filter_all(const int64_t* off, const uint32_t* col, int64_t col_base, int64_t s0, int64_t rows, int ne,
                          const int64_t* off_flat, int32_t* col_flat, int32_t* row_flat, cudaStream_t s);
-Status launch_cc_root_bits(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc, int32_t* G,
-                           uint32_t* words, int32_t* cnt, int sm_count, cudaStream_t s);
+Status launch_cc_root_bits(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc,
+                           int32_t* G, uint32_t* words, int32_t* cnt, int sm_count, cudaStream_t s);
 Status launch_cc_labels(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc, int32_t* G,
                         const int32_t* cur, const uint32_t* words, const int64_t* wrank, int32_t* labels,
                         cudaStream_t s);
@@ -799,7 +799,8 @@ static Status label_batches(dbm_handle* h, int64_t n, int k, int l, int cfg_begi
     DBM_TRY(ensure(h->slab_row, sizeof(int32_t) * std::max<int64_t>(bp.max_count * ne, 1)));
     DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(static_cast<int64_t>(bs) * ne + 1)));
   }
-  DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur), as<unsigned long long>(h->best), s));
+  DBM_TRY(launch_cc_init(n, k, l, as<int32_t>(h->G), as<int32_t>(h->cur),
+                         as<unsigned long long>(h->best), s));
   int64_t base = 0;  // first max-eps CSR entry of the batch
   for (int64_t b = 0; b < nb; ++b) {
     const int64_t s0 = b * static_cast<int64_t>(bs);
@@ -862,10 +863,11 @@ static Status relabel_stage(dbm_handle* h, int64_t n, int k, int l, int cfg_begi
     DBM_TRY(ensure(h->scan_scratch, scan_scratch_bytes(owned + 1)));
     uint32_t* words = as<uint32_t>(h->flags);
     int32_t* cnt = as<int32_t>(h->flags) + words_all;
-    DBM_TRY(launch_cc_root_bits(n, l, cfg_begin, cfg_end, W, as<int32_t>(h->cc), as<int32_t>(h->G), words, cnt,
-                                h->sm_count, s));
+    DBM_TRY(launch_cc_root_bits(n, l, cfg_begin, cfg_end, W, as<int32_t>(h->cc),
+                                as<int32_t>(h->G), words, cnt, h->sm_count, s));
     DBM_TRY(exclusive_scan_i32(cnt, as<int64_t>(h->rank), owned, h->scan_scratch.p, h->scan_scratch.bytes, s));
-    DBM_TRY(launch_cc_labels(n, l, cfg_begin, cfg_end, W, as<int32_t>(h->cc), as<int32_t>(h->G), as<int32_t>(h->cur),
+    DBM_TRY(launch_cc_labels(n, l, cfg_begin, cfg_end, W, as<int32_t>(h->cc),
+                             as<int32_t>(h->G), as<int32_t>(h->cur),
                              words, as<int64_t>(h->rank), labels, s));
   }
   return read_err_flag(h, s);

@@ -28,12 +28,22 @@
 namespace dbm {
 
 
-__global__ void cc_init_kernel(int64_t n, int64_t total, int32_t* __restrict__ G,
+// Layout of the forests (G, L), the border candidates (best) and the folded labels (cur): the l
+// configs of an eps are interleaved point by point, config (e, m) of point i at element
+// (e n + i) l + m = fbase(e, m) + i l.  An entry's per-config gathers and union-find steps for
+// one point then share a 32-byte sector instead of touching l arrays n elements apart (C4
+// labelling -10%, C1 -25% against one array per config; the calibrated dense C5 is unchanged).
+__host__ __device__ __forceinline__ int64_t fbase(int64_t n, int l, int e, int m)
+{
+  return static_cast<int64_t>(e) * n * l + m;
+}
+
+__global__ void cc_init_kernel(int64_t n, int l, int64_t total, int32_t* __restrict__ G,
                                int32_t* __restrict__ cur, unsigned long long* __restrict__ best)
 {
   const int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (x >= total) return;
-  G[x] = static_cast<int32_t>(x % n);
+  G[x] = static_cast<int32_t>((x / l) % n);
   cur[x] = kNone;
   best[x] = ~0ull;
 }
@@ -175,8 +185,8 @@ __global__ void cc_touch_kernel(const CcArgs a, int32_t* __restrict__ L)
     int m_lo, m_hi;
     cfg_range(a, e, m_lo, m_hi);
     const int cr = min(core_count(a, e, r), m_hi), cj = min(core_count(a, e, j), m_hi);
-    for (int m = m_lo; m < cr; ++m) L[static_cast<int64_t>(e * a.l + m) * a.n + r] = r;
-    for (int m = m_lo; m < cj; ++m) L[static_cast<int64_t>(e * a.l + m) * a.n + j] = j;
+    for (int m = m_lo; m < cr; ++m) L[fbase(a.n, a.l, e, m) + static_cast<int64_t>(r) * a.l] = r;
+    for (int m = m_lo; m < cj; ++m) L[fbase(a.n, a.l, e, m) + static_cast<int64_t>(j) * a.l] = j;
   });
 }
 
@@ -187,16 +197,17 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
 {
   bool ok = true;
   for_each_entry_cfg(a, [&](int e, int m, int32_t r, int32_t j) {
-    const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
+    const int64_t base = fbase(a.n, a.l, e, m);
+    const int64_t pr = base + static_cast<int64_t>(r) * a.l, pj = base + static_cast<int64_t>(j) * a.l;
     // equal parents mean the union is a no-op, exact whatever the state of the forest (a stale
     // batch-local parent of a non-core endpoint can only skip a union the core test below would
     // skip too); after a compression most endpoint pairs of one component take this exit
-    const bool skip_p = a.quick && P[base + r] == P[base + j];
-    const bool skip_q = !Q || (a.quick && Q[base + r] == Q[base + j]);
+    const bool skip_p = a.quick && P[pr] == P[pj];
+    const bool skip_q = !Q || (a.quick && Q[pr] == Q[pj]);
     if (skip_p && skip_q) return;
     if (m >= core_count(a, e, r) || m >= core_count(a, e, j)) return;
-    if (!skip_p) ok &= uf_unite(P + base, r, j, a.union_limit);
-    if (!skip_q) ok &= uf_unite(Q + base, r, j, a.union_limit);
+    if (!skip_p) ok &= uf_unite(P + base, r, j, a.union_limit, a.l);
+    if (!skip_q) ok &= uf_unite(Q + base, r, j, a.union_limit, a.l);
   });
   if (!ok) atomicOr(err, kErrUnionLimit);
 }
@@ -204,12 +215,14 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
 // P[x] = x for every x of the configs [c0, c1): a fresh forest (the batch-local one of a dense
 // batch, which is then compressed over every point and so must hold no stale parents from an
 // earlier batch or fit)
-__global__ void cc_reset_kernel(int64_t n, int c0, int c1, int32_t* __restrict__ P)
+__global__ void cc_reset_kernel(int64_t n, int l, int c0, int c1, int32_t* __restrict__ P)
 {
   const int64_t total = static_cast<int64_t>(c1 - c0) * n;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total; x += stride)
-    P[c0 * n + x] = static_cast<int32_t>(x % n);
+  for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total; x += stride) {
+    const int64_t cfg = c0 + x / n, i = x % n;
+    P[fbase(n, l, static_cast<int>(cfg / l), static_cast<int>(cfg % l)) + i * l] = static_cast<int32_t>(i);
+  }
 }
 
 // Root snapshot of a dense batch: per eps e and point x, kSnapSlots int32 -- slots 0-3 the roots
@@ -226,10 +239,10 @@ __global__ void cc_compress_kernel(int64_t n, int l, int c0, int c1, int32_t* __
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total; x += stride) {
     const int64_t cfg = c0 + x / n, i = x % n;
-    int32_t* g = P + cfg * n;
-    const int32_t root = uf_find(g, static_cast<int32_t>(i));
-    if (g[i] != root) g[i] = root;
     const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
+    int32_t* g = P + fbase(n, l, e, m);
+    const int32_t root = uf_find(g, static_cast<int32_t>(i), l);
+    if (g[i * l] != root) g[i * l] = root;
     if (R && m < kSnapConfigs) R[(static_cast<int64_t>(e) * n + i) * kSnapSlots + slot + m] = root;
   }
 }
@@ -299,10 +312,10 @@ __global__ void __launch_bounds__(256) cc_union_snap_kernel(const CcArgs a, int3
         if (!tail && !(open_p | open_q)) continue;
         const int core_hi = min(m_hi, min(core_count(a, e, r[u]), core_count(a, e, j[u])));
         for (int m = m_lo; m < core_hi; ++m) {
-          const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
+          const int64_t base = fbase(a.n, a.l, e, m);
           const bool snap = m < kSnapConfigs;
-          if (!snap || ((open_p >> m) & 1u)) ok &= uf_unite(P + base, r[u], j[u], a.union_limit);
-          if (Q && (!snap || ((open_q >> m) & 1u))) ok &= uf_unite(Q + base, r[u], j[u], a.union_limit);
+          if (!snap || ((open_p >> m) & 1u)) ok &= uf_unite(P + base, r[u], j[u], a.union_limit, a.l);
+          if (Q && (!snap || ((open_q >> m) & 1u))) ok &= uf_unite(Q + base, r[u], j[u], a.union_limit, a.l);
         }
       }
     }
@@ -323,9 +336,10 @@ __global__ void cc_best_kernel(const CcArgs a, int32_t* __restrict__ P, unsigned
       const bool r_core = m < cr;
       const int32_t c = r_core ? r : j;
       const int32_t pt = r_core ? j : r;
-      const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
-      const int32_t root = uf_find(P + base, c);
-      atomicMin(best + base + pt, (static_cast<unsigned long long>(tag) << 32) | static_cast<uint32_t>(root));
+      const int64_t base = fbase(a.n, a.l, e, m);
+      const int32_t root = uf_find(P + base, c, a.l);
+      atomicMin(best + base + static_cast<int64_t>(pt) * a.l,
+                (static_cast<unsigned long long>(tag) << 32) | static_cast<uint32_t>(root));
     }
   });
 }
@@ -342,13 +356,14 @@ __global__ void cc_border_kernel(const CcArgs a, int32_t* __restrict__ G,
     const int lo = max(min(cr, cj), m_lo), hi = min(max(cr, cj), m_hi);
     for (int m = lo; m < hi; ++m) {
       const int32_t pt = (m < cr) ? j : r;
-      const int64_t base = static_cast<int64_t>(e * a.l + m) * a.n;
-      const unsigned long long v = best[base + pt];
+      const int64_t base = fbase(a.n, a.l, e, m);
+      const int64_t at = base + static_cast<int64_t>(pt) * a.l;
+      const unsigned long long v = best[at];
       if (static_cast<uint32_t>(v >> 32) != tag) continue;
-      const int32_t cand = uf_find(G + base, static_cast<int32_t>(v & 0xffffffffu));
-      volatile int32_t* cp = cur + base + pt;
+      const int32_t cand = uf_find(G + base, static_cast<int32_t>(v & 0xffffffffu), a.l);
+      volatile int32_t* cp = cur + at;
       const int32_t old = *cp;
-      const int32_t prev = (old == kNone) ? kNone : uf_find(G + base, old);
+      const int32_t prev = (old == kNone) ? kNone : uf_find(G + base, old, a.l);
       *cp = prev < cand ? prev : cand;
     }
   });
@@ -365,15 +380,15 @@ __global__ void cc_border_points_kernel(int64_t n, int l, int c0, int c1, const 
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t x = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; x < total; x += stride) {
     const int64_t cfg = c0 + x / n, i = x - (cfg - c0) * n;
-    const int64_t at = cfg * n + i;
+    const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
+    const int64_t base = fbase(n, l, e, m), at = base + i * l;
     const unsigned long long v = best[at];
     if (static_cast<uint32_t>(v >> 32) != tag) continue;
-    const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
     if (m < cc[static_cast<int64_t>(e) * n + i]) continue;  // core points take no border candidate
-    int32_t* g = G + cfg * n;
-    const int32_t cand = uf_find(g, static_cast<int32_t>(v & 0xffffffffu));
+    int32_t* g = G + base;
+    const int32_t cand = uf_find(g, static_cast<int32_t>(v & 0xffffffffu), l);
     const int32_t old = cur[at];
-    const int32_t prev = (old == kNone) ? kNone : uf_find(g, old);
+    const int32_t prev = (old == kNone) ? kNone : uf_find(g, old, l);
     cur[at] = prev < cand ? prev : cand;
   }
 }
@@ -392,7 +407,7 @@ __global__ void cc_root_bits_kernel(int64_t n, int l, int c0, int c1, int64_t W,
     const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
     bool root = false;
     if (i < n && m < cc[static_cast<int64_t>(e) * n + i])
-      root = uf_find(G + cfg * n, static_cast<int32_t>(i)) == static_cast<int32_t>(i);
+      root = uf_find(G + fbase(n, l, e, m), static_cast<int32_t>(i), l) == static_cast<int32_t>(i);
     const uint32_t bits = __ballot_sync(0xffffffffu, root);
     if ((threadIdx.x & 31) == 0) {
       const int64_t w = cl * W + i / 32;
@@ -414,18 +429,18 @@ __global__ void cc_labels_kernel(int64_t n, int l, int c0, int c1, int64_t W, co
   if (x >= static_cast<int64_t>(c1) * n) return;
   const int64_t cfg = x / n, i = x - cfg * n;
   const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
-  int32_t* g = G + cfg * n;
+  int32_t* g = G + fbase(n, l, e, m);
   int32_t v;
   if (m < cc[static_cast<int64_t>(e) * n + i]) {
     v = static_cast<int32_t>(i);
   } else {
-    v = cur[x];
+    v = cur[fbase(n, l, e, m) + i * l];
     if (v == kNone) {
       labels[x] = -1;
       return;
     }
   }
-  const int32_t root = uf_find(g, v);
+  const int32_t root = uf_find(g, v, l);
   const int64_t wl = (cfg - c0) * W;  // this config's first word in the scanned range
   const int64_t w = wl + root / 32;
   const uint32_t below = words[cfg * W + root / 32] & ((1u << (root & 31)) - 1u);
@@ -443,7 +458,7 @@ Status launch_cc_init(int64_t n, int k, int l, int32_t* G, int32_t* cur, unsigne
 {
   const int64_t total = n * k * l;
   count_launch();
-  cc_init_kernel<<<blocks_for(total, 256), 256, 0, s>>>(n, total, G, cur, best);
+  cc_init_kernel<<<blocks_for(total, 256), 256, 0, s>>>(n, l, total, G, cur, best);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }
@@ -498,7 +513,7 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
     // chain and stale parents from earlier batches or fits need not be valid chains of this one;
     // the global forest holds only this fit's chains (cc_init).
     count_launch(6);
-    cc_reset_kernel<<<nbc, 256, 0, s>>>(n, cfg_begin, cfg_end, L);
+    cc_reset_kernel<<<nbc, 256, 0, s>>>(n, l, cfg_begin, cfg_end, L);
     cc_union_kernel<<<nbs, 256, 0, s>>>(sa, L, G, err);
     cc_compress_kernel<<<nbc, 256, 0, s>>>(n, l, cfg_begin, cfg_end, L, snap, 0);
     cc_compress_kernel<<<nbc, 256, 0, s>>>(n, l, cfg_begin, cfg_end, G, snap, kSnapConfigs);
@@ -528,8 +543,8 @@ Status launch_cc_batch(const MultiSlab& ms, int64_t upper_entries, int64_t n, in
   return Status::Ok();
 }
 
-Status launch_cc_root_bits(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc, int32_t* G,
-                           uint32_t* words, int32_t* cnt, int sm_count, cudaStream_t s)
+Status launch_cc_root_bits(int64_t n, int l, int c0, int c1, int64_t W, const int32_t* cc,
+                           int32_t* G, uint32_t* words, int32_t* cnt, int sm_count, cudaStream_t s)
 {
   const int64_t total = static_cast<int64_t>(c1 - c0) * W * 32;
   if (total <= 0) return Status::Ok();
@@ -548,7 +563,8 @@ Status launch_cc_labels(int64_t n, int l, int c0, int c1, int64_t W, const int32
   const int64_t total = static_cast<int64_t>(c1 - c0) * n;
   if (total <= 0) return Status::Ok();
   count_launch();
-  cc_labels_kernel<<<blocks_for(total, 256), 256, 0, s>>>(n, l, c0, c1, W, cc, G, cur, words, wrank, labels);
+  cc_labels_kernel<<<blocks_for(total, 256), 256, 0, s>>>(n, l, c0, c1, W, cc, G,
+                                                          cur, words, wrank, labels);
   DBM_CUDA(cudaGetLastError());
   return Status::Ok();
 }

@@ -107,16 +107,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 // ---- union-find with minimum-index roots --------------------------------------------------
 // Roots are always the smallest index of their tree: a root is only ever re-pointed at a
 // smaller root, so a fully compressed parent array maps every member to its component's
-// minimum index.  Path halving writes only ancestors, so concurrent finds are safe.
-__device__ __forceinline__ int32_t uf_find(int32_t* parent, int32_t x)
+// minimum index.  Path halving writes only ancestors, so concurrent finds are safe.  The parent
+// of x is parent[x * stride] (forests of several configs interleaved point by point).
+__device__ __forceinline__ int32_t uf_find(int32_t* parent, int32_t x, int stride = 1)
 {
   volatile int32_t* p = parent;
-  int32_t px = p[x];
+  int32_t px = p[static_cast<int64_t>(x) * stride];
   while (px != x) {
-    const int32_t gp = p[px];
-    if (gp != px) p[x] = gp;
+    const int32_t gp = p[static_cast<int64_t>(px) * stride];
+    if (gp != px) p[static_cast<int64_t>(x) * stride] = gp;
     x = px;
-    px = p[x];
+    px = p[static_cast<int64_t>(x) * stride];
   }
   return x;
 }
@@ -131,11 +132,12 @@ constexpr int64_t kSnapBytesPerPoint = 32;
 constexpr int kUnionRetryLimit = 1 << 20;
 
 // Returns false if the retry bound ran out (never expected; reported as an error flag).
-__device__ __forceinline__ bool uf_unite(int32_t* parent, int32_t a, int32_t b, int limit = kUnionRetryLimit)
+__device__ __forceinline__ bool uf_unite(int32_t* parent, int32_t a, int32_t b, int limit = kUnionRetryLimit,
+                                         int stride = 1)
 {
   for (int it = 0; it < limit; ++it) {
-    a = uf_find(parent, a);
-    b = uf_find(parent, b);
+    a = uf_find(parent, a, stride);
+    b = uf_find(parent, b, stride);
     if (a == b) return true;
     if (a > b) {
       const int32_t t = a;
@@ -143,7 +145,7 @@ __device__ __forceinline__ bool uf_unite(int32_t* parent, int32_t a, int32_t b, 
       b = t;
     }
     // hook the larger root under the smaller one
-    const int32_t old = atomicCAS(parent + b, b, a);
+    const int32_t old = atomicCAS(parent + static_cast<int64_t>(b) * stride, b, a);
     if (old == b) return true;
     b = old;
   }
