@@ -723,18 +723,19 @@ static Status graph_prep(dbm_handle* h, int64_t n, int64_t d, int k, const int32
 
 // Whether batch b's labelling walks compacted per-eps slabs (the reference's annotated route,
 // csr_multi_eps.cuh:194-234) or reads each max-eps entry's eps membership from its code.  The
-// labels are the same either way; compaction pays only for dense batches routed annotated (the
+// labels are the same either way.  Compaction (one pass over the max-eps entries) needs a call
+// that owns a config of a smaller eps, and pays only for dense batches routed annotated: the
 // walks then cover the smaller eps' entries once each instead of the max-eps entries once per
-// eps), and only when the call owns a config of a smaller eps.  Sparse batches walk directly:
-// on C4 the per-batch compaction cost more than it saved (labelling 2.10 -> 1.76 ms).  The
-// reported route stays the reference's.
+// eps.  Sparse batches walk directly: on C4 the per-batch compaction cost more than it saved,
+// for the whole grid (labelling 2.10 -> 1.76 ms) and for a multi-GPU rank that owns only
+// smaller-eps configs alike.  The reported route stays the reference's.
 static bool batch_compacts(const BatchPlan& bp, const std::vector<uint8_t>& routes, int64_t b, int64_t n, int k,
                            int l, int cfg_begin)
 {
   const int ne = k - 1;
+  if (routes[b] == DBM_BATCH_DENSE || ne <= 0 || cfg_begin >= ne * l) return false;
   const int64_t rows = bp.rows(b, n);
-  return routes[b] != DBM_BATCH_DENSE && ne > 0 && cfg_begin < ne * l &&
-         bp.bnnz[b] - rows >= kDenseEntriesPerRow * rows;
+  return bp.bnnz[b] - rows >= kDenseEntriesPerRow * rows;
 }
 
 // Bytes of the smaller-eps slabs the labelling compacts per batch (batch_compacts), sized by

@@ -44,17 +44,15 @@ def config_range(c: int, rank: int, world: int) -> tuple[int, int]:
     return c * rank // world, c * (rank + 1) // world
 
 
-# Relative per-element costs of the labelling kernels, fitted to C4 timings on one and two GPUs
-# (per rank: one walk of the eps = 4.5 slab ~0.83 ms for 3.86e6 entries, each further config's
-# union ~0.19 ms, the per-batch compaction of the smaller-eps slabs ~0.7 ms, relabel ~0.014 ms per
-# config and 1e6 points): the slab walks per entry of an eps the rank owns any config of; the
-# compaction per max-eps entry, paid once by a rank that owns any config of a smaller eps (it
-# reads every max-eps entry of every batch); the union per (entry, owned config); the relabel per
-# (point, owned config).
-LABEL_COST_WALK = 22.0
-LABEL_COST_COMPACT = 18.0
-LABEL_COST_UNION = 4.9
-LABEL_COST_RELABEL = 1.4
+# Per-element costs of the labelling kernels in ns, fitted to C4 config-range timings on one
+# GPU (dbm_fit_multi_from_graph; 8 batches, 3.84e6 max-eps entries): sparse batches walk the
+# max-eps entries with their codes, so every rank that owns a config pays one walk of them
+# (~0.13 ms) whatever its eps; the union per (entry of the config's eps, owned config), ~0.045 ms
+# per 1e6; the relabel per (point, owned config), ~0.013 ms per 1e6.  The per-rank fixed part
+# (~0.45 ms of launches and initialisation) is the same on every rank and does not move the split.
+LABEL_COST_WALK = 0.034
+LABEL_COST_UNION = 0.045
+LABEL_COST_RELABEL = 0.0134
 
 
 class _LabelCost:
@@ -63,18 +61,14 @@ class _LabelCost:
     def __init__(self, per_eps: list[float], l: int, n: int):
         self.l, self.n, self.k = int(l), int(n), len(per_eps)
         self.last = float(per_eps[-1]) if per_eps else 0.0
-        self.eps_pre = np.concatenate([[0.0], np.cumsum(np.asarray(per_eps, dtype=np.float64))])
         per_cfg = np.repeat(np.asarray(per_eps, dtype=np.float64), self.l)
         self.cfg_pre = np.concatenate([[0.0], np.cumsum(per_cfg)])
 
     def __call__(self, a: int, b: int) -> float:
         if b <= a:
             return 0.0
-        e0, e1 = a // self.l, (b - 1) // self.l
-        walk = self.eps_pre[e1 + 1] - self.eps_pre[e0]
-        compact = self.last if e0 < self.k - 1 else 0.0
         union = self.cfg_pre[b] - self.cfg_pre[a]
-        return float(LABEL_COST_WALK * walk + LABEL_COST_COMPACT * compact + LABEL_COST_UNION * union
+        return float(LABEL_COST_WALK * self.last + LABEL_COST_UNION * union
                      + LABEL_COST_RELABEL * self.n * (b - a))
 
 
@@ -86,10 +80,10 @@ def labelling_cost(per_eps: list[float], l: int, n: int, a: int, b: int) -> floa
 def labelling_ranges(per_eps: list[float], l: int, n: int, world: int) -> list[tuple[int, int]]:
     """Contiguous config ranges, one per rank, minimising the largest modelled labelling cost
     (bisection on the bound with a greedy feasibility sweep; the cost of a range only grows as
-    it widens).  A rank's cost counts each eps it touches once for the slab walks and the
-    compaction once if it owns any smaller-eps config, so the split prefers to keep an eps's
-    configs together and the largest eps's configs apart from the rest.  Deterministic: every
-    rank computes the same split from the same (all-reduced) entry counts."""
+    it widens).  Every rank that owns a config walks the max-eps entries once; the unions scale
+    with the entries of each owned config's eps, so the largest eps's configs are spread over
+    ranks.  Deterministic: every rank computes the same split from the same (all-reduced) entry
+    counts."""
     c = len(per_eps) * l
     if world <= 1 or c == 0:
         return [(0, c)] + [(c, c)] * max(0, world - 1)
