@@ -476,17 +476,20 @@ def label_roofline(nnz_eps, n, l, stats, label_ms, ws) -> dict:
     """HBM roofline of the labelling (per-batch compaction, batched connected components, border
     fold, relabel).  Algorithmic bytes per grid, the CC accounting of one sweep per configuration
     (a column index and a label gather per entry, the labels read and written, the core mask):
-    sum over configs of 8 * nnz(eps of the config) + 8 N + N / 8; plus, on annotated batches, the
-    compaction's 4 bytes read per max-eps entry and 8 bytes written per kept smaller-eps entry.
-    Over the phase's event time (the labelling kernels' share of the step)."""
+    sum over configs of 8 * nnz(eps of the config) + 8 N + N / 8; plus, where the fit compacts the
+    smaller-eps slabs (annotated batches of a dense graph, >= 64 entries per row; sparse batches
+    read each entry's eps from its code instead), the compaction's 4 bytes read per max-eps entry
+    and 8 bytes written per kept smaller-eps entry.  Over the phase's event time (the labelling
+    kernels' share of the step)."""
     mp = measured_peaks()
     peak = mp.get("hbm_gbs") or 6650.0
     bytes_cc = sum(l * (8.0 * v + 8.0 * n + n / 8.0) for v in nnz_eps)
-    annotated = int(stats.get("annotated_batches", 0) or 0) > 0
-    bytes_compact = (4.0 * nnz_eps[-1] + 8.0 * sum(nnz_eps[:-1])) if annotated and len(nnz_eps) > 1 else 0.0
+    compacts = int(stats.get("annotated_batches", 0) or 0) > 0 and bool(nnz_eps) and nnz_eps[-1] >= 64 * n
+    bytes_compact = (4.0 * nnz_eps[-1] + 8.0 * sum(nnz_eps[:-1])) if compacts and len(nnz_eps) > 1 else 0.0
     ms = float(np.mean(label_ms)) if label_ms else float("nan")
     achieved = (bytes_cc + bytes_compact) / (ms * 1e-3) / 1e9 if ms and ms > 0 else None
-    return {"bound": "hbm", "kernels": "filter_all, cc_touch/union/best/border, cc_root_bits/labels",
+    return {"bound": "hbm", "kernels": "filter_all (dense annotated batches), cc_touch/union/best/border, "
+                                       "cc_root_bits/labels",
             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak if achieved else None,
             "peak_source": "MEASURED_PEAKS.json hbm_gbs" if mp.get("hbm_gbs") else "fallback 6650 GB/s",
             "bytes_per_grid": bytes_cc + bytes_compact, "ms_per_grid": ms, "traffic": None,

@@ -89,9 +89,10 @@ __device__ __forceinline__ void for_each_entry(const CcArgs& a, F&& f)
     for (int64_t q = t0; q < s.count; q += stride) {
       const uint32_t w = static_cast<uint32_t>(s.col[q]);
       const int32_t j = static_cast<int32_t>(w & kColMask);
-      const int32_t r = s.row[q];
       const int e0 = max(static_cast<int>(w >> kCodeShift), a.cfg_begin / a.l);
       const int e1 = min(a.k, (a.cfg_end + a.l - 1) / a.l);  // owned eps [e0, e1)
+      if (e0 >= e1) continue;  // beyond every owned eps: the row index is not even read
+      const int32_t r = s.row[q];
       for (int e = e0; e < e1; ++e) f(e, r, j);
     }
   } else {
@@ -151,9 +152,10 @@ __device__ __forceinline__ void for_each_entry_cfg(const CcArgs& a, F&& f)
       const int64_t q = c.q << sh;
       const uint32_t w = static_cast<uint32_t>(s.col[q]);
       const int32_t j = static_cast<int32_t>(w & kColMask);
-      const int32_t r = s.row[q];
       const int e0 = max(static_cast<int>(w >> kCodeShift), a.cfg_begin / a.l);
       const int e1 = min(a.k, (a.cfg_end + a.l - 1) / a.l);  // owned eps [e0, e1)
+      if (e0 >= e1) continue;
+      const int32_t r = s.row[q];
       for (int e = e0; e < e1; ++e) {
         int m_lo, m_hi;
         cfg_range(a, e, m_lo, m_hi);
