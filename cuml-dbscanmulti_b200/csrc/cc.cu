@@ -201,13 +201,15 @@ __global__ void cc_union_kernel(const CcArgs a, int32_t* __restrict__ P, int32_t
   for_each_entry_cfg(a, [&](int e, int m, int32_t r, int32_t j) {
     const int64_t base = fbase(a.n, a.l, e, m);
     const int64_t pr = base + static_cast<int64_t>(r) * a.l, pj = base + static_cast<int64_t>(j) * a.l;
+    // the core counts are read together with the parents (one round of memory latency, not two)
+    const int cr = core_count(a, e, r), cj = core_count(a, e, j);
     // equal parents mean the union is a no-op, exact whatever the state of the forest (a stale
     // batch-local parent of a non-core endpoint can only skip a union the core test below would
     // skip too); after a compression most endpoint pairs of one component take this exit
     const bool skip_p = a.quick && P[pr] == P[pj];
     const bool skip_q = !Q || (a.quick && Q[pr] == Q[pj]);
     if (skip_p && skip_q) return;
-    if (m >= core_count(a, e, r) || m >= core_count(a, e, j)) return;
+    if (m >= cr || m >= cj) return;
     if (!skip_p) ok &= uf_unite(P + base, r, j, a.union_limit, a.l);
     if (!skip_q) ok &= uf_unite(Q + base, r, j, a.union_limit, a.l);
   });

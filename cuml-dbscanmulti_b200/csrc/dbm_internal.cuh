@@ -107,8 +107,11 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 // ---- union-find with minimum-index roots --------------------------------------------------
 // Roots are always the smallest index of their tree: a root is only ever re-pointed at a
 // smaller root, so a fully compressed parent array maps every member to its component's
-// minimum index.  Path halving writes only ancestors, so concurrent finds are safe.  The parent
-// of x is parent[x * stride] (forests of several configs interleaved point by point).
+// minimum index.  Path splitting (each visited node is re-pointed at its grandparent) writes only
+// ancestors, so concurrent finds are safe; one dependent load per step: the grandparent read for
+// the split is the next step's parent (a value another thread has moved on since is still an
+// ancestor, so the walk still ends at a root as read).  The parent of x is parent[x * stride]
+// (forests of several configs interleaved point by point).
 __device__ __forceinline__ int32_t uf_find(int32_t* parent, int32_t x, int stride = 1)
 {
   volatile int32_t* p = parent;
@@ -117,7 +120,7 @@ __device__ __forceinline__ int32_t uf_find(int32_t* parent, int32_t x, int strid
     const int32_t gp = p[static_cast<int64_t>(px) * stride];
     if (gp != px) p[static_cast<int64_t>(x) * stride] = gp;
     x = px;
-    px = p[static_cast<int64_t>(x) * stride];
+    px = gp;
   }
   return x;
 }
