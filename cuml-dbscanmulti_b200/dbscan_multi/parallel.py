@@ -172,11 +172,16 @@ class DeviceStages:
             return None
         words = int(self.lib.dbm_prune_mask_words())
         chunk = -(-units // nshards)
-        if self._prune_bufs is None or self._prune_bufs[0].numel() != nshards * chunk or \
+        # one int32 buffer per rank slot: [chunk counts | chunk * words mask words], so a single
+        # all-gather exchanges both; the counts and masks of all units are then strided views
+        per = chunk * (1 + words)
+        if self._prune_bufs is None or self._prune_bufs[0].numel() != nshards * per or \
                 self._prune_bufs[0].device != x.device:
-            self._prune_bufs = (torch.zeros(nshards * chunk, dtype=torch.int32, device=x.device),
-                                torch.zeros(nshards * chunk * words, dtype=torch.int32, device=x.device))
-        counts, masks = self._prune_bufs
+            gathered = torch.zeros(nshards * per, dtype=torch.int32, device=x.device)
+            counts = torch.zeros(nshards * chunk, dtype=torch.int32, device=x.device)
+            masks = torch.zeros(nshards * chunk * words, dtype=torch.int32, device=x.device)
+            self._prune_bufs = (gathered, counts, masks)
+        gathered, counts, masks = self._prune_bufs
         u0, u1 = min(units, shard * chunk), min(units, (shard + 1) * chunk)
         err = ctypes.create_string_buffer(1024)
         rc = self.lib.dbm_distance_prune_units(self.h._h, ctypes.c_void_p(x.data_ptr()), n, d,
@@ -185,9 +190,12 @@ class DeviceStages:
                                                stream_arg(s), err, len(err))
         if rc != DBM_OK:
             raise DbmError(rc, err.value.decode())
-        dist.all_gather_into_tensor(counts, counts[shard * chunk:(shard + 1) * chunk].clone(), group=self.group)
-        dist.all_gather_into_tensor(masks, masks[shard * chunk * words:(shard + 1) * chunk * words].clone(),
-                                    group=self.group)
+        mine = torch.cat([counts[shard * chunk:(shard + 1) * chunk],
+                          masks[shard * chunk * words:(shard + 1) * chunk * words]])
+        dist.all_gather_into_tensor(gathered, mine, group=self.group)
+        g = gathered.view(nshards, per)
+        counts.view(nshards, chunk).copy_(g[:, :chunk])
+        masks.view(nshards, chunk * words).copy_(g[:, chunk:])
         return counts, masks
 
     def distance_shard(self, x, eps: np.ndarray, shard: int, nshards: int, cap_hint: int):
@@ -285,7 +293,7 @@ def _gather_config_rows(dist, labels, C: int, n: int, group, ranges=None):
         return labels
     mx = max(sizes)
     a, b = ranges[rank]
-    send = torch.zeros((mx, n), dtype=labels.dtype, device=labels.device)
+    send = torch.empty((mx, n), dtype=labels.dtype, device=labels.device)  # rows past b - a are never read
     send[: b - a] = labels[a:b]
     out = torch.empty((world * mx, n), dtype=labels.dtype, device=labels.device)
     dist.all_gather_into_tensor(out, send, group=group)
