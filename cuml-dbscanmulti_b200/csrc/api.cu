@@ -1,7 +1,7 @@
 // api.cu -- fit_multi orchestrator and the C ABI of libdbm.so.
 //
 // Pass structure (B200 design; the reference's is runner_multi.cuh:549-749 / 771-1251):
-//   1. X -> XT (dim-major, padded) for TMA.
+//   1. Z-order, X -> XT (dim-major, padded) for TMA with the tile boxes, tile-pair prune.
 //   2. One distance pass over the upper triangle of tile pairs: exact per-eps degree
 //      histograms for every row and the list of neighbour pairs (i < j) within the largest
 //      eps, each with its smallest-eps code.  If the pair buffer was too small the pass is
@@ -11,9 +11,10 @@
 //   4. Batch plan: the reference's batch size for the budget, then its batch-correction
 //      rule replayed on the measured per-batch nnz (runner_multi.cuh:1340-1456), and the
 //      per-batch route (anotar_compensa or forced).
-//   5. Labelling, batches ascending: per eps a CSR slab for the batch rows (the max-eps rows
-//      as they are; smaller eps by order-preserving compaction), then the batched CC kernels
-//      for the l minPts configs of that eps.
+//   5. Labelling, batches ascending: the batched CC kernels for every owned config walk the
+//      batch rows' max-eps entries and read each entry's eps from its code (dense batches on
+//      the annotated route first compact the smaller eps' slabs, order-preserving, and walk
+//      those instead: batch_compacts).
 //   6. Roots -> ranks -> labels for all k*l configs at once.
 #include "dbm_internal.cuh"
 

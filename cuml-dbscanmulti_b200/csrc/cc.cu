@@ -428,11 +428,19 @@ __global__ void cc_labels_kernel(int64_t n, int l, int c0, int c1, int64_t W, co
                                  const uint32_t* __restrict__ words, const int64_t* __restrict__ wrank,
                                  int32_t* __restrict__ labels)
 {
-  const int64_t x0 = static_cast<int64_t>(c0) * n;
-  const int64_t x = x0 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (x >= static_cast<int64_t>(c1) * n) return;
-  const int64_t cfg = x / n, i = x - cfg * n;
-  const int e = static_cast<int>(cfg / l), m = static_cast<int>(cfg % l);
+  // threads in the forests' interleaved order (point-major within an eps, minPts config
+  // fastest): the parent and folded-label reads of a warp are contiguous, and its label writes
+  // are l runs of 32 / l consecutive points
+  const int e0 = c0 / l;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t per_eps = n * l;
+  const int e = e0 + static_cast<int>(t / per_eps);
+  const int64_t rem = t - static_cast<int64_t>(e - e0) * per_eps;
+  const int64_t i = rem / l;
+  const int m = static_cast<int>(rem - i * l);
+  const int64_t cfg = static_cast<int64_t>(e) * l + m;
+  if (cfg < c0 || cfg >= c1) return;
+  const int64_t x = cfg * n + i;
   int32_t* g = G + fbase(n, l, e, m);
   int32_t v;
   if (m < cc[static_cast<int64_t>(e) * n + i]) {
@@ -564,8 +572,9 @@ Status launch_cc_labels(int64_t n, int l, int c0, int c1, int64_t W, const int32
                         const int32_t* cur, const uint32_t* words, const int64_t* wrank, int32_t* labels,
                         cudaStream_t s)
 {
-  const int64_t total = static_cast<int64_t>(c1 - c0) * n;
-  if (total <= 0) return Status::Ok();
+  if (c1 <= c0) return Status::Ok();
+  // every (point, config) of the eps the range touches; threads outside the range return
+  const int64_t total = static_cast<int64_t>((c1 + l - 1) / l - c0 / l) * n * l;
   count_launch();
   cc_labels_kernel<<<blocks_for(total, 256), 256, 0, s>>>(n, l, c0, c1, W, cc, G,
                                                           cur, words, wrank, labels);

@@ -13,7 +13,7 @@
 //                        neighbour pairs the distance kernel emitted, both directions.
 //   filter_all_kernel    order-preserving per-row compaction of the max-eps CSR to every
 //                        smaller eps in one pass (filterKernel, csr_multi_eps.cuh:194-234,
-//                        runs once per eps): the annotated route.
+//                        runs once per eps): dense batches of the annotated route.
 //   batch_nnz_kernel     per-batch nnz at the largest eps (runner_multi.cuh:898-904).
 #include "dbm_internal.cuh"
 
