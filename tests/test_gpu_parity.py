@@ -180,6 +180,7 @@ RANDOM_CASES = [
     (2500, 64, 3, 2, 13, 333),
     (2500, 65, 2, 2, 14, None),
     (1500, 129, 3, 2, 15, 256),
+    (4500, 136, 2, 2, 19, 1500),  # ordered path with points wider than the shared-memory transpose
     (700, 300, 2, 2, 16, None),
     (9000, 8, 5, 1, 17, None),
     (9000, 2, 1, 5, 18, 2000),
