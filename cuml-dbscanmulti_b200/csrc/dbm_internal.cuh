@@ -104,6 +104,26 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
     : "memory");
 }
 
+// ---- a shard's share of the distance work items ----------------------------------------------
+// Runs of kShardRun consecutive items are dealt round-robin over the S shards (run r to shard
+// r % S): the ranks' shares cost alike whatever the cost profile along the J-major worklist
+// (contiguous thirds or halves did not: the dense parts of the point set land on one rank),
+// while each run keeps the worklist's locality (consecutive items of one tile J).  Local item i
+// of shard s is global item shard_item(i, s, S); the shard's valid local items are a prefix.
+constexpr int64_t kShardRun = 64;
+__host__ __device__ __forceinline__ int64_t shard_item(int64_t i, int s, int S)
+{
+  return ((i / kShardRun) * S + s) * kShardRun + i % kShardRun;
+}
+__host__ __device__ __forceinline__ int64_t shard_items(int64_t total, int s, int S)
+{
+  const int64_t runs = (total + kShardRun - 1) / kShardRun;
+  if (s >= runs) return 0;
+  const int64_t mine = (runs - 1 - s) / S + 1;
+  const int64_t last = s + (mine - 1) * S;  // global index of this shard's last run
+  return mine * kShardRun - (last == runs - 1 ? runs * kShardRun - total : 0);
+}
+
 // ---- union-find with minimum-index roots --------------------------------------------------
 // Roots are always the smallest index of their tree: a root is only ever re-pointed at a
 // smaller root, so a fully compressed parent array maps every member to its component's

@@ -44,8 +44,8 @@ struct DistParams {
   int32_t k;
   int32_t dbox;                      // dims per box actually used (<= kDimBox)
   int32_t nchunks;                   // ceil(d / dbox)
-  int64_t item_begin;                // this launch's share [item_begin, item_begin + item_count)
-  int64_t item_count;                // of the work items: tile pairs, or worklist entries
+  int32_t shard, nshards;            // this launch's share of the work items (tile pairs, or
+  int64_t item_count;                // worklist entries): item_count of them, mapped by shard_item
   const long long* work;             // worklist of tile-pair indices (nullptr: item = tile pair)
   const unsigned long long* count_dev;  // when set, item_count is read here on the device
   unsigned long long* counters;      // [0] edge cursor, [1] next tile pair
@@ -143,7 +143,8 @@ dist_tri_kernel(const __grid_constant__ CUtensorMap xt_map, const DistParams p)
     const long long i = static_cast<long long>(atomicAdd(p.counters + 1, 1ULL));
     const long long limit = p.count_dev ? static_cast<long long>(*p.count_dev) : p.item_count;
     if (i >= limit) return -1;
-    return p.work ? p.work[p.item_begin + i] : p.item_begin + i;
+    const long long g = shard_item(i, p.shard, p.nshards);
+    return p.work ? p.work[g] : g;
   };
   auto issue = [&](int stage, long long tile, int chunk) {
     // one thread: record the item and start both tile loads of this stage
@@ -568,12 +569,14 @@ Status launch_distance(const DistLaunch& a, cudaStream_t s)
   const int64_t T = ceil_div(a.n, kTile);
   const int64_t items = a.work ? a.work_count : T * (T + 1) / 2;
   const int shards = a.nshards > 0 ? a.nshards : 1;
-  p.item_begin = items * a.shard / shards;
-  p.item_count = items * (a.shard + 1) / shards - p.item_begin;
+  p.shard = a.shard;
+  p.nshards = shards;
+  p.item_count = shard_items(items, a.shard, shards);
   p.work = a.work;
   p.count_dev = a.work_count_dev;
-  if (a.work_count_dev) {
-    p.item_begin = 0;
+  if (a.work_count_dev) {  // a list of this launch's own (the screen's fallback tile pairs)
+    p.shard = 0;
+    p.nshards = 1;
     p.item_count = 0;
   }
   p.counters = a.counters;

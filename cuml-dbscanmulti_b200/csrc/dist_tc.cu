@@ -78,8 +78,7 @@ struct ScreenParams {
   int64_t npad;
   int32_t d;
   int32_t k;
-  int64_t item_begin;
-  int64_t item_count;
+  int64_t item_count;            // this shard's items (shard_item maps them into the worklist)
   const int64_t* total_dev;      // when set: worklist length on the device (capped at cap),
   int64_t cap;                   // and this shard's slice is computed here
   int32_t shard, nshards;
@@ -306,11 +305,10 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
   const int64_t n = p.n;
   const float cutoff = p.eps2[p.k - 1];
   const float se = p.sqrt_e;
-  int64_t item_begin = p.item_begin, item_count = p.item_count;
+  int64_t item_count = p.item_count;
   if (p.total_dev) {
     const int64_t total = *p.total_dev < p.cap ? *p.total_dev : p.cap;
-    item_begin = total * p.shard / p.nshards;
-    item_count = total * (p.shard + 1) / p.nshards - item_begin;
+    item_count = shard_items(total, p.shard, p.nshards);
   }
   if (tid < kMaxEps) s_eps2[tid] = p.eps2[tid];
   if (warp == 0) {
@@ -367,7 +365,7 @@ dist_screen_kernel(const __grid_constant__ CUtensorMap xt_map, const ScreenParam
     return q < clen ? cstart + q : s_chunk[(m + 1) & 1] + (q - clen);
   };
   auto load_entry = [&](long long idx) -> long long {
-    return idx < item_count ? __ldg(p.work + item_begin + idx) : -1;
+    return idx < item_count ? __ldg(p.work + shard_item(idx, p.shard, p.nshards)) : -1;
   };
   long long e_cur = load_entry(item_index(0));
   long long e_nxt = e_cur >= 0 ? load_entry(item_index(1)) : -1;
@@ -680,11 +678,9 @@ Status launch_screened_distance(const DistLaunch& a, const float* box_lo, const 
   if (a.work_total_dev) {
     p.total_dev = a.work_total_dev;
     p.cap = a.work_cap;
-    p.item_begin = 0;
     p.item_count = a.work_cap;  // an upper bound for the grid size
   } else {
-    p.item_begin = a.work_count * a.shard / shards;
-    p.item_count = a.work_count * (a.shard + 1) / shards - p.item_begin;
+    p.item_count = shard_items(a.work_count, a.shard, shards);
   }
   p.work = a.work;
   p.xt = a.xt;

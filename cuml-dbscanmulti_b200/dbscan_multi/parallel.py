@@ -33,11 +33,23 @@ from . import (DBM_OK, DbmError, DbscanMulti, FitResult, Options, Stats, ROUTE_N
 TILE = 128
 
 
-def tile_pair_range(n: int, shard: int, nshards: int) -> tuple[int, int]:
-    """The [begin, end) tile-pair indices a shard evaluates (same rule as dist.cu)."""
+SHARD_RUN = 64  # kShardRun of dbm_internal.cuh
+
+
+def shard_items(total: int, shard: int, nshards: int) -> np.ndarray:
+    """The global indices of the work items a shard evaluates, in its local order (the rule of
+    dbm_internal.cuh shard_item / shard_items): runs of SHARD_RUN consecutive items dealt
+    round-robin over the shards."""
+    i = np.arange(total, dtype=np.int64)
+    g = ((i // SHARD_RUN) * nshards + shard) * SHARD_RUN + i % SHARD_RUN
+    return g[g < total]
+
+
+def tile_pair_indices(n: int, shard: int, nshards: int) -> np.ndarray:
+    """The tile-pair indices (i <= j, triangle order) a shard evaluates when no worklist is
+    built (n < 4096: no pruning)."""
     t = (n + TILE - 1) // TILE
-    pairs = t * (t + 1) // 2
-    return pairs * shard // nshards, pairs * (shard + 1) // nshards
+    return shard_items(t * (t + 1) // 2, shard, nshards)
 
 
 def config_range(c: int, rank: int, world: int) -> tuple[int, int]:

@@ -61,10 +61,10 @@ class OracleStages:
     def distance_shard(self, x, eps, shard, nshards, cap_hint):
         n = len(self.pts)
         k = len(eps)
-        b, e = parallel.tile_pair_range(n, shard, nshards)
+        mine = parallel.tile_pair_indices(n, shard, nshards)
         hist = np.zeros((k, n), np.int32)
         words = []
-        for c in range(b, e):
+        for c in mine.tolist():
             ti, tj = tri_coords(c)
             for i in range(ti * TILE, min(n, ti * TILE + TILE)):
                 for j in range(tj * TILE, min(n, tj * TILE + TILE)):
@@ -118,12 +118,17 @@ def _free_port():
 
 
 def test_tile_pair_shards_partition_the_triangle():
-    for n in (1, 127, 128, 129, 1000, 4097):
+    for n in (1, 127, 128, 129, 1000, 4097, 40000):
         t = (n + TILE - 1) // TILE
         for world in (1, 2, 3, 8):
-            ranges = [parallel.tile_pair_range(n, r, world) for r in range(world)]
-            assert ranges[0][0] == 0 and ranges[-1][1] == t * (t + 1) // 2
-            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+            parts = [parallel.tile_pair_indices(n, r, world) for r in range(world)]
+            allp = np.sort(np.concatenate(parts))
+            assert np.array_equal(allp, np.arange(t * (t + 1) // 2))  # every tile pair exactly once
+            # runs of consecutive items stay together, and the shares differ by at most one run
+            sizes = [len(p) for p in parts]
+            assert max(sizes) - min(sizes) <= parallel.SHARD_RUN
+            for p in parts:
+                assert np.all(np.diff(p)[np.arange(len(p) - 1) % parallel.SHARD_RUN != parallel.SHARD_RUN - 1] == 1)
     assert [parallel.config_range(16, r, 8) for r in range(8)] == [(2 * r, 2 * r + 2) for r in range(8)]
     for c in (1, 5, 9, 16, 100):
         for world in (1, 2, 3, 8):
