@@ -3,9 +3,9 @@
 The reference's fit_multi is single-GPU (runner_multi.cuh:15-16 removed cuML's multi-node
 path).  Here the work shards without changing a single label:
 
-1. every rank evaluates an equal share of the 128 x 128 tile pairs (i <= j) of the distance
-   pass (``dbm_distance_shard``): per-code histograms for all N rows and the neighbour pairs
-   found in its share;
+1. every rank evaluates its share of the 128 x 128 tile pairs (i <= j; runs of 64 work items
+   dealt round-robin, so the shares cost alike) of the distance pass (``dbm_distance_shard``):
+   per-code histograms for all N rows and the neighbour pairs found in its share;
 2. the histograms are summed across ranks (all-reduce) -- exact degrees everywhere -- and the
    neighbour pairs are all-gathered (variable counts, padded);
 3. every rank labels a contiguous range of the k*l configurations from the complete graph

@@ -197,7 +197,9 @@ int dbm_fit_multi_host(dbm_handle* h, const float* x_host, int64_t n, int64_t d,
  * runs dbm_fit_multi_from_graph for its range of configs with the same options (an explicit
  * budget and csr_cap_bytes agreed across ranks keep the batch plan identical). */
 
-/* Distance pass over the shard-th of nshards equal ranges of 128x128 tile pairs (i <= j).
+/* Distance pass over the shard-th of nshards shares of the 128x128 tile pairs (i <= j): runs of
+ * 64 consecutive work items (surviving tile pairs, or all tile pairs below 4096 points) dealt
+ * round-robin over the shards, so the shares cost alike.
  * hist_dev: k*n int32 (zeroed here): pairs (i, j != i) of this shard per row and exact code.
  * edges_dev: edge_cap 64-bit words, i << 32 | code << 28 | j, one per neighbour pair i < j within
  * the largest eps found in this shard.  *edges_found receives the count; when it exceeds
