@@ -27,3 +27,20 @@ def test_fixed_eps_workloads_keep_their_grid():
     for name, cfg in bench.CONFIGS.items():
         if cfg.get("eps"):
             assert bench.workload_eps(cfg, np.zeros((4, cfg["d"]), np.float32)) == list(cfg["eps"])
+
+
+def test_labelling_roofline_counts_compaction_only_where_the_fit_compacts():
+    """The labelling's algorithmic bytes: one CC sweep per configuration, plus the smaller-eps
+    compaction only for dense graphs routed annotated (sparse batches read each entry's eps from
+    its code and compact nothing)."""
+    n, l = 1000, 2
+    stats = {"annotated_batches": 3}
+    sparse = [4 * n, 8 * n, 16 * n]
+    dense = [100 * n, 200 * n, 400 * n]
+    cc = lambda nnz: sum(l * (8.0 * v + 8.0 * n + n / 8.0) for v in nnz)
+    r = bench.label_roofline(sparse, n, l, stats, [1.0], 1)
+    assert r["bytes_per_grid"] == cc(sparse)
+    r = bench.label_roofline(dense, n, l, stats, [1.0], 1)
+    assert r["bytes_per_grid"] == cc(dense) + 4.0 * dense[-1] + 8.0 * sum(dense[:-1])
+    r = bench.label_roofline(dense, n, l, {"annotated_batches": 0}, [1.0], 1)
+    assert r["bytes_per_grid"] == cc(dense)
