@@ -307,3 +307,14 @@ def test_points_gathered_from_host_slices_and_limits_agreed(tmp_path, world):
     for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"g{r}.npy"), pts)
         assert list(np.load(tmp_path / f"l{r}.npy")) == [1000, 500 - (world - 1)]
+
+
+def test_labelling_split_spreads_the_largest_eps_configs():
+    """C4's per-eps entry counts (almost every entry belongs to the largest eps): every rank walks
+    the max-eps entries once whatever it owns, so the split spreads the largest eps's configs,
+    whose unions dominate, over the ranks instead of giving them all to one."""
+    pe = [394.0, 17668.0, 357400.0, 3840788.0]
+    for world in (2, 4, 8):
+        rs = parallel.labelling_ranges(pe, 4, 10**6, world)
+        owners = [r for r, (a, b) in enumerate(rs) if any(12 <= c < 16 for c in range(a, b))]
+        assert len(owners) >= min(world, 4) // 2 + 1, (world, rs)
